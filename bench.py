@@ -1,0 +1,373 @@
+#!/usr/bin/env python3
+"""Benchmark of the packed matrix-product path (one JSON line on rank 0).
+
+Workload: the Q8_0 matvec at TinyLlama lm_head shape,
+W 32000 x 2048 drawn N(0, 0.02) and quantized with the reference's Q8_0 rule (bit-exact
+GPU quantizer), x ~ N(0, 1). A step is one matvec. Six device copies of W (418 MB,
+> 3x the 126 MB L2) are used in rotation, so every step streams its weights from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W]      # our B200 path
+  python bench.py --impl reference                           # the reference's CPU path
+
+Metric: algorithmic bytes per step (packed W + x + y = 69,768,192 B) / time, in GB/s.
+value: device time of K steps (CUDA events, a CUDA graph of the C-ABI launches, max over
+ranks). e2e: the same steps through the host-pointer C-ABI call efg_host_matvec (pinned
+x in, y out every step; W resident after its first upload), wall clock.
+N > 1: each rank runs its own config-1 matvecs (weak scaling, no collective in the data
+path); value = bytes of all ranks / max time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ROWS, COLS = 32000, 2048
+Q8_0, Q4_0 = 3, 4
+N_COPIES = 6
+METRIC = "Q8_0 matvec HBM GB/s (lm_head 32000x2048)"
+
+
+def algo_bytes(qt, rows, cols):
+    return rows * (cols // 32) * (18 if qt == Q4_0 else 34) + 4 * cols + 4 * rows
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def rank_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ---------------------------------------------------------------- clocks (NVML)
+class ClockSampler:
+    """Samples SM clock and throttle reasons every 10 ms while running."""
+
+    NAMES = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sync_boost", 0x40: "sw_thermal_slowdown",
+             0x80: "hw_thermal_slowdown", 0x100: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting"}
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.stop_ev = [], 0, threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self.nvml = None
+
+    def _sample(self):
+        try:
+            self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+            self.reasons |= int(self.get_reasons(self.h))
+        except Exception:  # noqa: BLE001
+            pass
+
+    def _run(self):
+        while not self.stop_ev.is_set():
+            self._sample()
+            self.stop_ev.wait(0.01)
+
+    def __enter__(self):
+        if self.nvml:
+            self._sample()
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.nvml:
+            self.stop_ev.set()
+            self.t.join()
+            self._sample()
+
+    def summary(self):
+        if not self.nvml or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [n for b, n in self.NAMES.items() if self.reasons & b]
+        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- reference CPU leg
+def cpu_reference_matvec(seconds: float, qt=Q8_0, rows=ROWS, cols=COLS, copies=N_COPIES, steps=None, warmup=3,
+                         cap_seconds=150.0):
+    """The reference's AVX2 matvec (kern::matvec + ThreadPool, oracle/_ref) on the host
+    cores: rotating W copies (418 MB, larger than the host's last-level cache). Runs
+    `steps` matvecs (or for `seconds` when steps is None), never longer than cap_seconds."""
+    from oracle.oracle import Oracle, Reference
+
+    ref, orc = Reference(), Oracle()
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    X = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    W = orc.quantize_rows(qt, X, threads=threads)
+    del X
+    Ws = [W.copy() for _ in range(copies)]
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = np.zeros(rows, np.float32)
+    with ref.pool(threads) as pool:
+        for i in range(max(warmup, copies)):  # warm-up: page in every copy
+            ref.matvec_backend(qt, Ws[i % copies], x, rows, avx2=True, pool=pool, y=y)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            ref.matvec_backend(qt, Ws[n % copies], x, rows, avx2=True, pool=pool, y=y)
+            n += 1
+            el = time.perf_counter() - t0
+            if (steps is not None and n >= steps) or (steps is None and el >= seconds) or el >= cap_seconds:
+                break
+    return algo_bytes(qt, rows, cols) * n / el / 1e9, threads, n, el
+
+
+def run_reference_arm(args):
+    rank, world, _ = rank_env()
+    if rank != 0:
+        return 0
+    if not (ROOT / "oracle" / "_ref" / "libefref.so").exists():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libefref.so was not built"}))
+        return 0
+    # W untimed warm-up steps, then K timed steps (each one CPU matvec of the workload;
+    # stopped after 150 s, in which case "steps" reports the count actually timed)
+    gbs, threads, n, el = cpu_reference_matvec(0.0, steps=args.steps, warmup=args.warmup)
+    args.steps = n
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(el / n * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (Q8_0 weights)", "data": "synthetic (seeded N(0,0.02) W, N(0,1) x)",
+        "config": {"workload": "config1_q8_0_matvec_32000x2048", "rows": ROWS, "cols": COLS, "copies": N_COPIES,
+                   "l2": "host LLC exceeded by rotating copies"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
+                         "sample": f"{n} matvecs of the reference AVX2 kernel, ThreadPool({threads})"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------- our GPU arm
+def make_weights(efg, torch, qt, rows, cols, copies, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    X = torch.randn(rows, cols, generator=g, device="cuda", dtype=torch.float32) * 0.02
+    W = torch.empty(rows * (cols // 32) * (18 if qt == Q4_0 else 34), dtype=torch.uint8, device="cuda")
+    efg.quantize_rows(qt, X, rows, cols, W, True)
+    del X
+    return [W] + [W.clone() for _ in range(copies - 1)]
+
+
+def graph_of_steps(efg, torch, qt, Ws, x, y, rows, cols, n):
+    """A CUDA graph of n matvec launches made through the C ABI (rotating copies)."""
+    s = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        for i in range(2):  # launch once outside capture (attributes, lazy init)
+            efg.matvec(qt, y, Ws[i % len(Ws)], x, rows, cols)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(n):
+                efg.matvec(qt, y, Ws[i % len(Ws)], x, rows, cols)
+    return graph
+
+
+def time_steps(efg, torch, qt, Ws, x, y, rows, cols, steps, warmup, chunk=60):
+    """Device time (ms) of exactly `steps` matvecs, launched as CUDA graphs."""
+    chunk = max(len(Ws), min(chunk, steps))
+    g_full = graph_of_steps(efg, torch, qt, Ws, x, y, rows, cols, chunk)
+    rem = steps % chunk
+    g_rem = graph_of_steps(efg, torch, qt, Ws, x, y, rows, cols, rem) if rem else None
+    g_warm = graph_of_steps(efg, torch, qt, Ws, x, y, rows, cols, max(warmup, 1))
+    g_warm.replay()
+    torch.cuda.synchronize()
+    return g_full, g_rem, chunk
+
+
+def run_ours(args):
+    import torch
+
+    rank, world, local = rank_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    import edgeforge_b200 as efg
+
+    efg.set_weight_prefetch(True)  # static weights: stream them during the previous kernel's tail
+    hbm_peak, peak_kind = peaks()
+    nbytes = algo_bytes(Q8_0, ROWS, COLS)
+
+    Ws = make_weights(efg, torch, Q8_0, ROWS, COLS, N_COPIES, seed=1 + rank)
+    x = torch.randn(COLS, generator=torch.Generator(device="cuda").manual_seed(2), device="cuda")
+    y = torch.empty(ROWS, device="cuda")
+    g_full, g_rem, chunk = time_steps(efg, torch, Q8_0, Ws, x, y, ROWS, COLS, args.steps, args.warmup)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(args.steps // chunk):
+            g_full.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = nbytes * world * args.steps / (ms / 1e3) / 1e9
+    achieved = nbytes / (ms_step / 1e3) / 1e9  # per launch, one GPU
+
+    # ---- e2e: the host-pointer C-ABI call, pinned x in and y out every step
+    x_h = torch.empty(COLS, dtype=torch.float32).pin_memory().numpy()
+    y_h = torch.empty(ROWS, dtype=torch.float32).pin_memory().numpy()
+    x_h[:] = x.cpu().numpy()
+    Wh = Ws[0].cpu().numpy()
+    Whs = [Wh.copy() for _ in range(N_COPIES)]
+    for i in range(N_COPIES + args.warmup):  # first calls upload each copy once
+        efg.host_matvec(Q8_0, Whs[i % N_COPIES], x_h, ROWS, y=y_h)
+    barrier()
+    e2e_steps = max(args.steps, 1)
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        efg.host_matvec(Q8_0, Whs[i % N_COPIES], x_h, ROWS, y=y_h)
+    el = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([el], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        el = float(t.item())
+    e2e = nbytes * world * e2e_steps / el / 1e9
+    efg.host_release_weights()
+    assert efg.device_error() == 0
+
+    # ---- extra: the Q4_0 matvec at TinyLlama gate_proj shape (config 0), same protocol
+    q4_rows, q4_cols = 5632, 2048
+    q4_copies = 64  # 64 x 6.5 MB = 415 MB in rotation
+    W4 = make_weights(efg, torch, Q4_0, q4_rows, q4_cols, q4_copies, seed=3)
+    y4 = torch.empty(q4_rows, device="cuda")
+    k4 = 6400
+    g4, _, c4 = time_steps(efg, torch, Q4_0, W4, x, y4, q4_rows, q4_cols, k4, 64, chunk=640)
+    torch.cuda.synchronize()
+    s4, e4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s4.record()
+    for _ in range(k4 // c4):
+        g4.replay()
+    e4.record()
+    torch.cuda.synchronize()
+    ms4 = s4.elapsed_time(e4) / k4
+    gbs4 = algo_bytes(Q4_0, q4_rows, q4_cols) / (ms4 / 1e3) / 1e9
+    del W4
+
+    traffic = None
+    tpath = ROOT / "profiles" / "matvec_q8_0_32000x2048.json"
+    if tpath.exists():
+        traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline and (ROOT / "oracle" / "_ref" / "libefref.so").exists():
+            gbs_c, thr, n_c, el_c = cpu_reference_matvec(args.cpu_seconds)
+            cpu = {"value": round(gbs_c, 3), "unit": "GB/s", "cores": thr, "kind": "reference",
+                   "sample": f"{n_c} matvecs ({el_c:.1f} s) of the reference AVX2 kernel + ThreadPool({thr}) "
+                             f"on config 1, {N_COPIES} rotating W copies"}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (Q8_0 weights)", "data": "synthetic (seeded N(0,0.02) W, N(0,1) x)",
+            "config": {"workload": "config1_q8_0_matvec_32000x2048", "rows": ROWS, "cols": COLS,
+                       "copies": N_COPIES, "l2": "inputs larger than L2: 6 rotating W copies (418 MB)",
+                       "launch": "CUDA graph of C-ABI launches with early weight prefetch (PDL)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": nbytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * COLS,
+                    "d2h_bytes_per_step": 4 * ROWS,
+                    "api": "efg_host_matvec (host pointers; W resident after first upload)"},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "extra": {"config0_q4_0_matvec_5632x2048": {
+                "gbs": round(gbs4, 1), "frac_of_hbm": round(gbs4 / hbm_peak, 4), "us_per_launch": round(ms4 * 1e3, 3),
+                "bytes_per_launch": algo_bytes(Q4_0, q4_rows, q4_cols), "copies": q4_copies}},
+        }
+        print(json.dumps(line))
+    if world > 1:
+        del g_full, g_rem
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_profile(args):
+    """A few plain launches of one matvec, for ncu (no graphs, no CPU legs):
+    --profile q8  -> config 1 (Q8_0 32000x2048), --profile q4 -> config 0 (Q4_0 5632x2048),
+    --profile q4big -> Q4_0 16384x8192 (302 MB, a slice of config 4's rows)."""
+    import torch
+
+    import edgeforge_b200 as efg
+
+    torch.cuda.set_device(0)
+    qt, rows, cols, copies = {"q8": (Q8_0, ROWS, COLS, 3), "q4": (Q4_0, 5632, 2048, 24),
+                              "q4big": (Q4_0, 16384, 8192, 1)}[args.profile]
+    Ws = make_weights(efg, torch, qt, rows, cols, copies, seed=1)
+    x = torch.randn(cols, device="cuda")
+    y = torch.empty(rows, device="cuda")
+    for i in range(2 * copies + 3):
+        efg.matvec(qt, y, Ws[i % copies], x, rows, cols)
+    torch.cuda.synchronize()
+    assert efg.device_error() == 0
+    print(json.dumps({"profile": args.profile, "rows": rows, "cols": cols, "launches": 2 * copies + 3,
+                      "bytes_per_launch": algo_bytes(qt, rows, cols)}))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=6000)
+    ap.add_argument("--warmup", type=int, default=60)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["q8", "q4", "q4big"], help="a few plain launches for ncu")
+    args = ap.parse_args()
+    if args.profile:
+        return run_profile(args)
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,79 @@
+"""ctypes binding of libefg.so (the C ABI declared in include/efg.h).
+
+The library is loaded from this package directory only. There is no fallback: if it
+is missing, importing any operation raises, so a GPU run can never silently take a
+CPU or PyTorch path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libefg.so"
+
+_vp, _sz, _i = C.c_void_p, C.c_size_t, C.c_int
+_u64, _i32p = C.c_uint64, C.POINTER(C.c_int32)
+
+
+class EdgeForgeError(RuntimeError):
+    """A failed library call (the counterpart of ef::Error, include/ef/error.h:11-13)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class MatvecJob(C.Structure):
+    """efg_matvec_job (include/efg.h)."""
+
+    _fields_ = [("d_y", _vp), ("qtype", _i), ("d_W", _vp), ("rows", _sz), ("cols", _sz), ("d_x", _vp)]
+
+
+# name -> (restype, argtypes); every symbol include/efg.h declares.
+SIGNATURES = {
+    "efg_abi_version": (_i, []),
+    "efg_last_error": (C.c_char_p, []),
+    "efg_status_string": (C.c_char_p, [_i]),
+    "efg_device_error": (_i, [C.POINTER(_i)]),
+    "efg_set_weight_prefetch": (_i, [_i]),
+    "efg_row_bytes": (_u64, [_i, _u64]),
+    "efg_matvec_q4_0": (_i, [_vp, _vp, _vp, _sz, _sz, _vp]),
+    "efg_matvec_q8_0": (_i, [_vp, _vp, _vp, _sz, _sz, _vp]),
+    "efg_matvec": (_i, [_i, _vp, _vp, _vp, _sz, _sz, _vp]),
+    "efg_matvec_jobs": (_i, [C.POINTER(MatvecJob), _sz, _vp]),
+    "efg_dot_q4_0": (_i, [_vp, _vp, _vp, _sz, _vp]),
+    "efg_dot_q8_0": (_i, [_vp, _vp, _vp, _sz, _vp]),
+    "efg_quantize_row": (_i, [_i, _vp, _sz, _vp, _i, _vp]),
+    "efg_dequantize_row": (_i, [_i, _vp, _sz, _vp, _vp]),
+    "efg_quantize_rows": (_i, [_i, _vp, _sz, _sz, _vp, _i, _vp]),
+    "efg_dequantize_rows": (_i, [_i, _vp, _sz, _sz, _vp, _vp]),
+    "efg_row_f32": (_i, [_vp, _i, _vp, _sz, _sz, _i32p, _sz, _vp]),
+    "efg_host_matvec": (_i, [_i, _vp, _vp, _vp, _sz, _sz]),
+    "efg_host_quantize_row": (_i, [_i, _vp, _sz, _vp, _i]),
+    "efg_host_dequantize_row": (_i, [_i, _vp, _sz, _vp]),
+    "efg_host_release_weights": (_i, []),
+}
+
+_lib = None
+
+
+def load() -> C.CDLL:
+    """Loads libefg.so once and binds every declared symbol (raises if any is missing)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is not built: run `python -c 'import __graft_entry__ as g; g.build()'`")
+        lib = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(lib, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != 0:
+        lib = load()
+        raise EdgeForgeError(status, f"{lib.efg_status_string(status).decode()}: {lib.efg_last_error().decode()}")

@@ -1,0 +1,174 @@
+"""Python mirror of the reference's kernel API for the packed matrix-product path.
+
+Names and argument meaning follow the reference (include/ef/qkernels.h,
+include/ef/quant.h): ``matvec_q4_0(y, W, x, rows, cols)``, ``quantize_row(t, x, n,
+out, search)``, ... The arrays are torch CUDA tensors on the current device, and every
+call is queued on torch's current CUDA stream. Errors raise EdgeForgeError, the way the
+reference throws ef::Error (a row length that is not a multiple of 32 gives the
+reference's message, "Q4_0 needs a row length divisible by 32, got 30").
+
+The ``host_*`` functions take numpy arrays and are synchronous, exactly the
+reference's host-pointer calls (the weight matrix stays resident on the device).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from enum import IntEnum
+
+import numpy as np
+
+from ._lib import EdgeForgeError, MatvecJob, check, load
+
+
+class QType(IntEnum):
+    """ef::QType (include/ef/quant.h:35)."""
+
+    F32 = 0
+    F16 = 1
+    BF16 = 2
+    Q8_0 = 3
+    Q4_0 = 4
+
+
+QK = 32
+BLOCK_BYTES = {QType.Q4_0: 18, QType.Q8_0: 34}
+
+
+def row_bytes(qtype: int, cols: int) -> int:
+    """ef::qtype_row_bytes (include/ef/quant.h:42): raises for cols % 32 != 0."""
+    n = load().efg_row_bytes(int(qtype), int(cols))
+    if n == 0 and cols != 0:
+        raise EdgeForgeError(1, load().efg_last_error().decode())
+    return int(n)
+
+
+def _stream():
+    import torch
+
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t) -> C.c_void_p:
+    if t is None:
+        return C.c_void_p(0)
+    if not t.is_cuda:
+        raise EdgeForgeError(1, "expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise EdgeForgeError(1, "expected a contiguous tensor")
+    return C.c_void_p(t.data_ptr())
+
+
+# ---------------------------------------------------------------- matvec
+
+
+def matvec_q4_0(y, W, x, rows: int, cols: int) -> None:
+    """y[r] = dot(row r of W, x) for Q4_0 W (ef::kern::matvec_q4_0, qkernels.h:50)."""
+    check(load().efg_matvec_q4_0(_ptr(y), _ptr(W), _ptr(x), rows, cols, _stream()))
+
+
+def matvec_q8_0(y, W, x, rows: int, cols: int) -> None:
+    """ef::kern::matvec_q8_0 (qkernels.h:51)."""
+    check(load().efg_matvec_q8_0(_ptr(y), _ptr(W), _ptr(x), rows, cols, _stream()))
+
+
+def matvec(qtype: int, y, W, x, rows: int, cols: int) -> None:
+    """ef::kern::matvec for a WeightView of a packed type (qkernels.h:66)."""
+    check(load().efg_matvec(int(qtype), _ptr(y), _ptr(W), _ptr(x), rows, cols, _stream()))
+
+
+def matvec_jobs(jobs) -> None:
+    """ef::kern::matvec_jobs (qkernels.h:70-75). jobs: iterable of
+    (y, qtype, W, rows, cols, x) tuples of CUDA tensors."""
+    arr = (MatvecJob * len(jobs))()
+    for i, (y, qt, W, rows, cols, x) in enumerate(jobs):
+        arr[i] = MatvecJob(_ptr(y).value, int(qt), _ptr(W).value, rows, cols, _ptr(x).value)
+    check(load().efg_matvec_jobs(arr, len(jobs), _stream()))
+
+
+def dot_q4_0(out, row, x, n: int) -> None:
+    """ef::kern::dot_q4_0 (qkernels.h:47), result written to out[0]."""
+    check(load().efg_dot_q4_0(_ptr(out), _ptr(row), _ptr(x), n, _stream()))
+
+
+def dot_q8_0(out, row, x, n: int) -> None:
+    """ef::kern::dot_q8_0 (qkernels.h:48)."""
+    check(load().efg_dot_q8_0(_ptr(out), _ptr(row), _ptr(x), n, _stream()))
+
+
+# ---------------------------------------------------------------- quantize / dequantize
+
+
+def quantize_row(qtype: int, x, n: int, out, search: bool = True) -> None:
+    """ef::quantize_row (quant.h:52), bit-exact."""
+    check(load().efg_quantize_row(int(qtype), _ptr(x), n, _ptr(out), int(search), _stream()))
+
+
+def dequantize_row(qtype: int, data, n: int, out) -> None:
+    """ef::dequantize_row (quant.h:53), bit-exact."""
+    check(load().efg_dequantize_row(int(qtype), _ptr(data), n, _ptr(out), _stream()))
+
+
+def quantize_rows(qtype: int, X, rows: int, cols: int, out, search: bool = True) -> None:
+    """quantize_row over every row of a [rows][cols] matrix in one launch."""
+    check(load().efg_quantize_rows(int(qtype), _ptr(X), rows, cols, _ptr(out), int(search), _stream()))
+
+
+def dequantize_rows(qtype: int, data, rows: int, cols: int, out) -> None:
+    check(load().efg_dequantize_rows(int(qtype), _ptr(data), rows, cols, _ptr(out), _stream()))
+
+
+def row_f32(out, qtype: int, W, rows: int, cols: int, r: int | None = None, r_dev=None) -> None:
+    """ef::kern::row_f32 (qkernels.h:78): row r of W as FP32. r_dev: an int32 CUDA tensor
+    holding the row index (read on the device)."""
+    rp = C.cast(C.c_void_p(r_dev.data_ptr()), C.POINTER(C.c_int32)) if r_dev is not None else None
+    check(load().efg_row_f32(_ptr(out), int(qtype), _ptr(W), rows, cols, rp, r or 0, _stream()))
+
+
+def set_weight_prefetch(enable: bool) -> bool:
+    """efg_set_weight_prefetch: lets later matvec launches on this thread stream their
+    weights while the previous kernel finishes (weights must not be written just
+    before). Returns the previous setting."""
+    return bool(load().efg_set_weight_prefetch(int(enable)))
+
+
+def device_error() -> int:
+    """Reads and clears the device error word (EFG_OK or EFG_ETIMEOUT / EFG_EINVAL)."""
+    code = C.c_int(0)
+    check(load().efg_device_error(C.byref(code)))
+    return code.value
+
+
+# ---------------------------------------------------------------- host-pointer forms
+
+
+def _np(a, dtype):
+    a = np.ascontiguousarray(a, dtype=dtype)
+    return a, C.c_void_p(a.ctypes.data)
+
+
+def host_matvec(qtype: int, W: np.ndarray, x: np.ndarray, rows: int, y: np.ndarray | None = None) -> np.ndarray:
+    """Synchronous host-pointer matvec; W stays resident on the device between calls."""
+    W, pw = _np(W, np.uint8)
+    x, px = _np(x, np.float32)
+    if y is None:
+        y = np.zeros(rows, dtype=np.float32)
+    check(load().efg_host_matvec(int(qtype), C.c_void_p(y.ctypes.data), pw, px, rows, x.size))
+    return y
+
+
+def host_quantize_row(qtype: int, x: np.ndarray, search: bool = True) -> np.ndarray:
+    x, px = _np(x, np.float32)
+    out = np.zeros(row_bytes(qtype, x.size), dtype=np.uint8)
+    check(load().efg_host_quantize_row(int(qtype), px, x.size, C.c_void_p(out.ctypes.data), int(search)))
+    return out
+
+
+def host_dequantize_row(qtype: int, data: np.ndarray, n: int) -> np.ndarray:
+    data, pd = _np(data, np.uint8)
+    out = np.zeros(n, dtype=np.float32)
+    check(load().efg_host_dequantize_row(int(qtype), pd, n, C.c_void_p(out.ctypes.data)))
+    return out
+
+
+def host_release_weights() -> None:
+    check(load().efg_host_release_weights())

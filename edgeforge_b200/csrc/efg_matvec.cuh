@@ -1,0 +1,46 @@
+// efg_matvec.cuh - host-visible description of the packed matvec kernels (efg_matvec.cu).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace efg {
+
+enum class Fmt : int { Q8 = 3, Q4 = 4 };  // values = ef::QType
+enum class Epi : int { Store = 0, Add = 1, SwiGLU = 2 };
+
+constexpr int kMaxJobs = 4;
+
+struct MatvecJobDev {
+  const uint8_t* W;
+  float* y;
+  uint32_t rows;
+  uint32_t y_pos_stride;  // y += (*pos) * y_pos_stride when MatvecArgs::pos is set
+};
+
+// One fused matvec launch: n_jobs matrices with the same type and cols applied to the
+// same x (q/k/v or gate/up), or, for Epi::SwiGLU, jobs[0] = gate, jobs[1] = up with the
+// result silu(gate . x) * (up . x) written to jobs[0].y.
+struct MatvecArgs {
+  Fmt fmt = Fmt::Q4;
+  Epi epi = Epi::Store;
+  const float* x = nullptr;
+  const float* norm_w = nullptr;  // when set, x is replaced by rmsnorm(x) * norm_w first
+  float norm_eps = 1e-5f;
+  const int32_t* pos = nullptr;   // device-side position for y_pos_stride (decode step)
+  size_t cols = 0;
+  int n_jobs = 0;
+  MatvecJobDev jobs[kMaxJobs] = {};
+  bool pdl = false;               // launch with programmatic stream serialization
+};
+
+// Validates and launches. Returns an EFG_* status; on EFG_EINVAL/ECUDA the message is
+// left in the thread-local error string.
+int launch_matvec(const MatvecArgs& a, int* d_err, cudaStream_t stream);
+
+// True when the fast (bulk-copy) kernel accepts these arguments; otherwise
+// launch_matvec uses the generic kernel (plain loads, any alignment).
+bool matvec_fast_path_ok(const MatvecArgs& a);
+
+}  // namespace efg

@@ -1,0 +1,155 @@
+/*
+ * efg.h - C ABI of EdgeForge-B200: the packed Q4_0/Q8_0 matrix-product path of
+ * EdgeForge (MG782469/EdgeForge) rebuilt for NVIDIA B200 (sm_100a).
+ *
+ * Conventions
+ *  - Every function returns an int status (EFG_OK = 0, codes in efg_status.h below),
+ *    except the few that return a value and document how they report errors.
+ *    Nothing throws across this boundary. efg_last_error() gives a thread-local
+ *    message for the most recent failure on the calling thread.
+ *  - Pointers named d_* (and every pointer of the *_async / stream-taking calls) are
+ *    DEVICE pointers (cudaMalloc or equivalent) on the current CUDA device. `stream` is
+ *    a cudaStream_t passed as void* (NULL = the legacy default stream). Those calls are
+ *    stream-ordered and return once the work is queued.
+ *  - Calls with host_ in their name take HOST pointers and are synchronous: they are
+ *    the reference's own signatures (include/ef/qkernels.h, include/ef/quant.h) with a
+ *    status code added.
+ *  - Storage types use the reference's numbering (ef::QType, include/ef/quant.h:35).
+ *  - Block layout is the reference's, byte for byte (include/ef/quant.h:22-33):
+ *      Q4_0: 18 bytes / 32 weights = fp16 d, then 16 bytes; byte j holds code j in its
+ *            low nibble and code j+16 in its high nibble; w = (code - 8) * d.
+ *      Q8_0: 34 bytes / 32 weights = fp16 d, then 32 int8 codes; w = code * d.
+ *    A matrix is row-major [rows][cols] with rows packed back to back, exactly as
+ *    stored in an .efq file (include/ef/qfile.h:1-21). cols must be a multiple of 32.
+ *  - Device-side waits are bounded: a kernel that gives up records EFG_ETIMEOUT in a
+ *    per-device error word, read (and cleared) with efg_device_error().
+ */
+#ifndef EFG_H
+#define EFG_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (mirrors edgeforge_b200/csrc/efg_status.h) ------------------ */
+#define EFG_OK 0
+#define EFG_EINVAL 1
+#define EFG_ECUDA 2
+#define EFG_ENCCL 3
+#define EFG_ETIMEOUT 4
+#define EFG_ENOMEM 5
+#define EFG_EFORMAT 6
+#define EFG_ESTATE 7
+
+/* ---- storage types: ef::QType (include/ef/quant.h:35) -------------------------- */
+#define EFG_F32 0
+#define EFG_F16 1
+#define EFG_BF16 2
+#define EFG_Q8_0 3
+#define EFG_Q4_0 4
+
+/* ABI version of this header; bumped on any incompatible change. */
+int efg_abi_version(void);
+
+/* Message of the last failure on this thread ("" if none). Replaces the what() of
+ * ef::Error (include/ef/error.h:11-13). */
+const char* efg_last_error(void);
+
+/* Name of a status code ("EFG_OK", "EFG_EINVAL", ...). */
+const char* efg_status_string(int status);
+
+/* Reads and clears the error word that device-side bounded waits write on the current
+ * device (synchronises the device first). *code receives EFG_OK or EFG_ETIMEOUT. */
+int efg_device_error(int* code);
+
+/* Early weight streaming for the matvec calls made afterwards on this thread (default
+ * off). When on, a matvec may start copying its weight tiles while the previous kernel
+ * in the stream is still running (programmatic dependent launch); it still waits for
+ * that kernel before touching x or y. Only valid when W is not written by the kernels
+ * just before it, which holds for model weights loaded once. Returns the old setting. */
+int efg_set_weight_prefetch(int enable);
+
+/* Bytes of one row of `cols` weights, or 0 with efg_last_error() set when a block type
+ * gets cols % 32 != 0. Replaces ef::qtype_row_bytes (include/ef/quant.h:42,
+ * src/quant.cpp:136-149), which throws in that case. */
+uint64_t efg_row_bytes(int qtype, uint64_t cols);
+
+/* ================================================================ matvec
+ * y[r] = dot(row r of W, x) for r < rows, FP32 activations and accumulation, read
+ * straight from the packed blocks (no dequantized copy). Results agree with the
+ * reference's scalar kernel within 1e-5 of sum_i |w_i x_i| per row (the reference's own
+ * metric, tests/test_qinfer.cpp:58-67); the summation order differs, so not bit for bit.
+ * Deterministic: the same inputs give the same bits on every call. y must not alias
+ * x or W.
+ */
+
+/* Replaces ef::kern::matvec_q4_0 (include/ef/qkernels.h:50, src/qkernels.cpp:67-70). */
+int efg_matvec_q4_0(float* d_y, const uint8_t* d_W, const float* d_x, size_t rows, size_t cols, void* stream);
+/* Replaces ef::kern::matvec_q8_0 (include/ef/qkernels.h:51, src/qkernels.cpp:72-75). */
+int efg_matvec_q8_0(float* d_y, const uint8_t* d_W, const float* d_x, size_t rows, size_t cols, void* stream);
+/* Replaces ef::kern::matvec(y, WeightView, x, pool) (include/ef/qkernels.h:66,
+ * src/qkernels.cpp:275-278) for the packed types EFG_Q4_0 / EFG_Q8_0. */
+int efg_matvec(int qtype, float* d_y, const uint8_t* d_W, const float* d_x, size_t rows, size_t cols, void* stream);
+
+/* One job of a fused multi-matrix matvec: ef::kern::MatvecJob plus the WeightView it
+ * points to (include/ef/qkernels.h:28-34,70-74). */
+typedef struct {
+  float* d_y;
+  int qtype;
+  const uint8_t* d_W;
+  size_t rows, cols;
+  const float* d_x;
+} efg_matvec_job;
+
+/* Replaces ef::kern::matvec_jobs (include/ef/qkernels.h:75, src/qkernels.cpp:280-297):
+ * several products in one launch where the jobs share x, type and cols (q/k/v, gate/up);
+ * otherwise one launch per job. Each job's rows are computed exactly as by efg_matvec. */
+int efg_matvec_jobs(const efg_matvec_job* jobs, size_t n_jobs, void* stream);
+
+/* Replaces ef::kern::dot_q4_0 / dot_q8_0 (include/ef/qkernels.h:47-48): *d_out = dot of
+ * one packed row of n weights with x. */
+int efg_dot_q4_0(float* d_out, const uint8_t* d_row, const float* d_x, size_t n, void* stream);
+int efg_dot_q8_0(float* d_out, const uint8_t* d_row, const float* d_x, size_t n, void* stream);
+
+/* ================================================================ quantize / dequantize
+ * Bit-exact with the reference for every input, NaN and inf included.
+ */
+
+/* Replaces ef::quantize_row (include/ef/quant.h:52, src/quant.cpp:182-218) for
+ * EFG_Q4_0 (search != 0: the MSE scale search + least-squares refinement of
+ * src/quant.cpp:26-99; 0: the absmax scale) and EFG_Q8_0 (search ignored). */
+int efg_quantize_row(int qtype, const float* d_x, size_t n, void* d_out, int search, void* stream);
+/* Replaces ef::dequantize_row (include/ef/quant.h:53, src/quant.cpp:220-249) for the
+ * block types, and EFG_F32/EFG_F16/EFG_BF16 (exact widening). */
+int efg_dequantize_row(int qtype, const void* d_in, size_t n, float* d_out, void* stream);
+/* [rows][cols] forms of the two calls above: the loop of quantize_tensor_rows
+ * (src/quantizer.cpp:121-149) over a whole matrix in one launch. */
+int efg_quantize_rows(int qtype, const float* d_X, size_t rows, size_t cols, void* d_out, int search, void* stream);
+int efg_dequantize_rows(int qtype, const void* d_in, size_t rows, size_t cols, float* d_out, void* stream);
+
+/* Replaces ef::kern::row_f32 (include/ef/qkernels.h:78, src/qkernels.cpp:299-305):
+ * row r of W as FP32 (embedding lookup). r is read from device memory (*d_r) when
+ * d_r is not NULL, else r_host is used. */
+int efg_row_f32(float* d_out, int qtype, const uint8_t* d_W, size_t rows, size_t cols, const int32_t* d_r,
+                size_t r_host, void* stream);
+
+/* ================================================================ host-pointer forms
+ * Synchronous calls with the reference's exact arguments (host pointers). W is
+ * uploaded once and kept resident on the device, keyed by (pointer, size, type): the
+ * reference's W is a read-only view of a memory-mapped .efq (src/model.cpp:71-74), so
+ * the same pointer always holds the same bytes. Call efg_host_release_weights() if
+ * that is not true for the caller. x is copied in and y out on every call.
+ */
+int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols);
+int efg_host_quantize_row(int qtype, const float* x, size_t n, void* out, int search);
+int efg_host_dequantize_row(int qtype, const void* in, size_t n, float* out);
+/* Drops every resident copy made by the host-pointer calls. */
+int efg_host_release_weights(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EFG_H */

@@ -1,0 +1,312 @@
+"""ctypes access to the CPU checkers. TEST INFRASTRUCTURE ONLY.
+
+Two libraries:
+  * ``Oracle`` -> oracle/liboracle.so: the plain-C restatement (efo.c) of the
+    reference's algorithm for the quantized matrix-product path.
+  * ``Reference`` -> oracle/_ref/libefref.so: the reference implementation
+    itself, compiled from its own sources by oracle/Makefile.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import this
+module. The product library (edgeforge_b200) never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "liboracle.so"
+REF_SO = HERE / "_ref" / "libefref.so"
+
+F32, F16, BF16, Q8_0, Q4_0 = 0, 1, 2, 3, 4
+BLOCK_BYTES = {Q4_0: 18, Q8_0: 34}
+
+_fp = C.POINTER(C.c_float)
+_u8 = C.POINTER(C.c_uint8)
+_vp = C.c_void_p
+_sz = C.c_size_t
+
+
+def _p(a: np.ndarray, t=_vp):
+    return a.ctypes.data_as(t)
+
+
+def row_bytes(qtype: int, cols: int) -> int:
+    if qtype in BLOCK_BYTES:
+        if cols % 32:
+            raise ValueError(f"cols={cols} is not a multiple of 32")
+        return cols // 32 * BLOCK_BYTES[qtype]
+    return cols * (4 if qtype == F32 else 2)
+
+
+class _Lib:
+    """Shared numpy-level helpers; subclasses bind the symbol prefix."""
+
+    prefix = ""
+
+    def __init__(self, path: Path):
+        if not path.exists():
+            raise FileNotFoundError(f"{path} is not built (run: make -C {HERE})")
+        self.lib = C.CDLL(str(path))
+        self._bind()
+
+    def _fn(self, name, restype, *argtypes):
+        f = getattr(self.lib, self.prefix + name)
+        f.restype = restype
+        f.argtypes = list(argtypes)
+        return f
+
+    def _bind(self):
+        self.fp16_to_f32 = self._fn("fp16_to_f32", C.c_float, C.c_uint16)
+        self.f32_to_fp16 = self._fn("f32_to_fp16", C.c_uint16, C.c_float)
+        self.bf16_to_f32 = self._fn("bf16_to_f32", C.c_float, C.c_uint16)
+        self.f32_to_bf16 = self._fn("f32_to_bf16", C.c_uint16, C.c_float)
+        self._qrow = self._fn("quantize_row", C.c_int, C.c_int, _fp, _sz, _vp, C.c_int)
+        self._drow = self._fn("dequantize_row", C.c_int, C.c_int, _vp, _sz, _fp)
+        self._dot4 = self._fn("dot_q4_0", C.c_float, _u8, _fp, _sz)
+        self._dot8 = self._fn("dot_q8_0", C.c_float, _u8, _fp, _sz)
+        self._mv4 = self._fn("matvec_q4_0", None, _fp, _u8, _fp, _sz, _sz)
+        self._mv8 = self._fn("matvec_q8_0", None, _fp, _u8, _fp, _sz, _sz)
+        self._rms = self._fn("rmsnorm", None, _fp, _fp, _fp, _sz, C.c_float)
+        self._swiglu = self._fn("swiglu", None, _fp, _fp, _fp, _sz)
+        self._argmax = self._fn("argmax", _sz, _fp, _sz)
+        self._ropet = self._fn("rope_table", None, _fp, _fp, _sz, _sz, C.c_float)
+        self._ropea = self._fn("rope_apply", None, _fp, _sz, _sz, _fp, _fp)
+        self._attn = self._fn("attention", None, _fp, _fp, _fp, _fp, _sz, _sz, _sz, _sz, _fp)
+
+    # ---- rows -------------------------------------------------------------
+    def quantize_row(self, qtype: int, x: np.ndarray, search: bool = True) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(row_bytes(qtype, x.size), dtype=np.uint8)
+        if self._qrow(qtype, _p(x, _fp), x.size, _p(out), int(search)) != 0:
+            raise ValueError("quantize_row rejected the input")
+        return out
+
+    def dequantize_row(self, qtype: int, data: np.ndarray, n: int) -> np.ndarray:
+        data = np.ascontiguousarray(data, dtype=np.uint8)
+        out = np.zeros(n, dtype=np.float32)
+        if self._drow(qtype, _p(data), n, _p(out, _fp)) != 0:
+            raise ValueError("dequantize_row rejected the input")
+        return out
+
+    # ---- packed dots --------------------------------------------------------
+    def dot(self, qtype: int, row: np.ndarray, x: np.ndarray) -> float:
+        f = self._dot4 if qtype == Q4_0 else self._dot8
+        return f(_p(row, _u8), _p(x, _fp), x.size)
+
+    def matvec(self, qtype: int, W: np.ndarray, x: np.ndarray, rows: int) -> np.ndarray:
+        W = np.ascontiguousarray(W, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(rows, dtype=np.float32)
+        f = self._mv4 if qtype == Q4_0 else self._mv8
+        f(_p(y, _fp), _p(W, _u8), _p(x, _fp), rows, x.size)
+        return y
+
+    # ---- FP32 ops -----------------------------------------------------------
+    def rmsnorm(self, x, w, eps):
+        x = np.ascontiguousarray(x, np.float32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.zeros_like(x)
+        self._rms(_p(out, _fp), _p(x, _fp), _p(w, _fp), x.size, eps)
+        return out
+
+    def swiglu(self, g, u):
+        g = np.ascontiguousarray(g, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        out = np.zeros_like(g)
+        self._swiglu(_p(out, _fp), _p(g, _fp), _p(u, _fp), g.size)
+        return out
+
+    def argmax(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        return int(self._argmax(_p(x, _fp), x.size))
+
+    def rope_table(self, max_pos, hd, theta):
+        c = np.zeros((max_pos, hd // 2), np.float32)
+        s = np.zeros((max_pos, hd // 2), np.float32)
+        self._ropet(_p(c, _fp), _p(s, _fp), max_pos, hd, theta)
+        return c, s
+
+    def rope_apply(self, x, n_heads, hd, cos_row, sin_row):
+        x = np.array(x, np.float32, copy=True)
+        cos_row = np.ascontiguousarray(cos_row, np.float32)
+        sin_row = np.ascontiguousarray(sin_row, np.float32)
+        self._ropea(_p(x, _fp), n_heads, hd, _p(cos_row, _fp), _p(sin_row, _fp))
+        return x
+
+    def attention(self, q, k_cache, v_cache, n_pos, H, KV, hd):
+        q = np.ascontiguousarray(q, np.float32)
+        k_cache = np.ascontiguousarray(k_cache, np.float32)
+        v_cache = np.ascontiguousarray(v_cache, np.float32)
+        out = np.zeros(H * hd, np.float32)
+        scores = np.zeros(max(n_pos, 1), np.float32)
+        self._attn(_p(out, _fp), _p(q, _fp), _p(k_cache, _fp), _p(v_cache, _fp), n_pos, H, KV, hd, _p(scores, _fp))
+        return out
+
+
+class Oracle(_Lib):
+    """The C restatement (oracle/efo.c)."""
+
+    prefix = "efo_"
+
+    def __init__(self, path: Path = ORACLE_SO):
+        super().__init__(path)
+
+    def _bind(self):
+        super()._bind()
+        self._qrows = self._fn("quantize_rows", C.c_int, C.c_int, _fp, _sz, _sz, _vp, C.c_int, C.c_int)
+        self._drows = self._fn("dequantize_rows", C.c_int, C.c_int, _vp, _sz, _sz, _fp, C.c_int)
+        self._mvmt = self._fn("matvec_mt", None, C.c_int, _fp, _u8, _fp, _sz, _sz, C.c_int)
+        self._exact = self._fn("exact_dot", None, C.c_int, _u8, _fp, _sz,
+                               C.POINTER(C.c_double), C.POINTER(C.c_double))
+
+    def quantize_rows(self, qtype, X, search=True, threads=os.cpu_count() or 1):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        rows, cols = X.shape
+        out = np.zeros((rows, row_bytes(qtype, cols)), dtype=np.uint8)
+        if self._qrows(qtype, _p(X, _fp), rows, cols, _p(out), int(search), int(threads)) != 0:
+            raise ValueError("quantize_rows rejected the input")
+        return out
+
+    def dequantize_rows(self, qtype, Wq, cols, threads=os.cpu_count() or 1):
+        Wq = np.ascontiguousarray(Wq, dtype=np.uint8)
+        rows = Wq.size // row_bytes(qtype, cols)
+        out = np.zeros((rows, cols), dtype=np.float32)
+        if self._drows(qtype, _p(Wq), rows, cols, _p(out, _fp), int(threads)) != 0:
+            raise ValueError("dequantize_rows rejected the input")
+        return out
+
+    def matvec_mt(self, qtype, W, x, rows, threads=os.cpu_count() or 1):
+        W = np.ascontiguousarray(W, dtype=np.uint8)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.zeros(rows, dtype=np.float32)
+        self._mvmt(qtype, _p(y, _fp), _p(W, _u8), _p(x, _fp), rows, x.size, int(threads))
+        return y
+
+    def exact_dots(self, qtype, W, x, rows):
+        """(exact, magnitude) per row: double dot of the dequantized row with x, sum|w x|."""
+        W = np.ascontiguousarray(W, dtype=np.uint8).reshape(rows, -1)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        ex = np.zeros(rows)
+        mag = np.zeros(rows)
+        e, m = C.c_double(), C.c_double()
+        for r in range(rows):
+            self._exact(qtype, _p(W[r], _u8), _p(x, _fp), x.size, C.byref(e), C.byref(m))
+            ex[r], mag[r] = e.value, m.value
+        return ex, mag
+
+
+class Reference(_Lib):
+    """The reference implementation, compiled from its own sources (oracle/_ref)."""
+
+    prefix = "efr_"
+
+    def __init__(self, path: Path = REF_SO):
+        super().__init__(path)
+
+    def _bind(self):
+        super()._bind()
+        self._fn("last_error", C.c_char_p)
+        self.avx2 = bool(self._fn("avx2_compiled", C.c_int)())
+        self._pool_new = self._fn("pool_new", _vp, C.c_uint)
+        self._pool_free = self._fn("pool_free", None, _vp)
+        self._mv = self._fn("matvec", C.c_int, C.c_int, _vp, C.c_int, _fp, _u8, _fp, _sz, _sz)
+        self._qrows = self._fn("quantize_rows", C.c_int, _vp, C.c_int, _fp, _sz, _sz, _vp, C.c_int)
+        self._drows = self._fn("dequantize_rows", C.c_int, _vp, C.c_int, _vp, _sz, _sz, _fp)
+        self._qmodel = self._fn("quantize_model", C.c_int, C.c_char_p, C.c_char_p, C.c_char_p, C.c_uint)
+        self._dec_new = self._fn("decoder_new", _vp, C.c_char_p, _sz, C.c_uint)
+        self._dec_free = self._fn("decoder_free", None, _vp)
+        self._dec_reset = self._fn("decoder_reset", None, _vp)
+        self._dec_fwd = self._fn("decoder_forward", C.c_int, _vp, C.c_int, C.c_int32, _sz, _fp)
+        self._dec_bpt = self._fn("decoder_bytes_per_token", C.c_uint64, _vp)
+
+    def error(self) -> str:
+        return self.lib.efr_last_error().decode()
+
+    def pool(self, threads: int):
+        return _Pool(self, threads)
+
+    def matvec_backend(self, qtype, W, x, rows, avx2=True, pool=None, y=None):
+        if y is None:
+            y = np.zeros(rows, dtype=np.float32)
+        h = pool.handle if pool is not None else None
+        if self._mv(int(avx2), h, qtype, _p(y, _fp), _p(W, _u8), _p(x, _fp), rows, x.size) != 0:
+            raise RuntimeError(self.error())
+        return y
+
+    def quantize_rows(self, qtype, X, search=True, pool=None):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        rows, cols = X.shape
+        out = np.zeros((rows, row_bytes(qtype, cols)), dtype=np.uint8)
+        h = pool.handle if pool is not None else None
+        if self._qrows(h, qtype, _p(X, _fp), rows, cols, _p(out), int(search)) != 0:
+            raise RuntimeError(self.error())
+        return out
+
+    def dequantize_rows(self, qtype, Wq, cols, pool=None):
+        Wq = np.ascontiguousarray(Wq, dtype=np.uint8)
+        rows = Wq.size // row_bytes(qtype, cols)
+        out = np.zeros((rows, cols), dtype=np.float32)
+        h = pool.handle if pool is not None else None
+        if self._drows(h, qtype, _p(Wq), rows, cols, _p(out, _fp)) != 0:
+            raise RuntimeError(self.error())
+        return out
+
+    def quantize_model(self, model_dir, out_file, policy="auto", threads=0):
+        if self._qmodel(str(model_dir).encode(), str(out_file).encode(), policy.encode(), threads) != 0:
+            raise RuntimeError(self.error())
+
+    def decoder(self, efq_file, max_seq, threads=1):
+        return _Decoder(self, efq_file, max_seq, threads)
+
+
+class _Pool:
+    def __init__(self, ref: Reference, threads: int):
+        self.ref = ref
+        self.threads = threads
+        self.handle = ref._pool_new(threads)
+
+    def close(self):
+        if self.handle:
+            self.ref._pool_free(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
+class _Decoder:
+    """Model::load_efq + Transformer from the reference (one token per forward)."""
+
+    def __init__(self, ref: Reference, efq_file, max_seq, threads):
+        self.ref = ref
+        self.h = ref._dec_new(str(efq_file).encode(), max_seq, threads)
+        if not self.h:
+            raise RuntimeError(ref.error())
+
+    def forward(self, token: int, pos: int, vocab: int, avx2=True, logits=True):
+        out = np.zeros(vocab, dtype=np.float32) if logits else None
+        if self.ref._dec_fwd(self.h, int(avx2), token, pos, _p(out, _fp) if logits else None) != 0:
+            raise RuntimeError(self.ref.error())
+        return out
+
+    def reset(self):
+        self.ref._dec_reset(self.h)
+
+    def bytes_per_token(self):
+        return int(self.ref._dec_bpt(self.h))
+
+    def close(self):
+        if self.h:
+            self.ref._dec_free(self.h)
+            self.h = None
+
+
+def reference_available() -> bool:
+    return REF_SO.exists()

@@ -1,0 +1,181 @@
+"""Packed Q4_0/Q8_0 matvec on the GPU against the CPU oracle, through the C ABI.
+
+Tolerance: the reference's own metric, |y - exact| / sum_i |w_i x_i| <= 1e-5 per row
+(tests/test_qinfer.cpp:58-67, eval_quant.cpp:31), where exact is the double-precision
+dot of the dequantized row. The oracle's scalar kernel is checked against the same
+bound and against the GPU result (their difference is summation order only).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+from conftest import golden, rel_dot_errors
+
+from oracle.oracle import Q4_0, Q8_0, row_bytes
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def dev(a, cuda):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+def run_matvec(efg, cuda, qt, W: np.ndarray, x: np.ndarray, rows: int, offset: int = 0) -> np.ndarray:
+    import torch
+
+    Wf = np.ascontiguousarray(W).reshape(-1)
+    if offset:
+        # place W at a byte offset to force the generic (unaligned) path
+        buf = torch.zeros(Wf.size + 64, dtype=torch.uint8, device=cuda)
+        buf[offset:offset + Wf.size] = dev(Wf, cuda)
+        dW = buf[offset:offset + Wf.size]
+    else:
+        dW = dev(Wf, cuda)
+    dx = dev(x.astype(np.float32), cuda)
+    dy = torch.full((max(rows, 1),), float("nan"), dtype=torch.float32, device=cuda)
+    efg.matvec(qt, dy, dW, dx, rows, x.size)
+    torch.cuda.synchronize()
+    return dy.cpu().numpy()[:rows]
+
+
+def random_packed(qt, rows, cols, rng):
+    rb = row_bytes(qt, cols)
+    v = rng.integers(0, 256, rows * rb, dtype=np.uint8).reshape(-1, 18 if qt == Q4_0 else 34)
+    h = rng.uniform(-0.05, 0.05, v.shape[0]).astype(np.float16).view(np.uint16)
+    v[:, 0] = (h & 0xFF).astype(np.uint8)
+    v[:, 1] = (h >> 8).astype(np.uint8)
+    return v.reshape(rows, rb)
+
+
+@pytest.mark.parametrize("n", [32, 64, 96, 2048, 5632])
+@pytest.mark.parametrize("qt", [Q4_0, Q8_0])
+def test_matvec_golden_vectors(efg_lib, cuda, oracle, n, qt):
+    g = golden("matvec.npz")
+    name = "q4" if qt == Q4_0 else "q8"
+    W, x = g[f"{name}_W_{n}"], g[f"x_{n}"]
+    y = run_matvec(efg_lib, cuda, qt, W, x, 24)
+    assert rel_dot_errors(oracle, qt, W, x, 24, y).max() < TOL
+    ys = g[f"{name}_y_scalar_{n}"]  # the reference's scalar kernel
+    mag = oracle.exact_dots(qt, W, x, 24)[1]
+    assert (np.abs(y.astype(np.float64) - ys) / np.maximum(mag, 1e-30)).max() < 2 * TOL
+
+
+def test_hand_blocks_exact(efg_lib, cuda, oracle):
+    """test_qinfer.cpp:100-122: exact results on hand-written blocks."""
+    one = oracle.f32_to_fp16(1.0)
+    blk = np.zeros(18 * 2, np.uint8)  # two blocks (64 columns: the fast path)
+    blk[0], blk[1] = one & 0xFF, one >> 8
+    blk[2:18] = 0x88
+    blk[2 + 3] = 0x0F
+    blk[18], blk[19] = one & 0xFF, one >> 8
+    blk[20:36] = 0x88
+    x = np.zeros(64, np.float32)
+    x[3], x[19] = 2.0, 0.5
+    assert run_matvec(efg_lib, cuda, Q4_0, blk, x, 1)[0] == 10.0
+    assert run_matvec(efg_lib, cuda, Q4_0, blk[:18], x[:32], 1)[0] == 10.0  # generic path
+    blk[0] = blk[1] = 0
+    assert run_matvec(efg_lib, cuda, Q4_0, blk, x, 1)[0] == 0.0
+    b8 = np.zeros(68, np.uint8)
+    for o in (0, 34):
+        b8[o], b8[o + 1] = one & 0xFF, one >> 8
+        b8[o + 2] = np.uint8(256 - 127)
+        b8[o + 2 + 31] = 127
+    x[:] = 1.0
+    assert run_matvec(efg_lib, cuda, Q8_0, b8, x, 1)[0] == 0.0
+    b8[2 + 5] = 3
+    assert run_matvec(efg_lib, cuda, Q8_0, b8, x, 1)[0] == 3.0
+
+
+@pytest.mark.parametrize("qt", [Q4_0, Q8_0])
+@pytest.mark.parametrize("rows,cols", [(1, 64), (3, 128), (37, 192), (300, 256), (5, 320), (129, 1024),
+                                       (7, 96), (11, 32), (1000, 4096), (33, 8192), (2, 11264)])
+def test_matvec_shapes(efg_lib, cuda, oracle, qt, rows, cols):
+    rng = np.random.default_rng(rows * 7919 + cols)
+    W = random_packed(qt, rows, cols, rng)
+    x = rng.standard_normal(cols).astype(np.float32) * np.where(rng.standard_normal(cols) > 2, 30, 1).astype(np.float32)
+    y = run_matvec(efg_lib, cuda, qt, W, x, rows)
+    assert rel_dot_errors(oracle, qt, W, x, rows, y).max() < TOL
+
+
+@pytest.mark.parametrize("qt", [Q4_0, Q8_0])
+def test_unaligned_weights_take_the_generic_path(efg_lib, cuda, oracle, qt):
+    rng = np.random.default_rng(5)
+    W = random_packed(qt, 40, 256, rng)
+    x = rng.standard_normal(256).astype(np.float32)
+    for off in (2, 6, 8):
+        y = run_matvec(efg_lib, cuda, qt, W, x, 40, offset=off)
+        assert rel_dot_errors(oracle, qt, W, x, 40, y).max() < TOL
+
+
+def test_empty_and_zero_width(efg_lib, cuda):
+    import torch
+
+    y = torch.full((4,), 5.0, device=cuda)
+    efg_lib.matvec(Q4_0, y, torch.zeros(1, dtype=torch.uint8, device=cuda), torch.zeros(1, device=cuda), 0, 64)
+    torch.cuda.synchronize()
+    assert y.cpu().tolist() == [5.0] * 4  # rows == 0: nothing written
+    efg_lib.matvec(Q4_0, y, torch.zeros(1, dtype=torch.uint8, device=cuda), torch.zeros(1, device=cuda), 4, 0)
+    torch.cuda.synchronize()
+    assert y.cpu().tolist() == [0.0] * 4  # zero blocks: every dot is 0
+
+
+def test_bad_row_length_raises_like_the_reference(efg_lib, cuda):
+    import torch
+
+    t = torch.zeros(64, device=cuda)
+    with pytest.raises(efg_lib.EdgeForgeError, match="Q4_0 needs a row length divisible by 32, got 30"):
+        efg_lib.matvec_q4_0(t, t, t, 1, 30)
+
+
+def test_deterministic_and_jobs_equal_single_calls(efg_lib, cuda, oracle):
+    """matvec_jobs computes each job exactly like matvec (qkernels.h:68-69), and results
+    do not change between calls."""
+    import torch
+
+    rng = np.random.default_rng(9)
+    x = dev(rng.standard_normal(2048).astype(np.float32), cuda)
+    mats = [dev(random_packed(Q4_0, r, 2048, rng), cuda) for r in (2048, 256, 256)]
+    ys = [torch.empty(r, device=cuda) for r in (2048, 256, 256)]
+    efg_lib.matvec_jobs([(y, Q4_0, W, y.numel(), 2048, x) for y, W in zip(ys, mats)])
+    singles = []
+    for W, y in zip(mats, ys):
+        s = torch.empty_like(y)
+        efg_lib.matvec_q4_0(s, W, x, y.numel(), 2048)
+        singles.append(s)
+    torch.cuda.synchronize()
+    for a, b in zip(ys, singles):
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+    again = torch.empty_like(ys[0])
+    efg_lib.matvec_q4_0(again, mats[0], x, 2048, 2048)
+    torch.cuda.synchronize()
+    assert torch.equal(again.view(torch.int32), ys[0].view(torch.int32))
+    assert efg_lib.device_error() == 0
+
+
+@pytest.mark.parametrize("cfg", ["c0_q4_5632x2048", "c1_q8_32000x2048", "down_q4_2048x5632"])
+def test_config_shapes_quantized_gaussian(efg_lib, cuda, oracle, cfg):
+    """BASELINE configs 0/1 (and the down_proj shape of config 3): W ~ N(0, 0.02)
+    quantized by the reference algorithm, x ~ N(0, 1)."""
+    qt, rows, cols = {"c0_q4_5632x2048": (Q4_0, 5632, 2048), "c1_q8_32000x2048": (Q8_0, 32000, 2048),
+                      "down_q4_2048x5632": (Q4_0, 2048, 5632)}[cfg]
+    rng = np.random.default_rng(0)
+    X = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    W = oracle.quantize_rows(qt, X, search=True)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = run_matvec(efg_lib, cuda, qt, W, x, rows)
+    assert rel_dot_errors(oracle, qt, W, x, rows, y).max() < TOL
+    yo = oracle.matvec_mt(qt, W, x, rows)
+    assert np.abs(y - yo).max() <= 1e-5 * np.abs(yo).max() * 10
+
+
+def test_host_pointer_matvec_keeps_weights_resident(efg_lib, cuda, oracle):
+    rng = np.random.default_rng(3)
+    W = random_packed(Q8_0, 500, 2048, rng)
+    for _ in range(3):
+        x = rng.standard_normal(2048).astype(np.float32)
+        y = efg_lib.host_matvec(Q8_0, W, x, 500)
+        assert rel_dot_errors(oracle, Q8_0, W, x, 500, y).max() < TOL
+    efg_lib.host_release_weights()
