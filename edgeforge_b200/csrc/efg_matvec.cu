@@ -3,10 +3,12 @@
 // The reference computes y = W x row by row on CPU threads, one 18/34-byte block at a
 // time (src/qkernels.cpp:39-75, 213-297). Here the whole matrix streams from HBM once:
 //
-//  * One persistent CTA per SM. A producer warp copies row tiles (TR whole rows, a
-//    contiguous byte range of the packed matrix) into a ring of NS shared-memory stages
-//    with 1-D bulk async copies (cp.async.bulk, completion counted on an mbarrier), so
-//    no thread spends instructions moving weights and every byte of HBM is read once.
+//  * One persistent CTA per SM. A producer warp copies row tiles (RB whole rows, a
+//    contiguous byte range of the packed matrix, a few KB) into a ring of up to 32
+//    shared-memory stages with 1-D bulk async copies (cp.async.bulk, completion counted
+//    on an mbarrier), so >100 KB per SM stays in flight, no thread spends instructions
+//    moving weights and every byte of HBM is read once. Tile k of a CTA belongs to row
+//    group k % RG (the G warps that together cover one row).
 //  * Each consumer lane owns one 64-column "slot" of a row: a pair of blocks, which is
 //    9 (Q4_0) or 17 (Q8_0) aligned 32-bit words whatever the row's offset, read from
 //    shared memory without bank conflicts (stride 9 or 17 words). The lane keeps the 64
@@ -36,7 +38,7 @@ namespace efg {
 
 namespace {
 
-constexpr int kMaxThreads = 384;  // 1 producer warp + up to 11 consumer warps
+constexpr int kMaxThreads = 512;  // 1 producer warp + up to 15 consumer warps (4 warps per SMSP: 128 registers)
 constexpr int kMaxConsumerWarps = kMaxThreads / 32 - 1;
 constexpr int kNormBarrier = 15;  // named barrier id for the RMSNorm reduction
 
@@ -46,7 +48,7 @@ struct KParams {
   float norm_eps;
   int* err;
   const int32_t* pos;
-  uint32_t cols, rb_words, S, G, RG, TR, NS, stage_bytes, n_jobs, tiles_total;
+  uint32_t cols, rb_words, S, G, H, RG, TR, BPS, NS, stage_bytes, n_jobs, tiles_total;
   uint32_t job_tile_start[kMaxJobs + 1];
   MatvecJobDev jobs[kMaxJobs];
 };
@@ -101,8 +103,12 @@ __device__ __forceinline__ void q8_half(uint32_t w, float2 xp, float2& a) {
   a = __ffma2_rn(__fadd2_rn(f2(q8_field<0>(w), q8_field<8>(w)), f2(-q8_bias<0>(), -q8_bias<8>())), xp, a);
 }
 
+// fp16 bits -> float on the FMA pipe (mixed-precision add of -0.0, exact for every
+// input; the plain conversion goes through the slower XU pipe).
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
-  return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+  float r;
+  asm("add.rn.f32.f16 %0, %1, 0f80000000;" : "=f"(r) : "h"(static_cast<unsigned short>(h)));
+  return r;
 }
 
 // Column offset (within the 64-column slot) of x pair k: Q4 pairs (c, c + 16) for the
@@ -123,11 +129,18 @@ constexpr int slot_words() {
 }
 
 // Dot of one slot (64 columns, two blocks) with the lane's x registers.
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+// saddr: shared-memory address of the slot's first word.
 template <Fmt F>
-__device__ __forceinline__ float slot_dot(const uint32_t* __restrict__ wp, const float2 (&xp)[32]) {
+__device__ __forceinline__ float slot_dot(uint32_t saddr, const float2 (&xp)[32]) {
   uint32_t w[slot_words<F>()];
 #pragma unroll
-  for (int i = 0; i < slot_words<F>(); ++i) w[i] = wp[i];
+  for (int i = 0; i < slot_words<F>(); ++i) w[i] = lds32(saddr + 4u * i);
   const float2 z = f2(0.f, 0.f);
   float2 a0 = z, b0 = z, a1 = z, b1 = z;
   float d0, d1;
@@ -185,19 +198,29 @@ __device__ __forceinline__ void locate_tile(const KParams& p, uint32_t tile, uin
 
 template <Fmt F, int RB, Epi E, bool NORM>
 __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __grid_constant__ KParams p) {
+  // A tile (one stage) holds TR = BPS * H * RB/n_mat rows of each matrix and is consumed
+  // by one row group: G x H warps, G warps covering the 64-column slots of a row and H
+  // warps taking different rows. It is read in BPS batches; in each batch warp (g, h)
+  // handles RB rows (for SwiGLU RB/2 gate rows and the same RB/2 up rows, the up rows
+  // being stored TR rows on). The CTA's k-th tile (tile = blockIdx.x + k * gridDim.x)
+  // goes to stage k % NS and row group k % RG. NS is a multiple of RG, so stage s belongs
+  // to row group s % RG alone and its phases are consumed in order.
   extern __shared__ __align__(128) uint8_t smem[];
-  const uint32_t nc = p.G * p.RG;  // consumer warps
+  const uint32_t nc = p.G * p.H * p.RG;  // consumer warps
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.NS * p.stage_bytes);
   uint64_t* empty = full + p.NS;
-  float* red = reinterpret_cast<float*>(empty + p.NS);  // [2][RG][RB][G]
-  double* norm_red = reinterpret_cast<double*>(red + 2 * p.RG * RB * p.G + 2);
+  float* red = reinterpret_cast<float*>(empty + p.NS);                               // [RG*H][2][RB][G]
+  double* norm_red = reinterpret_cast<double*>(red + 2 * p.RG * p.H * RB * p.G + 2);  // [16]
+  float* xs = reinterpret_cast<float*>(norm_red + 16);                          // [S][65]
+  constexpr int n_mat = E == Epi::SwiGLU ? 2 : 1;
+  constexpr uint32_t RBH = E == Epi::SwiGLU ? RB / 2 : RB;  // rows of each matrix per batch
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < p.NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], nc);
+      mbar_init(&empty[s], p.G * p.H);
     }
     fence_barrier_init();
   }
@@ -210,21 +233,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
     // ------------------------------------------------------------ producer
     if (lane != 0) return;
     const uint64_t pol = l2_evict_first_policy();
-    uint32_t it = 0;
+    const uint32_t rb = p.rb_words * 4u;
+    uint32_t k = 0, s = 0, round = 0;
     bool ok = true;
-    for (uint32_t tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++it) {
-      const uint32_t s = it % p.NS;
-      if (it >= p.NS && !mbar_wait(&empty[s], ((it / p.NS) & 1u) ^ 1u, p.err)) {
+    for (uint32_t tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++k) {
+      if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u, p.err)) {
         ok = false;
         break;
       }
       uint32_t j, r0, nrows;
       locate_tile(p, tile, j, r0, nrows);
-      const uint32_t rb = p.rb_words * 4u;
       const uint32_t bytes = nrows * rb;
       const uint32_t bulk = bytes & ~15u;
       uint8_t* dst = stages + s * p.stage_bytes;
-      const int n_mat = E == Epi::SwiGLU ? 2 : 1;
       // The ragged end of the last tile (bytes % 16) is copied by this thread; the
       // release of the arrive below orders it before the consumers' acquire.
       for (int m = 0; m < n_mat; ++m) {
@@ -233,31 +254,41 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
         for (uint32_t b = bulk; b < bytes; ++b) d[b] = src[b];
       }
       mbar_arrive_expect_tx(&full[s], bulk * n_mat);
-      for (int m = 0; m < n_mat; ++m) {
-        const uint8_t* src = p.jobs[E == Epi::SwiGLU ? m : j].W + static_cast<size_t>(r0) * rb;
-        if (bulk) bulk_g2s(dst + m * (p.TR * rb), src, bulk, &full[s], pol);
+      if (bulk) {
+        for (int m = 0; m < n_mat; ++m) {
+          const uint8_t* src = p.jobs[E == Epi::SwiGLU ? m : j].W + static_cast<size_t>(r0) * rb;
+          bulk_g2s(dst + m * (p.TR * rb), src, bulk, &full[s], pol);
+        }
+      }
+      if (++s == p.NS) {
+        s = 0;
+        ++round;
       }
     }
     if (!ok) {
       // Let copies already issued land before the CTA can exit (bounded as well).
-      const uint32_t first = it > p.NS ? it - p.NS : 0;
-      for (uint32_t k = first; k < it; ++k) mbar_wait(&full[k % p.NS], (k / p.NS) & 1u, nullptr);
+      const uint32_t first = k > p.NS ? k - p.NS : 0;
+      for (uint32_t q = first; q < k; ++q) mbar_wait(&full[q % p.NS], (q / p.NS) & 1u, nullptr);
     }
     return;
   }
 
   // -------------------------------------------------------------- consumers
-  const uint32_t g = warp % p.G, rg = warp / p.G;
+  const uint32_t g = warp % p.G, h = (warp / p.G) % p.H, rg = warp / (p.G * p.H);
   const uint32_t slot = g * 32 + lane;
   const bool active = slot < p.S;
   pdl_wait();  // x, norm weights and y belong to the previous kernel in the stream
 
-  float inv = 1.0f;
+  // x is read once per CTA with coalesced loads into a padded shared array (65 floats
+  // per 64-column slot, so the per-lane reads below hit 32 different banks), with the
+  // RMSNorm folded in: h = w * (x * inv) exactly as src/kernels.cpp:74.
+  const uint32_t tid = threadIdx.x;  // consumers are threads [0, nc * 32)
+  for (uint32_t i = tid; i < p.cols; i += nc * 32) xs[(i >> 6) * 65 + (i & 63)] = p.x[i];
   if constexpr (NORM) {
     // rmsnorm scale from the whole x (src/kernels.cpp:69-73): double sum of squares.
     double ss = 0.0;
-    for (uint32_t i = threadIdx.x; i < p.cols; i += nc * 32) {
-      const double v = static_cast<double>(p.x[i]);
+    for (uint32_t i = tid; i < p.cols; i += nc * 32) {
+      const double v = static_cast<double>(xs[(i >> 6) * 65 + (i & 63)]);
       ss += v * v;
     }
     ss = warp_sum_d(ss);
@@ -266,77 +297,82 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
     double tot = 0.0;
     for (uint32_t w = 0; w < nc; ++w) tot += norm_red[w];
     const double mean = p.cols ? tot / static_cast<double>(p.cols) : 0.0;
-    inv = static_cast<float>(1.0 / sqrt(mean + static_cast<double>(p.norm_eps)));
+    const float inv = static_cast<float>(1.0 / sqrt(mean + static_cast<double>(p.norm_eps)));
+    for (uint32_t i = tid; i < p.cols; i += nc * 32) {
+      float& h = xs[(i >> 6) * 65 + (i & 63)];
+      h = p.norm_w[i] * (h * inv);
+    }
   }
+  named_barrier(kNormBarrier, nc * 32);
   float2 xp[32];
 #pragma unroll
   for (int k = 0; k < 32; ++k) {
     float lo = 0.f, hi = 0.f;
     if (active) {
-      const uint32_t c = slot * 64 + pair_col<F>(k);
-      lo = p.x[c];
-      hi = p.x[c + pair_step<F>()];
-      if constexpr (NORM) {
-        lo = p.norm_w[c] * (lo * inv);
-        hi = p.norm_w[c + pair_step<F>()] * (hi * inv);
-      }
+      const float* xr = xs + slot * 65 + pair_col<F>(k);
+      lo = xr[0];
+      hi = xr[pair_step<F>()];
     }
     xp[k] = f2(lo, hi);
   }
 
-  constexpr int RBH = E == Epi::SwiGLU ? RB / 2 : RB;  // logical rows per warp per tile
+  const uint32_t lane_base = smem_addr(stages) + slot * slot_words<F>() * 4u;
+  const uint32_t row_bytes = p.rb_words * 4u;
+  float* rbase = red + (rg * p.H + h) * 2 * RB * p.G;
+  const uint32_t batch_rows = p.H * RBH;  // rows of each matrix per batch
   // After a failed (timed-out) wait a warp stops reading and writing but keeps walking
-  // the tile loop, so the named barriers of its row group still see every warp.
+  // its tiles, so the named barriers of its row group still see every warp.
   bool alive = true;
-  uint32_t it = 0, buf = 0;
-  for (uint32_t tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++it) {
-    const uint32_t s = it % p.NS;
-    if (alive && !mbar_wait(&full[s], (it / p.NS) & 1u, p.err)) alive = false;
+  uint32_t buf = 0, s = rg, phase = 0;
+  for (uint32_t tile = blockIdx.x + rg * gridDim.x; tile < p.tiles_total; tile += p.RG * gridDim.x) {
+    if (alive && !mbar_wait(&full[s], phase, p.err)) alive = false;
     uint32_t j, r0, nrows;
     locate_tile(p, tile, j, r0, nrows);
     if (!alive) nrows = 0;
-    const uint32_t* stage = reinterpret_cast<const uint32_t*>(stages + s * p.stage_bytes);
-    float acc[RB];
+    const uint32_t sbase = lane_base + s * p.stage_bytes;
+    float* y = p.jobs[j].y + (p.pos ? *p.pos * p.jobs[j].y_pos_stride : 0);
+    for (uint32_t b = 0; b < p.BPS; ++b) {
+      float acc[RB];
 #pragma unroll
-    for (int i = 0; i < RB; ++i) {
-      // SwiGLU: the first RB/2 entries are gate rows, the rest the matching up rows
-      // (stored TR rows further on in the stage).
-      const uint32_t lr = rg * RBH + (i % RBH);
-      const uint32_t srow = (E == Epi::SwiGLU && i >= RBH) ? lr + p.TR : lr;
-      acc[i] = (active && lr < nrows) ? slot_dot<F>(stage + srow * p.rb_words + slot * slot_words<F>(), xp) : 0.f;
+      for (int i = 0; i < static_cast<int>(RB); ++i) {
+        const uint32_t lr = b * batch_rows + h * RBH + i % RBH;  // row within the tile, per matrix
+        const uint32_t srow = (E == Epi::SwiGLU && i >= static_cast<int>(RBH)) ? lr + p.TR : lr;
+        acc[i] = (active && lr < nrows) ? slot_dot<F>(sbase + srow * row_bytes, xp) : 0.f;
+      }
+      if (b + 1 == p.BPS) {
+        __syncwarp();
+        if (alive && lane == 0) mbar_arrive(&empty[s]);  // all reads of this stage are done
+      }
+      const float v = warp_reduce_rows<RB>(acc, lane);
+      const float mine = __shfl_sync(0xFFFFFFFFu, v, (lane % RB) * (32 / RB));  // lane i < RB: row i
+      float total = mine;
+      bool writer = lane < static_cast<int>(RB);
+      if (p.G > 1) {
+        float* rbuf = rbase + buf * RB * p.G;
+        if (lane < static_cast<int>(RB)) rbuf[lane * p.G + g] = mine;
+        named_barrier(1 + rg * p.H + h, p.G * 32);
+        writer = writer && g == 0;
+        if (writer) {
+          total = 0.f;
+          for (uint32_t q = 0; q < p.G; ++q) total += rbuf[lane * p.G + q];
+        }
+        buf ^= 1u;
+      }
+      const uint32_t lr = b * batch_rows + h * RBH + lane;
+      if constexpr (E == Epi::SwiGLU) {
+        const float up = __shfl_down_sync(0xFFFFFFFFu, total, RBH);
+        if (writer && lane < static_cast<int>(RBH) && lr < nrows) y[r0 + lr] = silu(total) * up;
+      } else {
+        if (writer && lr < nrows) {
+          if constexpr (E == Epi::Add) y[r0 + lr] += total;
+          else y[r0 + lr] = total;
+        }
+      }
     }
-    __syncwarp();
-    if (alive && lane == 0) mbar_arrive(&empty[s]);
-
-    const float v = warp_reduce_rows<RB>(acc, lane);
-    const float mine = __shfl_sync(0xFFFFFFFFu, v, (lane % RB) * (32 / RB));  // lane i < RB: row i
-    float total = mine;
-    bool writer = lane < RB;
-    if (p.G > 1) {
-      float* rbuf = red + buf * p.RG * RB * p.G;
-      if (lane < RB) rbuf[(rg * RB + lane) * p.G + g] = mine;
-      named_barrier(1 + rg, p.G * 32);
-      writer = writer && g == 0;
-      if (writer) {
-        total = 0.f;
-        for (uint32_t q = 0; q < p.G; ++q) total += rbuf[(rg * RB + lane) * p.G + q];
-      }
-      buf ^= 1u;
-    }
-    if constexpr (E == Epi::SwiGLU) {
-      const float up = __shfl_down_sync(0xFFFFFFFFu, total, RBH);
-      const uint32_t lr = rg * RBH + lane;
-      if (writer && lane < RBH && lr < nrows) {
-        float* y = p.jobs[0].y + (p.pos ? *p.pos * p.jobs[0].y_pos_stride : 0);
-        y[r0 + lr] = silu(total) * up;
-      }
-    } else {
-      const uint32_t lr = rg * RB + lane;
-      if (writer && lr < nrows) {
-        float* y = p.jobs[j].y + (p.pos ? *p.pos * p.jobs[j].y_pos_stride : 0);
-        if constexpr (E == Epi::Add) y[r0 + lr] += total;
-        else y[r0 + lr] = total;
-      }
+    s += p.RG;
+    if (s >= p.NS) {
+      s -= p.NS;
+      phase ^= 1u;
     }
   }
 }
@@ -439,58 +475,79 @@ GenFn pick_generic(Fmt f, Epi e) {
 }
 
 struct Plan {
-  uint32_t S, G, RG, RB, TR, NS, stage_bytes, tiles;
+  uint32_t S, G, H, RG, RB, BPS, TR, NS, stage_bytes, tiles;
   size_t smem;
   bool ok;
 };
 
-constexpr size_t kSmemBudget = 200 * 1024;
+constexpr size_t kSmemBudget = 212 * 1024;
+constexpr uint32_t kMaxStages = 48;
 
+// Chooses the shape of the pipeline for one launch. Measured on B200: a CTA's bulk-copy
+// ring streams at full rate with stages of >= 16 KB and ~200 KB in flight per SM (4-5 KB
+// stages stall at under half rate), and 16 consumer warps hide the arithmetic. The
+// candidates are (H warps per stage splitting rows, RB rows per warp per batch, BPS
+// batches per stage); each must keep every row group busy when the matrix is large
+// enough, with NS a multiple of the row-group count.
 Plan plan_fast(const MatvecArgs& a, const DeviceInfo& dev) {
-  Plan pl{};
+  Plan best{};
+  best.ok = false;
   const uint32_t bb = a.fmt == Fmt::Q4 ? 18u : 34u;
   const uint32_t rb = static_cast<uint32_t>(a.cols / 32 * bb);
-  pl.S = static_cast<uint32_t>(a.cols / 64);
-  pl.G = (pl.S + 31) / 32;
-  pl.ok = a.cols % 64 == 0 && pl.G >= 1 && pl.G <= static_cast<uint32_t>(kMaxConsumerWarps);
-  if (!pl.ok) return pl;
-  pl.RG = std::max<uint32_t>(1, 8 / pl.G);
-  if (pl.G * pl.RG > static_cast<uint32_t>(kMaxConsumerWarps)) pl.RG = kMaxConsumerWarps / pl.G;
+  const uint32_t S = static_cast<uint32_t>(a.cols / 64);
+  const uint32_t G = (S + 31) / 32;
+  if (a.cols % 64 != 0 || G < 1 || G > static_cast<uint32_t>(kMaxConsumerWarps)) return best;
   const int n_mat = a.epi == Epi::SwiGLU ? 2 : 1;
+  const int nj = a.epi == Epi::SwiGLU ? 1 : a.n_jobs;
   auto tiles_for = [&](uint32_t TR) {
     uint32_t t = 0;
-    const int nj = a.epi == Epi::SwiGLU ? 1 : a.n_jobs;
     for (int j = 0; j < nj; ++j) t += (a.jobs[j].rows + TR - 1) / TR;
     return t;
   };
-  // Largest row batch that still leaves >= 2 tiles per SM (load balance); if none
-  // does, the smallest one. The tile byte size must be a multiple of 16 so every tile
-  // starts 16-byte aligned for the bulk copy.
-  pl.RB = 0;
-  for (uint32_t rbv : {4u, 2u, 1u}) {
-    if (a.epi == Epi::SwiGLU && rbv < 2) continue;
-    const uint32_t TR = pl.RG * (a.epi == Epi::SwiGLU ? rbv / 2 : rbv);
-    if ((static_cast<uint64_t>(TR) * rb) % 16 != 0) continue;
-    pl.RB = rbv;
-    if (tiles_for(TR) >= 2u * static_cast<uint32_t>(dev.sm_count)) break;
+  const size_t xs_bytes = static_cast<size_t>(S) * 65 * 4;
+  long best_score = -1;
+  for (uint32_t H : {1u, 2u, 4u}) {
+    const uint32_t RG = static_cast<uint32_t>(kMaxConsumerWarps) / (G * H);
+    if (RG < 1) continue;
+    for (uint32_t rbv : {4u, 2u, 1u}) {
+      if (a.epi == Epi::SwiGLU && rbv < 2) continue;
+      const uint32_t rbh = a.epi == Epi::SwiGLU ? rbv / 2 : rbv;
+      for (uint32_t bps : {1u, 2u, 4u}) {
+        const uint32_t TR = bps * H * rbh;
+        if ((static_cast<uint64_t>(TR) * rb) % 16 != 0) continue;
+        const uint64_t stage = (static_cast<uint64_t>(TR) * rb * n_mat + 15) / 16 * 16;
+        const size_t tail = 2 * 8 * kMaxStages + (2 * RG * H * rbv * G + 2) * 4 + 16 * 8 + xs_bytes + 128;
+        const size_t budget = std::min(kSmemBudget, dev.smem_optin > tail ? dev.smem_optin - tail : 0);
+        uint32_t NS = static_cast<uint32_t>(std::min<uint64_t>(kMaxStages, budget / stage));
+        NS = NS / RG * RG;
+        if (NS < RG || NS < 2) continue;
+        const uint32_t tiles = tiles_for(TR);
+        const bool busy = tiles >= static_cast<uint32_t>(dev.sm_count) * RG;
+        const long stage_kb = static_cast<long>(std::min<uint64_t>(stage, 16384) / 1024);
+        const long flight_kb = static_cast<long>(std::min<uint64_t>(NS * stage, 160 * 1024) / 1024);
+        const long warps = static_cast<long>(G * H * RG);
+        // busy first (else the most tiles), then stage size, bytes in flight, warps, RB
+        const long score = busy ? (1L << 40) + (stage_kb << 28) + (flight_kb << 16) + (warps << 8) + (rbv << 4)
+                                : static_cast<long>(tiles) * 64 + rbv;
+        if (score > best_score) {
+          best_score = score;
+          best.S = S;
+          best.G = G;
+          best.H = H;
+          best.RG = RG;
+          best.RB = rbv;
+          best.BPS = bps;
+          best.TR = TR;
+          best.NS = NS;
+          best.stage_bytes = static_cast<uint32_t>(stage);
+          best.tiles = tiles;
+          best.smem = NS * stage + 2 * NS * 8 + (2 * RG * H * rbv * G + 2) * 4 + 16 * 8 + xs_bytes;
+          best.ok = true;
+        }
+      }
+    }
   }
-  if (pl.RB == 0) {
-    pl.ok = false;
-    return pl;
-  }
-  pl.TR = pl.RG * (a.epi == Epi::SwiGLU ? pl.RB / 2 : pl.RB);
-  pl.tiles = tiles_for(pl.TR);
-  pl.stage_bytes = static_cast<uint32_t>((static_cast<uint64_t>(pl.TR) * rb * n_mat + 127) / 128 * 128);
-  const size_t tail = 2 * 8 * 16 /* barriers */ + (2 * pl.RG * pl.RB * pl.G + 2) * 4 + 16 * 8 + 128;
-  const size_t budget = std::min(kSmemBudget, dev.smem_optin > tail ? dev.smem_optin - tail : 0);
-  pl.NS = static_cast<uint32_t>(std::min<size_t>(8, budget / std::max<uint32_t>(pl.stage_bytes, 1)));
-  if (pl.NS < 2) {
-    pl.ok = false;
-    return pl;
-  }
-  pl.smem = pl.NS * static_cast<size_t>(pl.stage_bytes) + 2 * pl.NS * 8 + (2 * pl.RG * pl.RB * pl.G + 2) * 4 +
-            16 * 8;
-  return pl;
+  return best;
 }
 
 }  // namespace
@@ -565,8 +622,10 @@ int launch_matvec(const MatvecArgs& a, int* d_err, cudaStream_t stream) {
   if (fast) {
     k.S = pl.S;
     k.G = pl.G;
+    k.H = pl.H;
     k.RG = pl.RG;
     k.TR = pl.TR;
+    k.BPS = pl.BPS;
     k.NS = pl.NS;
     k.stage_bytes = pl.stage_bytes;
     k.rb_words = static_cast<uint32_t>(a.cols / 32 * (a.fmt == Fmt::Q4 ? 18 : 34) / 4);
@@ -582,7 +641,7 @@ int launch_matvec(const MatvecArgs& a, int* d_err, cudaStream_t stream) {
     if (int st = ensure_smem_attr(reinterpret_cast<const void*>(fn), pl.smem)) return st;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(std::min<uint32_t>(k.tiles_total, static_cast<uint32_t>(dev->sm_count)));
-    cfg.blockDim = dim3(32 * (pl.G * pl.RG + 1));
+    cfg.blockDim = dim3(32 * (pl.G * pl.H * pl.RG + 1));
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = stream;
     cfg.attrs = attr;

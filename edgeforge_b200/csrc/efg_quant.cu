@@ -30,6 +30,16 @@ __device__ __forceinline__ int round_to_int(float v) {
   return static_cast<int>(r);
 }
 
+// float(code) * d with the NaN results of the reference's x86-64 build (SSE mulss):
+// a NaN operand comes back quieted with its payload, and 0 * inf gives the "real
+// indefinite" NaN 0xFFC00000. For every other input this is the IEEE product.
+__device__ __forceinline__ float dequant_mul(int code, float d) {
+  const uint32_t db = __float_as_uint(d);
+  if ((db & 0x7FFFFFFFu) > 0x7F800000u) return __uint_as_float(db | 0x00400000u);
+  if ((db & 0x7FFFFFFFu) == 0x7F800000u && code == 0) return __uint_as_float(0xFFC00000u);
+  return __fmul_rn(static_cast<float>(code), d);
+}
+
 __device__ __forceinline__ int clamp_i(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
 __device__ __forceinline__ float clamp_f(float v, float lo, float hi) { return v < lo ? lo : (hi < v ? hi : v); }
 __device__ __forceinline__ double clamp_d(double v, double lo, double hi) { return v < lo ? lo : (hi < v ? hi : v); }
@@ -227,7 +237,7 @@ __global__ void dequantize_kernel(const uint8_t* __restrict__ in, float* __restr
       int code;
       if constexpr (QT == 4) code = (j < 16 ? (blk[2 + j] & 0x0F) : (blk[2 + j - 16] >> 4)) - 8;
       else code = static_cast<int8_t>(blk[2 + j]);
-      v[k] = __fmul_rn(static_cast<float>(code), d);
+      v[k] = dequant_mul(code, d);
     }
     float* o = out + b * 32 + 4 * q;
     if (o_vec) {
@@ -279,7 +289,7 @@ __global__ void row_f32_kernel(int qtype, const uint8_t* __restrict__ W, uint64_
       const float d = fp16_to_f32(blk[0] | (blk[1] << 8));
       const int code = qtype == 4 ? (j < 16 ? (blk[2 + j] & 0x0F) : (blk[2 + j - 16] >> 4)) - 8
                                   : static_cast<int8_t>(blk[2 + j]);
-      v = __fmul_rn(static_cast<float>(code), d);
+      v = dequant_mul(code, d);
     } else if (qtype == 0) {
       v = __uint_as_float(row[4 * i] | (row[4 * i + 1] << 8) | (row[4 * i + 2] << 16) |
                           (static_cast<uint32_t>(row[4 * i + 3]) << 24));
