@@ -253,7 +253,9 @@ def run_ours(args):
     x_h[:] = x.cpu().numpy()
     Wh = Ws[0].cpu().numpy()
     Whs = [Wh.copy() for _ in range(N_COPIES)]
-    for i in range(N_COPIES + args.warmup):  # first calls upload each copy once
+    for w in Whs:  # like a model load: each weight copy is registered (uploaded) once
+        efg.host_register_weights(w)
+    for i in range(args.warmup):
         efg.host_matvec(Q8_0, Whs[i % N_COPIES], x_h, ROWS, y=y_h)
     barrier()
     e2e_steps = max(args.steps, 1)
@@ -274,7 +276,7 @@ def run_ours(args):
     q4_copies = 64  # 64 x 6.5 MB = 415 MB in rotation
     W4 = make_weights(efg, torch, Q4_0, q4_rows, q4_cols, q4_copies, seed=3)
     y4 = torch.empty(q4_rows, device="cuda")
-    k4 = 6400
+    k4 = 1280  # kept well below the headline's launch count so the Q8_0 kernel dominates
     g4, _, c4 = time_steps(efg, torch, Q4_0, W4, x, y4, q4_rows, q4_cols, k4, 64, chunk=640)
     torch.cuda.synchronize()
     s4, e4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -287,6 +289,7 @@ def run_ours(args):
     gbs4 = algo_bytes(Q4_0, q4_rows, q4_cols) / (ms4 / 1e3) / 1e9
     del W4
 
+    # DRAM bytes per launch of this kernel from the committed ncu capture summary
     traffic = None
     tpath = ROOT / "profiles" / "matvec_q8_0_32000x2048.json"
     if tpath.exists():
@@ -313,7 +316,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * COLS,
                     "d2h_bytes_per_step": 4 * ROWS,
-                    "api": "efg_host_matvec (host pointers; W resident after first upload)"},
+                    "api": "efg_host_matvec (host pointers; W registered resident once, like a model load)"},
             "gpu_launches": args.steps,
             "clocks": clocks.summary(),
             "extra": {"config0_q4_0_matvec_5632x2048": {

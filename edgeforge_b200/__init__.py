@@ -16,6 +16,8 @@ from .api import (  # noqa: F401
     host_dequantize_row,
     host_matvec,
     host_quantize_row,
+    host_register_weights,
+    host_unregister_weights,
     host_release_weights,
     matvec,
     matvec_jobs,

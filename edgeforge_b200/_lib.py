@@ -52,6 +52,8 @@ SIGNATURES = {
     "efg_host_matvec": (_i, [_i, _vp, _vp, _vp, _sz, _sz]),
     "efg_host_quantize_row": (_i, [_i, _vp, _sz, _vp, _i]),
     "efg_host_dequantize_row": (_i, [_i, _vp, _sz, _vp]),
+    "efg_host_register_weights": (_i, [_vp, _sz]),
+    "efg_host_unregister_weights": (_i, [_vp]),
     "efg_host_release_weights": (_i, []),
 }
 

@@ -146,8 +146,21 @@ def _np(a, dtype):
     return a, C.c_void_p(a.ctypes.data)
 
 
+def host_register_weights(W: np.ndarray) -> None:
+    """Uploads W once and keeps it resident; later host calls on views inside W use the
+    device copy. W must not change while registered (efg_host_register_weights)."""
+    if not W.flags["C_CONTIGUOUS"]:
+        raise EdgeForgeError(1, "register_weights needs a contiguous array")
+    check(load().efg_host_register_weights(C.c_void_p(W.ctypes.data), W.nbytes))
+
+
+def host_unregister_weights(W: np.ndarray) -> None:
+    check(load().efg_host_unregister_weights(C.c_void_p(W.ctypes.data)))
+
+
 def host_matvec(qtype: int, W: np.ndarray, x: np.ndarray, rows: int, y: np.ndarray | None = None) -> np.ndarray:
-    """Synchronous host-pointer matvec; W stays resident on the device between calls."""
+    """Synchronous host-pointer matvec (W read from a registered resident copy when it
+    lies inside one, else uploaded for this call)."""
     W, pw = _np(W, np.uint8)
     x, px = _np(x, np.float32)
     if y is None:

@@ -62,9 +62,22 @@ struct HostCtx {
   size_t in_cap = 0;
   void* out = nullptr;
   size_t out_cap = 0;
-  // (host pointer, bytes, type) -> resident device copy of a weight matrix
-  std::map<std::tuple<const void*, size_t, int>, void*> weights;
+  void* wtmp = nullptr;  // per-call upload of an unregistered W
+  size_t wtmp_cap = 0;
+  // registered host ranges: start -> (bytes, device copy)
+  std::map<const uint8_t*, std::pair<size_t, void*>> ranges;
 };
+
+// Device address of [p, p + n) if it lies inside a registered range, else nullptr.
+const uint8_t* resident(const HostCtx* h, const uint8_t* p, size_t n) {
+  auto it = h->ranges.upper_bound(p);
+  if (it == h->ranges.begin()) return nullptr;
+  --it;
+  const uint8_t* base = it->first;
+  const size_t len = it->second.first;
+  if (p < base || static_cast<size_t>(p - base) > len || n > len - static_cast<size_t>(p - base)) return nullptr;
+  return static_cast<const uint8_t*>(it->second.second) + (p - base);
+}
 
 HostCtx g_host[64];
 
@@ -233,15 +246,11 @@ int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_
   std::lock_guard<std::mutex> lk(h->mu);
   if ((st = host_stream(h))) return st;
   const size_t wbytes = rows * (cols / 32) * (qtype == EFG_Q4_0 ? 18 : 34);
-  const auto key = std::make_tuple(static_cast<const void*>(W), wbytes, qtype);
-  auto it = h->weights.find(key);
-  void* dW = nullptr;
-  if (it == h->weights.end()) {
-    EFG_TRY_CUDA(cudaMalloc(&dW, wbytes ? wbytes : 16), "resident weight allocation");
-    if (wbytes) EFG_TRY_CUDA(cudaMemcpyAsync(dW, W, wbytes, cudaMemcpyHostToDevice, h->stream), "weight upload");
-    h->weights.emplace(key, dW);
-  } else {
-    dW = it->second;
+  const void* dW = resident(h, W, wbytes);
+  if (!dW) {
+    if ((st = ensure(h->wtmp, h->wtmp_cap, wbytes + 16))) return st;
+    if (wbytes) EFG_TRY_CUDA(cudaMemcpyAsync(h->wtmp, W, wbytes, cudaMemcpyHostToDevice, h->stream), "weight upload");
+    dW = h->wtmp;
   }
   if ((st = ensure(h->in, h->in_cap, cols * sizeof(float) + 16))) return st;
   if ((st = ensure(h->out, h->out_cap, rows * sizeof(float) + 16))) return st;
@@ -294,14 +303,56 @@ int efg_host_dequantize_row(int qtype, const void* in, size_t n, float* out) {
   return EFG_OK;
 }
 
+int efg_host_register_weights(const void* host, size_t bytes) {
+  if (!host || bytes == 0) return fail(EFG_EINVAL, "register_weights: empty range");
+  int st;
+  HostCtx* h = host_ctx(st);
+  if (!h) return st;
+  std::lock_guard<std::mutex> lk(h->mu);
+  if ((st = host_stream(h))) return st;
+  const auto* p = static_cast<const uint8_t*>(host);
+  auto it = h->ranges.find(p);
+  if (it != h->ranges.end() && it->second.first != bytes) {
+    EFG_TRY_CUDA(cudaStreamSynchronize(h->stream), "stream synchronize");
+    cudaFree(it->second.second);
+    h->ranges.erase(it);
+    it = h->ranges.end();
+  }
+  if (it == h->ranges.end()) {
+    for (const auto& kv : h->ranges) {  // overlapping ranges would make lookups ambiguous
+      if (p < kv.first + kv.second.first && kv.first < p + bytes)
+        return fail(EFG_EINVAL, "register_weights: range overlaps a registered range");
+    }
+    void* d = nullptr;
+    EFG_TRY_CUDA(cudaMalloc(&d, bytes), "resident weight allocation");
+    it = h->ranges.emplace(p, std::make_pair(bytes, d)).first;
+  }
+  EFG_TRY_CUDA(cudaMemcpyAsync(it->second.second, host, bytes, cudaMemcpyHostToDevice, h->stream), "weight upload");
+  EFG_TRY_CUDA(cudaStreamSynchronize(h->stream), "stream synchronize");
+  return EFG_OK;
+}
+
+int efg_host_unregister_weights(const void* host) {
+  int st;
+  HostCtx* h = host_ctx(st);
+  if (!h) return st;
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto it = h->ranges.find(static_cast<const uint8_t*>(host));
+  if (it == h->ranges.end()) return fail(EFG_EINVAL, "unregister_weights: range not registered");
+  if (h->stream) EFG_TRY_CUDA(cudaStreamSynchronize(h->stream), "stream synchronize");
+  cudaFree(it->second.second);
+  h->ranges.erase(it);
+  return EFG_OK;
+}
+
 int efg_host_release_weights(void) {
   int st;
   HostCtx* h = host_ctx(st);
   if (!h) return st;
   std::lock_guard<std::mutex> lk(h->mu);
   if (h->stream) EFG_TRY_CUDA(cudaStreamSynchronize(h->stream), "stream synchronize");
-  for (auto& kv : h->weights) cudaFree(kv.second);
-  h->weights.clear();
+  for (auto& kv : h->ranges) cudaFree(kv.second.second);
+  h->ranges.clear();
   return EFG_OK;
 }
 

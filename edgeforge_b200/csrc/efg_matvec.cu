@@ -128,57 +128,75 @@ constexpr int slot_words() {
   return F == Fmt::Q4 ? 9 : 17;
 }
 
-// Dot of one slot (64 columns, two blocks) with the lane's x registers.
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
   return v;
 }
 
-// saddr: shared-memory address of the slot's first word.
-template <Fmt F>
-__device__ __forceinline__ float slot_dot(uint32_t saddr, const float2 (&xp)[32]) {
-  uint32_t w[slot_words<F>()];
-#pragma unroll
-  for (int i = 0; i < slot_words<F>(); ++i) w[i] = lds32(saddr + 4u * i);
-  const float2 z = f2(0.f, 0.f);
-  float2 a0 = z, b0 = z, a1 = z, b1 = z;
-  float d0, d1;
+// Word K of a slot (compile-time) for one row: which x pairs it multiplies and which
+// block accumulators it feeds. Q4_0 slot: word 0 = d_b, codes 0-1 | words 1-3 = codes
+// 2-13 | word 4 = codes 14-15, d_b+1 | words 5-8 = the 16 code bytes of block b+1.
+// Q8_0 slot: word 0 = d_b, codes 0-1 | words 1-7 = codes 2-29 | word 8 = codes 30-31,
+// d_b+1 | words 9-16 = the 32 codes of block b+1.
+template <Fmt F, int K>
+__device__ __forceinline__ void slot_word(uint32_t w, const float2 (&xp)[32], float2& a0, float2& b0, float2& a1,
+                                          float2& b1) {
   if constexpr (F == Fmt::Q4) {
-    // word 0: d_b, codes 0-1 | words 1-3: codes 2-13 | word 4: codes 14-15, d_b+1 |
-    // words 5-8: the 16 code bytes of block b+1.
-    d0 = half_bits_to_float(w[0] & 0xFFFFu);
-    d1 = half_bits_to_float(w[4] >> 16);
-    q4_half(w[0] >> 16, xp[0], xp[1], a0, b0);
-    q4_word(w[1], xp[2], xp[3], xp[4], xp[5], a0, b0);
-    q4_word(w[2], xp[6], xp[7], xp[8], xp[9], a0, b0);
-    q4_word(w[3], xp[10], xp[11], xp[12], xp[13], a0, b0);
-    q4_half(w[4], xp[14], xp[15], a0, b0);
-    q4_word(w[5], xp[16], xp[17], xp[18], xp[19], a1, b1);
-    q4_word(w[6], xp[20], xp[21], xp[22], xp[23], a1, b1);
-    q4_word(w[7], xp[24], xp[25], xp[26], xp[27], a1, b1);
-    q4_word(w[8], xp[28], xp[29], xp[30], xp[31], a1, b1);
+    if constexpr (K == 0) q4_half(w >> 16, xp[0], xp[1], a0, b0);
+    else if constexpr (K <= 3) q4_word(w, xp[4 * K - 2], xp[4 * K - 1], xp[4 * K], xp[4 * K + 1], a0, b0);
+    else if constexpr (K == 4) q4_half(w, xp[14], xp[15], a0, b0);
+    else q4_word(w, xp[16 + 4 * (K - 5)], xp[17 + 4 * (K - 5)], xp[18 + 4 * (K - 5)], xp[19 + 4 * (K - 5)], a1, b1);
   } else {
-    // word 0: d_b, codes 0-1 | words 1-7: codes 2-29 | word 8: codes 30-31, d_b+1 |
-    // words 9-16: the 32 codes of block b+1.
-    d0 = half_bits_to_float(w[0] & 0xFFFFu);
-    d1 = half_bits_to_float(w[8] >> 16);
-    q8_half(w[0] >> 16, xp[0], a0);
-#pragma unroll
-    for (int k = 1; k < 8; ++k) {
-      q8_half(w[k], xp[2 * k - 1], b0);
-      q8_half(w[k] >> 16, xp[2 * k], a0);
-    }
-    q8_half(w[8], xp[15], b0);
-#pragma unroll
-    for (int k = 9; k < 17; ++k) {
-      q8_half(w[k], xp[16 + 2 * (k - 9)], a1);
-      q8_half(w[k] >> 16, xp[17 + 2 * (k - 9)], b1);
+    if constexpr (K == 0) {
+      q8_half(w >> 16, xp[0], a0);
+    } else if constexpr (K <= 7) {
+      q8_half(w, xp[2 * K - 1], b0);
+      q8_half(w >> 16, xp[2 * K], a0);
+    } else if constexpr (K == 8) {
+      q8_half(w, xp[15], b0);
+    } else {
+      q8_half(w, xp[16 + 2 * (K - 9)], a1);
+      q8_half(w >> 16, xp[17 + 2 * (K - 9)], b1);
     }
   }
-  const float s0 = (a0.x + a0.y) + (b0.x + b0.y);
-  const float s1 = (a1.x + a1.y) + (b1.x + b1.y);
-  return d0 * s0 + d1 * s1;
+}
+
+template <Fmt F, int RB, int K>
+__device__ __forceinline__ void rows_word(const uint32_t (&w)[RB][slot_words<F>()], const float2 (&xp)[32],
+                                          float2 (&a0)[RB], float2 (&b0)[RB], float2 (&a1)[RB], float2 (&b1)[RB]) {
+  if constexpr (K < slot_words<F>()) {
+#pragma unroll
+    for (int r = 0; r < RB; ++r) slot_word<F, K>(w[r][K], xp, a0[r], b0[r], a1[r], b1[r]);
+    rows_word<F, RB, K + 1>(w, xp, a0, b0, a1, b1);
+  }
+}
+
+// Dots of RB rows' slots (64 columns, two blocks each) with the lane's x registers,
+// computed word by word across the rows so their independent FMA chains interleave.
+// addr[r]: shared-memory address of row r's slot; rows with valid[r] false give 0.
+template <Fmt F, int RB>
+__device__ __forceinline__ void slot_dots(const uint32_t (&addr)[RB], const bool (&valid)[RB], const float2 (&xp)[32],
+                                          float (&out)[RB]) {
+  constexpr int NW = slot_words<F>();
+  uint32_t w[RB][NW];
+#pragma unroll
+  for (int r = 0; r < RB; ++r)
+#pragma unroll
+    for (int i = 0; i < NW; ++i) w[r][i] = valid[r] ? lds32(addr[r] + 4u * i) : 0u;
+  const float2 z = f2(0.f, 0.f);
+  float2 a0[RB], b0[RB], a1[RB], b1[RB];
+#pragma unroll
+  for (int r = 0; r < RB; ++r) a0[r] = b0[r] = a1[r] = b1[r] = z;
+  rows_word<F, RB, 0>(w, xp, a0, b0, a1, b1);
+#pragma unroll
+  for (int r = 0; r < RB; ++r) {
+    const float d0 = half_bits_to_float(w[r][0] & 0xFFFFu);
+    const float d1 = half_bits_to_float(w[r][F == Fmt::Q4 ? 4 : 8] >> 16);
+    const float s0 = (a0[r].x + a0[r].y) + (b0[r].x + b0[r].y);
+    const float s1 = (a1[r].x + a1[r].y) + (b1[r].x + b1[r].y);
+    out[r] = valid[r] ? d0 * s0 + d1 * s1 : 0.f;
+  }
 }
 
 __device__ __forceinline__ void named_barrier(int id, int threads) {
@@ -210,7 +228,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.NS * p.stage_bytes);
   uint64_t* empty = full + p.NS;
-  float* red = reinterpret_cast<float*>(empty + p.NS);                               // [RG*H][2][RB][G]
+  uint64_t* xready = empty + p.NS;                                                   // x staged
+  float* red = reinterpret_cast<float*>(xready + 1);                                 // [RG*H][2][RB][G]
   double* norm_red = reinterpret_cast<double*>(red + 2 * p.RG * p.H * RB * p.G + 2);  // [16]
   float* xs = reinterpret_cast<float*>(norm_red + 16);                          // [S][65]
   constexpr int n_mat = E == Epi::SwiGLU ? 2 : 1;
@@ -222,6 +241,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], p.G * p.H);
     }
+    mbar_init(xready, 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -234,9 +254,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
     if (lane != 0) return;
     const uint64_t pol = l2_evict_first_policy();
     const uint32_t rb = p.rb_words * 4u;
+    // Weight tiles requested for this SM return in order, so a deep prefetch would hold
+    // back the consumers' read of x by microseconds. Prefetch ~32 KB (it lands while the
+    // previous kernel finishes), then wait until x is staged before filling the ring.
+    const uint32_t prefetch = std::max(1u, std::min(p.NS, (32768u + p.stage_bytes - 1) / p.stage_bytes));
     uint32_t k = 0, s = 0, round = 0;
     bool ok = true;
     for (uint32_t tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++k) {
+      if (k == prefetch && !mbar_wait(xready, 0, p.err)) {
+        ok = false;
+        break;
+      }
       if (round > 0 && !mbar_wait(&empty[s], (round - 1) & 1u, p.err)) {
         ok = false;
         break;
@@ -304,6 +332,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
     }
   }
   named_barrier(kNormBarrier, nc * 32);
+  if (threadIdx.x == 0) mbar_arrive(xready);  // the producer may now fill the whole ring
   float2 xp[32];
 #pragma unroll
   for (int k = 0; k < 32; ++k) {
@@ -333,12 +362,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
     float* y = p.jobs[j].y + (p.pos ? *p.pos * p.jobs[j].y_pos_stride : 0);
     for (uint32_t b = 0; b < p.BPS; ++b) {
       float acc[RB];
+      uint32_t addr[RB];
+      bool valid[RB];
 #pragma unroll
       for (int i = 0; i < static_cast<int>(RB); ++i) {
         const uint32_t lr = b * batch_rows + h * RBH + i % RBH;  // row within the tile, per matrix
         const uint32_t srow = (E == Epi::SwiGLU && i >= static_cast<int>(RBH)) ? lr + p.TR : lr;
-        acc[i] = (active && lr < nrows) ? slot_dot<F>(sbase + srow * row_bytes, xp) : 0.f;
+        addr[i] = sbase + srow * row_bytes;
+        valid[i] = active && lr < nrows;
       }
+      slot_dots<F, static_cast<int>(RB)>(addr, valid, xp, acc);
       if (b + 1 == p.BPS) {
         __syncwarp();
         if (alive && lane == 0) mbar_arrive(&empty[s]);  // all reads of this stage are done
@@ -516,7 +549,7 @@ Plan plan_fast(const MatvecArgs& a, const DeviceInfo& dev) {
         const uint32_t TR = bps * H * rbh;
         if ((static_cast<uint64_t>(TR) * rb) % 16 != 0) continue;
         const uint64_t stage = (static_cast<uint64_t>(TR) * rb * n_mat + 15) / 16 * 16;
-        const size_t tail = 2 * 8 * kMaxStages + (2 * RG * H * rbv * G + 2) * 4 + 16 * 8 + xs_bytes + 128;
+        const size_t tail = 2 * 8 * kMaxStages + 8 + (2 * RG * H * rbv * G + 2) * 4 + 16 * 8 + xs_bytes + 128;
         const size_t budget = std::min(kSmemBudget, dev.smem_optin > tail ? dev.smem_optin - tail : 0);
         uint32_t NS = static_cast<uint32_t>(std::min<uint64_t>(kMaxStages, budget / stage));
         NS = NS / RG * RG;
@@ -541,7 +574,7 @@ Plan plan_fast(const MatvecArgs& a, const DeviceInfo& dev) {
           best.NS = NS;
           best.stage_bytes = static_cast<uint32_t>(stage);
           best.tiles = tiles;
-          best.smem = NS * stage + 2 * NS * 8 + (2 * RG * H * rbv * G + 2) * 4 + 16 * 8 + xs_bytes;
+          best.smem = NS * stage + 2 * NS * 8 + 8 + (2 * RG * H * rbv * G + 2) * 4 + 16 * 8 + xs_bytes;
           best.ok = true;
         }
       }

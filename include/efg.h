@@ -137,16 +137,22 @@ int efg_row_f32(float* d_out, int qtype, const uint8_t* d_W, size_t rows, size_t
                 size_t r_host, void* stream);
 
 /* ================================================================ host-pointer forms
- * Synchronous calls with the reference's exact arguments (host pointers). W is
- * uploaded once and kept resident on the device, keyed by (pointer, size, type): the
- * reference's W is a read-only view of a memory-mapped .efq (src/model.cpp:71-74), so
- * the same pointer always holds the same bytes. Call efg_host_release_weights() if
- * that is not true for the caller. x is copied in and y out on every call.
+ * Synchronous calls with the reference's exact arguments (host pointers). x is copied in
+ * and y out on every call. W is read from a resident device copy when it lies inside a
+ * range registered with efg_host_register_weights() (the reference passes read-only
+ * views of a memory-mapped .efq, src/model.cpp:71-74: register the file's data once at
+ * load); otherwise it is uploaded on every call, so a caller that rewrites its buffer
+ * between calls always gets results for the current bytes.
  */
 int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols);
 int efg_host_quantize_row(int qtype, const float* x, size_t n, void* out, int search);
 int efg_host_dequantize_row(int qtype, const void* in, size_t n, float* out);
-/* Drops every resident copy made by the host-pointer calls. */
+/* Uploads [host, host + bytes) once and keeps it on the device; the caller promises not to
+ * modify those bytes while registered. Registering a range again refreshes its copy. */
+int efg_host_register_weights(const void* host, size_t bytes);
+/* Drops the resident copy of the range starting at `host`. */
+int efg_host_unregister_weights(const void* host);
+/* Drops every resident copy. */
 int efg_host_release_weights(void);
 
 #ifdef __cplusplus

@@ -70,3 +70,15 @@ def test_reference_names_are_mirrored(efg_lib):
     for name in ("matvec_q4_0", "matvec_q8_0", "matvec", "matvec_jobs", "dot_q4_0", "dot_q8_0", "quantize_row",
                  "dequantize_row", "row_f32", "row_bytes"):
         assert callable(getattr(efg_lib, name))
+
+
+def test_reference_api_shim_compiles(efg_lib, tmp_path):
+    """include/efg_ref_shim.hpp gives the reference's C++ signatures; reference-style test
+    code (tests/shim/shim_test.cpp) compiles and links against it and libefg.so."""
+    import subprocess
+
+    exe = tmp_path / "shim_test"
+    r = subprocess.run(["g++", "-std=c++20", "-O1", "-Wall", "-Werror", "-I", str(ROOT / "include"),
+                        str(ROOT / "tests" / "shim" / "shim_test.cpp"), "-L", str(ROOT / "edgeforge_b200"), "-lefg",
+                        "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr

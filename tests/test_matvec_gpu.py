@@ -171,11 +171,44 @@ def test_config_shapes_quantized_gaussian(efg_lib, cuda, oracle, cfg):
     assert np.abs(y - yo).max() <= 1e-5 * np.abs(yo).max() * 10
 
 
-def test_host_pointer_matvec_keeps_weights_resident(efg_lib, cuda, oracle):
+def test_host_pointer_matvec_registered_and_fresh_weights(efg_lib, cuda, oracle):
+    """Registered weights stay resident (views inside the range included); an unregistered
+    buffer is read anew on every call, so rewriting it between calls is safe."""
     rng = np.random.default_rng(3)
     W = random_packed(Q8_0, 500, 2048, rng)
+    efg_lib.host_register_weights(W)
+    rb = row_bytes(Q8_0, 2048)
     for _ in range(3):
         x = rng.standard_normal(2048).astype(np.float32)
         y = efg_lib.host_matvec(Q8_0, W, x, 500)
         assert rel_dot_errors(oracle, Q8_0, W, x, 500, y).max() < TOL
+        sub = W[100:140]  # a view inside the registered range
+        ys = efg_lib.host_matvec(Q8_0, sub, x, 40)
+        assert np.array_equal(ys.view(np.uint32), y[100:140].view(np.uint32))
+    efg_lib.host_unregister_weights(W)
+    U = random_packed(Q4_0, 64, 256, rng)
+    x = rng.standard_normal(256).astype(np.float32)
+    y1 = efg_lib.host_matvec(Q4_0, U, x, 64)
+    U[:, 0:2] = 0  # zero every first-block scale in place
+    y2 = efg_lib.host_matvec(Q4_0, U, x, 64)
+    assert rel_dot_errors(oracle, Q4_0, U, x, 64, y2).max() < TOL
+    assert not np.array_equal(y1, y2)
     efg_lib.host_release_weights()
+    _ = rb
+
+
+def test_reference_cpp_cases_through_the_shim(efg_lib, cuda, tmp_path):
+    """Reference test cases written against the reference's C++ API (ef::kern::matvec_q4_0,
+    ef::quantize_row, ...) compile unchanged against include/efg_ref_shim.hpp and pass on
+    the GPU (tests/shim/shim_test.cpp)."""
+    import subprocess
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    exe = tmp_path / "shim_test"
+    subprocess.run(["g++", "-std=c++20", "-O2", "-I", str(root / "include"), str(root / "tests" / "shim" / "shim_test.cpp"),
+                    "-L", str(root / "edgeforge_b200"), "-lefg", f"-Wl,-rpath,{root / 'edgeforge_b200'}", "-o", str(exe)],
+                   check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "0 failures" in r.stdout
