@@ -6,6 +6,8 @@ include/efg.h); this package is the Python mirror of the reference's kernel API 
 from ._lib import EdgeForgeError, LIB_PATH, load  # noqa: F401
 from .api import (  # noqa: F401
     BLOCK_BYTES,
+    Decoder,
+    GreedyResult,
     QK,
     QType,
     dequantize_row,
@@ -13,6 +15,7 @@ from .api import (  # noqa: F401
     device_error,
     dot_q4_0,
     dot_q8_0,
+    efq_check,
     host_dequantize_row,
     host_matvec,
     host_quantize_row,

@@ -30,6 +30,13 @@ class MatvecJob(C.Structure):
     _fields_ = [("d_y", _vp), ("qtype", _i), ("d_W", _vp), ("rows", _sz), ("cols", _sz), ("d_x", _vp)]
 
 
+class ModelInfo(C.Structure):
+    """efg_model_info (include/efg.h)."""
+
+    _fields_ = [(n, C.c_int32) for n in ("hidden", "intermediate", "layers", "heads", "kv_heads", "head_dim", "vocab",
+                                          "max_seq", "n_q4", "n_q8", "embed_type")] + [("bytes_per_token", C.c_uint64)]
+
+
 # name -> (restype, argtypes); every symbol include/efg.h declares.
 SIGNATURES = {
     "efg_abi_version": (_i, []),
@@ -55,6 +62,14 @@ SIGNATURES = {
     "efg_host_register_weights": (_i, [_vp, _sz]),
     "efg_host_unregister_weights": (_i, [_vp]),
     "efg_host_release_weights": (_i, []),
+    "efg_efq_check": (_i, [_vp, _u64]),
+    "efg_decoder_open": (_i, [C.c_char_p, _sz, C.POINTER(_vp)]),
+    "efg_decoder_close": (_i, [_vp]),
+    "efg_decoder_info": (_i, [_vp, C.POINTER(ModelInfo)]),
+    "efg_decoder_reset": (_i, [_vp]),
+    "efg_decoder_forward": (_i, [_vp, C.c_int32, _sz, _vp]),
+    "efg_decoder_generate": (_i, [_vp, _vp, _sz, _sz, C.c_int32, _vp, _vp, C.POINTER(_sz), _vp,
+                                  C.POINTER(C.c_double), C.POINTER(C.c_double)]),
 }
 
 _lib = None

@@ -17,7 +17,7 @@ from enum import IntEnum
 
 import numpy as np
 
-from ._lib import EdgeForgeError, MatvecJob, check, load
+from ._lib import EdgeForgeError, MatvecJob, ModelInfo, check, load
 
 
 class QType(IntEnum):
@@ -185,3 +185,96 @@ def host_dequantize_row(qtype: int, data: np.ndarray, n: int) -> np.ndarray:
 
 def host_release_weights() -> None:
     check(load().efg_host_release_weights())
+
+
+# ---------------------------------------------------------------- .efq and the decode step
+
+
+def efq_check(data: bytes | np.ndarray) -> None:
+    """Validates an .efq file image (ef::parse_efq, src/qfile.cpp:125-223); raises
+    EdgeForgeError carrying the reference's message on a malformed file."""
+    buf = np.frombuffer(data, dtype=np.uint8) if isinstance(data, (bytes, bytearray)) else np.ascontiguousarray(data)
+    check(load().efg_efq_check(C.c_void_p(buf.ctypes.data if buf.size else 0), buf.size))
+
+
+class GreedyResult:
+    """ef::GreedyResult (include/ef/model.h:117-123)."""
+
+    def __init__(self, tokens, step_logits, prefill_seconds, decode_seconds):
+        self.tokens = tokens
+        self.step_logits = step_logits
+        self.prefill_seconds = prefill_seconds
+        self.decode_seconds = decode_seconds
+        self.decode_forwards = max(len(tokens) - 1, 0)
+
+
+class Decoder:
+    """ef::Model::load_efq + ef::Transformer (src/model.cpp:66-111, 153-276) on the GPU:
+    the .efq's tensors are uploaded once, the KV cache is FP32 on the device, and one
+    decode step is a recorded CUDA graph."""
+
+    def __init__(self, efq_path, max_seq: int):
+        h = C.c_void_p(0)
+        check(load().efg_decoder_open(str(efq_path).encode(), int(max_seq), C.byref(h)))
+        self._h = h
+        info = ModelInfo()
+        check(load().efg_decoder_info(h, C.byref(info)))
+        self.info = info
+        self.vocab = info.vocab
+        self.max_seq = info.max_seq
+
+    def close(self) -> None:
+        if self._h:
+            load().efg_decoder_close(self._h)
+            self._h = C.c_void_p(0)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def bytes_per_token(self) -> int:
+        """ef::Model::weight_bytes_per_token (src/qfile.cpp:237-241)."""
+        return int(self.info.bytes_per_token)
+
+    def reset(self) -> None:
+        check(load().efg_decoder_reset(self._h))
+
+    def forward(self, token: int, pos: int, compute_logits: bool = True) -> np.ndarray | None:
+        """ef::Transformer::forward: logits (vocab floats) or None."""
+        out = np.empty(self.vocab, np.float32) if compute_logits else None
+        check(load().efg_decoder_forward(self._h, int(token), int(pos),
+                                         C.c_void_p(out.ctypes.data) if out is not None else None))
+        return out
+
+    def generate(self, prompt, max_new: int, eos_id: int = -1, forced=None,
+                 keep_step_logits: bool = False) -> GreedyResult:
+        """ef::generate_greedy (src/model.cpp:278-304). `forced` (max_new ids) teacher-forces
+        the decode steps; the returned tokens are still each step's argmax."""
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        toks = np.zeros(max(max_new, 1), np.int32)
+        n = C.c_size_t(0)
+        pf = C.c_double(0)
+        dc = C.c_double(0)
+        f = None
+        if forced is not None:
+            f = np.ascontiguousarray(forced, np.int32)
+            if f.size != max_new:
+                raise EdgeForgeError(1, "forced needs max_new ids")
+        logits = np.zeros((max(max_new - 1, 0), self.vocab), np.float32) if keep_step_logits else None
+        check(load().efg_decoder_generate(
+            self._h, C.c_void_p(prompt.ctypes.data), prompt.size, int(max_new), int(eos_id),
+            C.c_void_p(f.ctypes.data) if f is not None else None, C.c_void_p(toks.ctypes.data), C.byref(n),
+            C.c_void_p(logits.ctypes.data) if logits is not None and logits.size else None,
+            C.byref(pf), C.byref(dc)))
+        k = n.value
+        steps = logits[: max(k - 1, 0)] if logits is not None else None
+        return GreedyResult(toks[:k].tolist(), steps, pf.value, dc.value)

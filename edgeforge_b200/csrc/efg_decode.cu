@@ -1,0 +1,761 @@
+// efg_decode.cu - the TinyLlama decode step of the reference (src/model.cpp:184-304) on a
+// B200: Model::load_efq, Transformer::forward and generate_greedy.
+//
+// The .efq data region is uploaded once; every weight is a device pointer into it. One
+// decode step is a fixed sequence of launches that reads the position and the token from
+// device memory, so it is captured once into a CUDA graph and replayed for every token:
+//
+//   embed (BF16 row of tokens[pos])
+//   per layer: q/k/v matvec with the RMSNorm prologue (v written straight into the KV
+//              cache at pos) -> attention (RoPE of q and the new k, k-cache write, GQA
+//              softmax over pos+1 positions) -> o_proj matvec with residual add ->
+//              gate/up matvec with the RMSNorm prologue and SwiGLU epilogue -> down matvec
+//              with residual add
+//   lm_head matvec with the final RMSNorm prologue -> argmax (next token, pos + 1)
+//
+// All launches use programmatic dependent launch: the matvecs start streaming their
+// weights while the previous kernel finishes, and wait for it before touching
+// activations. Norm, residual and SwiGLU follow the reference's float operation order
+// (src/kernels.cpp:69-111); matvec sums differ in order only (<= 1e-5 of sum|w x|).
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/efg.h"
+#include "efg_device.cuh"
+#include "efg_efq.h"
+#include "efg_host.h"
+#include "efg_matvec.cuh"
+
+namespace efg {
+namespace {
+
+constexpr int kAttnThreads = 128;
+
+cudaLaunchConfig_t cfg_of(dim3 grid, dim3 block, size_t smem, cudaStream_t s, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t c{};
+  c.gridDim = grid;
+  c.blockDim = block;
+  c.dynamicSmemBytes = smem;
+  c.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  c.attrs = attr;
+  c.numAttrs = 1;
+  return c;
+}
+
+// x = row tokens[*pos] of the embedding table (src/qkernels.cpp:299-305).
+__global__ void embed_kernel(const uint8_t* __restrict__ table, int type, uint32_t vocab, uint32_t dim,
+                             const int32_t* __restrict__ tokens, const int32_t* __restrict__ pos,
+                             float* __restrict__ x, int* err) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int32_t tok = tokens[*pos];
+  if (tok < 0 || static_cast<uint32_t>(tok) >= vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) record_error(err, EFG_EINVAL);
+    return;
+  }
+  const uint64_t rb = type == 0 ? 4ull * dim : type <= 2 ? 2ull * dim : dim / 32ull * (type == 3 ? 34 : 18);
+  const uint8_t* row = table + static_cast<uint64_t>(tok) * rb;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
+    float v;
+    if (type == 2) {
+      v = bf16_to_f32(row[2 * i] | (row[2 * i + 1] << 8));
+    } else if (type == 1) {
+      v = fp16_to_f32(row[2 * i] | (row[2 * i + 1] << 8));
+    } else if (type == 0) {
+      v = __uint_as_float(row[4 * i] | (row[4 * i + 1] << 8) | (row[4 * i + 2] << 16) |
+                          (static_cast<uint32_t>(row[4 * i + 3]) << 24));
+    } else {
+      const uint8_t* blk = row + (i / 32) * (type == 3 ? 34 : 18);
+      const int j = i % 32;
+      const float d = fp16_to_f32(blk[0] | (blk[1] << 8));
+      const int code = type == 4 ? (j < 16 ? (blk[2 + j] & 15) : (blk[2 + j - 16] >> 4)) - 8
+                                 : static_cast<int8_t>(blk[2 + j]);
+      v = __fmul_rn(static_cast<float>(code), d);
+    }
+    x[i] = v;
+  }
+}
+
+// One query head per CTA (src/kernels.cpp:133-174): RoPE of q and of the new key (half-split
+// rotation, HF order a*c - b*s, b*c + a*s), the key written to the cache at pos by the first
+// head of each KV group, scores scaled by 1/sqrt(hd), softmax with a double sum, then the
+// probability-weighted sum of the cached values in position order.
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(
+    const float* __restrict__ q, const float* __restrict__ knew, float* __restrict__ k_layer,
+    const float* __restrict__ v_layer, float* __restrict__ ctx, const float* __restrict__ rope_cos,
+    const float* __restrict__ rope_sin, const int32_t* __restrict__ pos_p, int H, int KV, int hd, int max_seq,
+    int* err) {
+  extern __shared__ float sm[];
+  float* qh = sm;            // [hd]
+  float* kn = qh + hd;       // [hd]
+  float* sc = kn + hd;       // [max_seq]
+  __shared__ float red_f[kAttnThreads / 32];
+  __shared__ double red_d[kAttnThreads / 32];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pos = *pos_p;
+  if (pos < 0 || pos >= max_seq) {
+    if (threadIdx.x == 0) record_error(err, EFG_ESTATE);
+    return;
+  }
+  const int h = blockIdx.x, group = H / KV, kv = h / group, half = hd / 2, kvd = KV * hd;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const float* c = rope_cos + static_cast<size_t>(pos) * half;
+  const float* s = rope_sin + static_cast<size_t>(pos) * half;
+  for (int i = tid; i < half; i += blockDim.x) {
+    const float a = q[h * hd + i], b = q[h * hd + i + half];
+    qh[i] = __fsub_rn(__fmul_rn(a, c[i]), __fmul_rn(b, s[i]));
+    qh[i + half] = __fadd_rn(__fmul_rn(b, c[i]), __fmul_rn(a, s[i]));
+    const float ka = knew[kv * hd + i], kb = knew[kv * hd + i + half];
+    kn[i] = __fsub_rn(__fmul_rn(ka, c[i]), __fmul_rn(kb, s[i]));
+    kn[i + half] = __fadd_rn(__fmul_rn(kb, c[i]), __fmul_rn(ka, s[i]));
+  }
+  __syncthreads();
+  if (h % group == 0)
+    for (int i = tid; i < hd; i += blockDim.x) k_layer[static_cast<size_t>(pos) * kvd + kv * hd + i] = kn[i];
+  const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));
+  const int n_pos = pos + 1;
+  float mx = -INFINITY;
+  for (int t = tid; t < n_pos; t += blockDim.x) {
+    const float* kt = t == pos ? kn : k_layer + static_cast<size_t>(t) * kvd + kv * hd;
+    // dot with 8 partial sums combined pairwise (src/kernels.cpp:28-43)
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int i = 0;
+    for (; i + 8 <= hd; i += 8)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[k] = __fadd_rn(a[k], __fmul_rn(qh[i + k], kt[i + k]));
+    for (; i < hd; ++i) a[0] = __fadd_rn(a[0], __fmul_rn(qh[i], kt[i]));
+    const float dot = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
+                                __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
+    sc[t] = __fmul_rn(dot, scale);
+    mx = fmaxf(mx, sc[t]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+  if (lane == 0) red_f[wid] = mx;
+  __syncthreads();
+  mx = red_f[0];
+  for (int w = 1; w < static_cast<int>(blockDim.x / 32); ++w) mx = fmaxf(mx, red_f[w]);
+  // softmax (src/kernels.cpp:77-92): exp(x - max), sum in double, scale by float(1/sum)
+  double sum = 0.0;
+  for (int t = tid; t < n_pos; t += blockDim.x) {
+    const float e = expf(__fsub_rn(sc[t], mx));
+    sc[t] = e;
+    sum += static_cast<double>(e);
+  }
+  sum = warp_sum_d(sum);
+  if (lane == 0) red_d[wid] = sum;
+  __syncthreads();
+  double tot = 0.0;
+  for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) tot += red_d[w];
+  const float inv = static_cast<float>(1.0 / tot);
+  for (int t = tid; t < n_pos; t += blockDim.x) sc[t] = __fmul_rn(sc[t], inv);
+  __syncthreads();
+  for (int d = tid; d < hd; d += blockDim.x) {
+    float acc = 0.f;
+    for (int t = 0; t < n_pos; ++t)
+      acc = __fadd_rn(acc, __fmul_rn(sc[t], v_layer[static_cast<size_t>(t) * kvd + kv * hd + d]));
+    ctx[h * hd + d] = acc;
+  }
+}
+
+// out = silu(gate) * up (src/kernels.cpp:94-99), for the unfused path.
+__global__ void swiglu_kernel(float* __restrict__ out, const float* __restrict__ g, const float* __restrict__ u,
+                              uint32_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const float gv = g[i];
+    out[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), u[i]);
+  }
+}
+
+// h = w * (x * inv) with inv = float(1 / sqrt(mean(x^2) + eps)) (src/kernels.cpp:69-75), for
+// the unfused path; one CTA.
+__global__ void rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ x, const float* __restrict__ w,
+                               uint32_t n, float eps) {
+  __shared__ double red[32];
+  pdl_wait();
+  pdl_launch_dependents();
+  double ss = 0.0;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss += static_cast<double>(x[i]) * static_cast<double>(x[i]);
+  ss = warp_sum_d(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  double tot = 0.0;
+  for (uint32_t k = 0; k < blockDim.x / 32; ++k) tot += red[k];
+  const float inv = static_cast<float>(1.0 / sqrt((n ? tot / n : 0.0) + static_cast<double>(eps)));
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) h[i] = __fmul_rn(w[i], __fmul_rn(x[i], inv));
+}
+
+// Index of the first maximum of logits (src/kernels.cpp:105-111); records it, makes it the
+// next token unless that token is given, and advances the position.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, uint32_t n,
+                                                      int32_t* __restrict__ tokens, int32_t* __restrict__ out_tokens,
+                                                      int32_t* __restrict__ pos_p, const int32_t* __restrict__ n_fixed,
+                                                      int max_seq) {
+  __shared__ float bv[32];
+  __shared__ uint32_t bi[32];
+  pdl_wait();
+  pdl_launch_dependents();
+  float best = -INFINITY;
+  uint32_t idx = 0xFFFFFFFFu;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = logits[i];
+    if (v > best || (idx == 0xFFFFFFFFu && !(v != v))) {  // first non-NaN candidate, then strictly greater
+      if (idx == 0xFFFFFFFFu || v > best) {
+        best = v;
+        idx = i;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+    const uint32_t oi = __shfl_xor_sync(0xFFFFFFFFu, idx, o);
+    if (oi != 0xFFFFFFFFu && (idx == 0xFFFFFFFFu || ov > best || (ov == best && oi < idx))) {
+      best = ov;
+      idx = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    bv[threadIdx.x >> 5] = best;
+    bi[threadIdx.x >> 5] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    best = bv[0];
+    idx = bi[0];
+    for (uint32_t w = 1; w < blockDim.x / 32; ++w) {
+      if (bi[w] != 0xFFFFFFFFu && (idx == 0xFFFFFFFFu || bv[w] > best || (bv[w] == best && bi[w] < idx))) {
+        best = bv[w];
+        idx = bi[w];
+      }
+    }
+    // The reference starts from index 0 and takes strictly greater values, so a NaN at
+    // index 0 is never replaced (all comparisons with it are false).
+    const float first = logits[0];
+    if (first != first) idx = 0;
+    if (idx == 0xFFFFFFFFu) idx = 0;
+    const int32_t pos = *pos_p;
+    out_tokens[pos] = static_cast<int32_t>(idx);
+    if (pos + 1 < max_seq && pos + 1 >= *n_fixed) tokens[pos + 1] = static_cast<int32_t>(idx);
+    *pos_p = pos + 1;
+  }
+}
+
+// A prefill step without logits only advances the position.
+__global__ void advance_kernel(int32_t* pos_p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) *pos_p += 1;
+}
+
+struct Mat {
+  int type = 0;
+  const uint8_t* w = nullptr;
+  uint32_t rows = 0, cols = 0;
+};
+
+struct Layer {
+  Mat q, k, v, o, gate, up, down;
+  const float* attn_norm = nullptr;
+  const float* ffn_norm = nullptr;
+};
+
+}  // namespace
+
+struct Decoder {
+  efq::Layout L;
+  efq::Config c;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint8_t* d_data = nullptr;
+  float *kc = nullptr, *vc = nullptr, *rcos = nullptr, *rsin = nullptr;
+  float *x = nullptr, *h = nullptr, *q = nullptr, *knew = nullptr, *ctx = nullptr, *act = nullptr, *gate = nullptr,
+        *up = nullptr, *logits = nullptr;
+  int32_t *state = nullptr;  // [0] pos, [1] n_fixed, then tokens[max_seq], out_tokens[max_seq]
+  size_t max_seq = 0;
+  size_t cached = 0;
+  Mat embed, lm_head;
+  const float* final_norm = nullptr;
+  std::vector<Layer> layers;
+  uint64_t bytes_per_token = 0;
+  int n_q4 = 0, n_q8 = 0;
+  cudaGraphExec_t g_full = nullptr, g_prefill = nullptr;
+  int* d_err = nullptr;
+  int32_t* pos_p() const { return state; }
+  int32_t* nfix_p() const { return state + 1; }
+  int32_t* tokens() const { return state + 2; }
+  int32_t* out_tokens() const { return state + 2 + max_seq; }
+};
+
+namespace {
+
+int check_mat(const Mat& m, const char* name) {
+  if (m.type != 3 && m.type != 4)
+    return fail(EFG_EINVAL, "matrix '%s' is stored as %s; the B200 decode step runs Q4_0 and Q8_0 matrices", name,
+                efq::type_name(m.type));
+  return EFG_OK;
+}
+
+int enqueue_step(Decoder& D, bool logits, cudaStream_t s) {
+  cudaLaunchAttribute attr[1];
+  const uint32_t Dm = static_cast<uint32_t>(D.c.hidden), F = static_cast<uint32_t>(D.c.intermediate),
+                 kvd = static_cast<uint32_t>(D.c.kv_dim()), V = static_cast<uint32_t>(D.c.vocab);
+  const int H = static_cast<int>(D.c.heads), KV = static_cast<int>(D.c.kv_heads), hd = static_cast<int>(D.c.head_dim);
+  {
+    cudaLaunchConfig_t cf = cfg_of(dim3(std::max(1u, std::min(16u, (Dm + 255) / 256))), dim3(256), 0, s, attr);
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, embed_kernel, D.embed.w, D.embed.type, V, Dm,
+                                    static_cast<const int32_t*>(D.tokens()), static_cast<const int32_t*>(D.pos_p()),
+                                    D.x, D.d_err),
+                 "embed launch");
+  }
+  for (size_t l = 0; l < D.layers.size(); ++l) {
+    const Layer& Ly = D.layers[l];
+    float* kl = D.kc + l * D.max_seq * kvd;
+    float* vl = D.vc + l * D.max_seq * kvd;
+    // q/k/v: jobs grouped by type; v goes straight into the cache at pos.
+    const MatvecJobDev jq{Ly.q.w, D.q, Ly.q.rows, 0}, jk{Ly.k.w, D.knew, Ly.k.rows, 0}, jv{Ly.v.w, vl, Ly.v.rows, kvd};
+    const Mat* mats[3] = {&Ly.q, &Ly.k, &Ly.v};
+    const MatvecJobDev js[3] = {jq, jk, jv};
+    bool done[3] = {false, false, false};
+    for (int i = 0; i < 3; ++i) {
+      if (done[i]) continue;
+      MatvecArgs a;
+      a.fmt = mats[i]->type == 4 ? Fmt::Q4 : Fmt::Q8;
+      a.x = D.x;
+      a.norm_w = Ly.attn_norm;
+      a.norm_eps = static_cast<float>(D.c.rms_eps);
+      a.pos = D.pos_p();
+      a.cols = Dm;
+      a.pdl = true;
+      for (int k = i; k < 3; ++k)
+        if (!done[k] && mats[k]->type == mats[i]->type) {
+          a.jobs[a.n_jobs++] = js[k];
+          done[k] = true;
+        }
+      if (!matvec_fast_path_ok(a)) {  // explicit RMSNorm, then plain matvecs
+        cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(256), 0, s, attr);
+        EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rmsnorm_kernel, D.h, static_cast<const float*>(D.x), Ly.attn_norm, Dm,
+                                        static_cast<float>(D.c.rms_eps)),
+                     "rmsnorm launch");
+        a.x = D.h;
+        a.norm_w = nullptr;
+      }
+      if (int st = launch_matvec(a, D.d_err, s)) return st;
+    }
+    {
+      const size_t smem = (2 * hd + D.max_seq) * sizeof(float);
+      cudaLaunchConfig_t cf = cfg_of(dim3(H), dim3(kAttnThreads), smem, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, attention_kernel, static_cast<const float*>(D.q),
+                                      static_cast<const float*>(D.knew), kl, static_cast<const float*>(vl), D.ctx,
+                                      static_cast<const float*>(D.rcos), static_cast<const float*>(D.rsin),
+                                      static_cast<const int32_t*>(D.pos_p()), H, KV, hd, static_cast<int>(D.max_seq),
+                                      D.d_err),
+                   "attention launch");
+    }
+    {  // o_proj, residual add into x (src/model.cpp:247-249)
+      MatvecArgs a;
+      a.fmt = Ly.o.type == 4 ? Fmt::Q4 : Fmt::Q8;
+      a.epi = Epi::Add;
+      a.x = D.ctx;
+      a.cols = Dm;
+      a.pdl = true;
+      a.n_jobs = 1;
+      a.jobs[0] = MatvecJobDev{Ly.o.w, D.x, Ly.o.rows, 0};
+      if (int st = launch_matvec(a, D.d_err, s)) return st;
+    }
+    {  // gate/up with the ffn RMSNorm and SwiGLU (src/model.cpp:253-258)
+      MatvecArgs a;
+      a.fmt = Ly.gate.type == 4 ? Fmt::Q4 : Fmt::Q8;
+      a.epi = Epi::SwiGLU;
+      a.x = D.x;
+      a.norm_w = Ly.ffn_norm;
+      a.norm_eps = static_cast<float>(D.c.rms_eps);
+      a.cols = Dm;
+      a.pdl = true;
+      a.n_jobs = 2;
+      a.jobs[0] = MatvecJobDev{Ly.gate.w, D.act, Ly.gate.rows, 0};
+      a.jobs[1] = MatvecJobDev{Ly.up.w, D.act, Ly.up.rows, 0};
+      if (Ly.gate.type == Ly.up.type && matvec_fast_path_ok(a)) {
+        if (int st = launch_matvec(a, D.d_err, s)) return st;
+      } else {
+        cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(256), 0, s, attr);
+        EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rmsnorm_kernel, D.h, static_cast<const float*>(D.x), Ly.ffn_norm, Dm,
+                                        static_cast<float>(D.c.rms_eps)),
+                     "rmsnorm launch");
+        for (int m = 0; m < 2; ++m) {
+          const Mat& M = m == 0 ? Ly.gate : Ly.up;
+          MatvecArgs b;
+          b.fmt = M.type == 4 ? Fmt::Q4 : Fmt::Q8;
+          b.x = D.h;
+          b.cols = Dm;
+          b.pdl = true;
+          b.n_jobs = 1;
+          b.jobs[0] = MatvecJobDev{M.w, m == 0 ? D.gate : D.up, M.rows, 0};
+          if (int st = launch_matvec(b, D.d_err, s)) return st;
+        }
+        cudaLaunchConfig_t cg = cfg_of(dim3(std::max(1u, std::min(64u, (F + 255) / 256))), dim3(256), 0, s, attr);
+        EFG_TRY_CUDA(cudaLaunchKernelEx(&cg, swiglu_kernel, D.act, static_cast<const float*>(D.gate),
+                                        static_cast<const float*>(D.up), F),
+                     "swiglu launch");
+      }
+    }
+    {  // down, residual add (src/model.cpp:260-262)
+      MatvecArgs a;
+      a.fmt = Ly.down.type == 4 ? Fmt::Q4 : Fmt::Q8;
+      a.epi = Epi::Add;
+      a.x = D.act;
+      a.cols = F;
+      a.pdl = true;
+      a.n_jobs = 1;
+      a.jobs[0] = MatvecJobDev{Ly.down.w, D.x, Ly.down.rows, 0};
+      if (int st = launch_matvec(a, D.d_err, s)) return st;
+    }
+  }
+  if (logits) {
+    MatvecArgs a;
+    a.fmt = D.lm_head.type == 4 ? Fmt::Q4 : Fmt::Q8;
+    a.x = D.x;
+    a.norm_w = D.final_norm;
+    a.norm_eps = static_cast<float>(D.c.rms_eps);
+    a.cols = Dm;
+    a.pdl = true;
+    a.n_jobs = 1;
+    a.jobs[0] = MatvecJobDev{D.lm_head.w, D.logits, D.lm_head.rows, 0};
+    if (!matvec_fast_path_ok(a)) {
+      cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(256), 0, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rmsnorm_kernel, D.h, static_cast<const float*>(D.x), D.final_norm, Dm,
+                                      static_cast<float>(D.c.rms_eps)),
+                   "rmsnorm launch");
+      a.x = D.h;
+      a.norm_w = nullptr;
+    }
+    if (int st = launch_matvec(a, D.d_err, s)) return st;
+    cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(1024), 0, s, attr);
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, argmax_kernel, static_cast<const float*>(D.logits), V, D.tokens(),
+                                    D.out_tokens(), D.pos_p(), static_cast<const int32_t*>(D.nfix_p()),
+                                    static_cast<int>(D.max_seq)),
+                 "argmax launch");
+  } else {
+    cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(32), 0, s, attr);
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, advance_kernel, D.pos_p()), "advance launch");
+  }
+  return EFG_OK;
+}
+
+int capture(Decoder& D, bool logits, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  EFG_TRY_CUDA(cudaStreamBeginCapture(D.stream, cudaStreamCaptureModeThreadLocal), "graph capture");
+  const int st = enqueue_step(D, logits, D.stream);
+  const cudaError_t e = cudaStreamEndCapture(D.stream, &g);
+  if (st != EFG_OK) {
+    if (g) cudaGraphDestroy(g);
+    return st;
+  }
+  EFG_TRY_CUDA(e, "graph capture end");
+  const cudaError_t ie = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  EFG_TRY_CUDA(ie, "graph instantiate");
+  return EFG_OK;
+}
+
+void destroy(Decoder* D) {
+  if (!D) return;
+  if (D->stream) cudaStreamSynchronize(D->stream);
+  if (D->g_full) cudaGraphExecDestroy(D->g_full);
+  if (D->g_prefill) cudaGraphExecDestroy(D->g_prefill);
+  for (void* p : {static_cast<void*>(D->d_data), static_cast<void*>(D->kc), static_cast<void*>(D->vc),
+                  static_cast<void*>(D->rcos), static_cast<void*>(D->rsin), static_cast<void*>(D->x),
+                  static_cast<void*>(D->state)})
+    if (p) cudaFree(p);
+  if (D->stream) cudaStreamDestroy(D->stream);
+  delete D;
+}
+
+int open_decoder(const char* path, size_t max_seq, Decoder** out) {
+  if (!path || !out) return fail(EFG_EINVAL, "decoder_open: null argument");
+  *out = nullptr;
+  FILE* f = std::fopen(path, "rb");
+  if (!f) return fail(EFG_EINVAL, "cannot open '%s'", path);
+  std::fseek(f, 0, SEEK_END);
+  const long long fsize = std::ftell(f);
+  std::fseek(f, 0, SEEK_SET);
+  std::vector<uint8_t> file(static_cast<size_t>(fsize > 0 ? fsize : 0));
+  const size_t got = file.empty() ? 0 : std::fread(file.data(), 1, file.size(), f);
+  std::fclose(f);
+  if (got != file.size()) return fail(EFG_EINVAL, "'%s': short read", path);
+  std::unique_ptr<Decoder, void (*)(Decoder*)> D(new Decoder, destroy);
+  try {
+    D->L = efq::parse(file.data(), file.size());
+  } catch (const efq::FormatError& e) {
+    return fail(EFG_EFORMAT, "'%s': %s", path, e.what());
+  }
+  D->c = D->L.cfg;
+  const efq::Config& c = D->c;
+  if (max_seq == 0) return fail(EFG_EINVAL, "Transformer: max_seq must be > 0");
+  if (max_seq > static_cast<size_t>(c.max_position))
+    return fail(EFG_EINVAL, "Transformer: max_seq %zu exceeds max_position_embeddings %lld", max_seq,
+                static_cast<long long>(c.max_position));
+  D->max_seq = max_seq;
+  DeviceInfo* dev = current_device();
+  if (!dev) return EFG_ECUDA;
+  D->device = dev->device;
+  D->d_err = dev->d_err;
+  EFG_TRY_CUDA(cudaStreamCreateWithFlags(&D->stream, cudaStreamNonBlocking), "stream create");
+  const uint64_t base = D->L.data_start;
+  const uint64_t region = file.size() - base;
+  EFG_TRY_CUDA(cudaMalloc(&D->d_data, region ? region : 16), "weight allocation");
+  EFG_TRY_CUDA(cudaMemcpy(D->d_data, file.data() + base, region, cudaMemcpyHostToDevice), "weight upload");
+  auto mat = [&](const std::string& name) {
+    const efq::Tensor& t = D->L.at(name);
+    Mat m;
+    m.type = t.type;
+    m.w = D->d_data + (t.offset - base);
+    m.rows = static_cast<uint32_t>(t.rows());
+    m.cols = static_cast<uint32_t>(t.cols());
+    (m.type == 4 ? D->n_q4 : D->n_q8) += (m.type == 3 || m.type == 4) ? 1 : 0;
+    return m;
+  };
+  auto vec = [&](const std::string& name) {
+    const efq::Tensor& t = D->L.at(name);
+    return reinterpret_cast<const float*>(D->d_data + (t.offset - base));
+  };
+  try {
+    D->embed = mat("model.embed_tokens.weight");
+    if (D->embed.type == 3 || D->embed.type == 4) (D->embed.type == 4 ? D->n_q4 : D->n_q8) -= 1;
+    D->lm_head = c.tie_embeddings ? D->embed : mat("lm_head.weight");
+    D->final_norm = vec("model.norm.weight");
+    D->layers.resize(static_cast<size_t>(c.layers));
+    for (int64_t l = 0; l < c.layers; ++l) {
+      const std::string p = "model.layers." + std::to_string(l) + ".";
+      Layer& Ly = D->layers[static_cast<size_t>(l)];
+      Ly.q = mat(p + "self_attn.q_proj.weight");
+      Ly.k = mat(p + "self_attn.k_proj.weight");
+      Ly.v = mat(p + "self_attn.v_proj.weight");
+      Ly.o = mat(p + "self_attn.o_proj.weight");
+      Ly.gate = mat(p + "mlp.gate_proj.weight");
+      Ly.up = mat(p + "mlp.up_proj.weight");
+      Ly.down = mat(p + "mlp.down_proj.weight");
+      Ly.attn_norm = vec(p + "input_layernorm.weight");
+      Ly.ffn_norm = vec(p + "post_attention_layernorm.weight");
+      for (const Mat* m : {&Ly.q, &Ly.k, &Ly.v, &Ly.o, &Ly.gate, &Ly.up, &Ly.down})
+        if (int st = check_mat(*m, "layer matrix")) return st;
+    }
+  } catch (const efq::FormatError& e) {
+    return fail(EFG_EFORMAT, "'%s': %s", path, e.what());
+  }
+  if (int st = check_mat(D->lm_head, "lm_head.weight")) return st;
+  for (const auto& t : D->L.tensors)  // src/qfile.cpp:237-241
+    if (t.name != "model.embed_tokens.weight") D->bytes_per_token += t.bytes;
+  if (c.tie_embeddings) D->bytes_per_token += D->L.at("model.embed_tokens.weight").bytes;
+
+  const size_t kvd = static_cast<size_t>(c.kv_dim()), half = static_cast<size_t>(c.head_dim / 2);
+  if (c.head_dim % 2 != 0 || c.heads % c.kv_heads != 0)
+    return fail(EFG_EINVAL, "decoder: head_dim must be even and heads a multiple of kv_heads");
+  const size_t attn_smem = (2 * static_cast<size_t>(c.head_dim) + max_seq) * sizeof(float);
+  if (attn_smem > 227 * 1024)
+    return fail(EFG_EINVAL, "decoder: max_seq %zu is too long for the attention kernel", max_seq);
+  if (attn_smem > 48 * 1024)
+    EFG_TRY_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(attn_smem)),
+                 "attention smem attribute");
+  const size_t cache = static_cast<size_t>(c.layers) * max_seq * kvd;
+  EFG_TRY_CUDA(cudaMalloc(&D->kc, cache * sizeof(float)), "KV cache allocation");
+  EFG_TRY_CUDA(cudaMalloc(&D->vc, cache * sizeof(float)), "KV cache allocation");
+  EFG_TRY_CUDA(cudaMemset(D->kc, 0, cache * sizeof(float)), "KV cache init");
+  EFG_TRY_CUDA(cudaMemset(D->vc, 0, cache * sizeof(float)), "KV cache init");
+  // RoPE table exactly as src/kernels.cpp:113-131 computes it (float pow/cos/sin).
+  std::vector<float> cs(max_seq * half), sn(max_seq * half), inv(half);
+  for (size_t i = 0; i < half; ++i)
+    inv[i] = 1.0f / std::pow(static_cast<float>(c.rope_theta), static_cast<float>(2 * i) / static_cast<float>(c.head_dim));
+  for (size_t p = 0; p < max_seq; ++p)
+    for (size_t i = 0; i < half; ++i) {
+      const float ang = static_cast<float>(p) * inv[i];
+      cs[p * half + i] = std::cos(ang);
+      sn[p * half + i] = std::sin(ang);
+    }
+  EFG_TRY_CUDA(cudaMalloc(&D->rcos, cs.size() * sizeof(float) + 16), "rope allocation");
+  EFG_TRY_CUDA(cudaMalloc(&D->rsin, sn.size() * sizeof(float) + 16), "rope allocation");
+  EFG_TRY_CUDA(cudaMemcpy(D->rcos, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice), "rope upload");
+  EFG_TRY_CUDA(cudaMemcpy(D->rsin, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice), "rope upload");
+  const size_t Dm = static_cast<size_t>(c.hidden), F = static_cast<size_t>(c.intermediate),
+               V = static_cast<size_t>(c.vocab);
+  // one activation arena: x, h, q, knew, ctx, act, gate, up, logits (each 256-byte aligned)
+  auto al = [](size_t n) { return (n * sizeof(float) + 255) / 256 * 256; };
+  const size_t arena = al(Dm) * 5 + al(kvd) + al(F) * 3 + al(V);
+  EFG_TRY_CUDA(cudaMalloc(&D->x, arena), "activation allocation");
+  uint8_t* a = reinterpret_cast<uint8_t*>(D->x);
+  size_t o = al(Dm);
+  D->h = reinterpret_cast<float*>(a + o), o += al(Dm);
+  D->q = reinterpret_cast<float*>(a + o), o += al(Dm);
+  D->ctx = reinterpret_cast<float*>(a + o), o += al(Dm);
+  o += al(Dm);
+  D->knew = reinterpret_cast<float*>(a + o), o += al(kvd);
+  D->act = reinterpret_cast<float*>(a + o), o += al(F);
+  D->gate = reinterpret_cast<float*>(a + o), o += al(F);
+  D->up = reinterpret_cast<float*>(a + o), o += al(F);
+  D->logits = reinterpret_cast<float*>(a + o);
+  EFG_TRY_CUDA(cudaMalloc(&D->state, (2 + 2 * max_seq) * sizeof(int32_t)), "state allocation");
+  EFG_TRY_CUDA(cudaMemset(D->state, 0, (2 + 2 * max_seq) * sizeof(int32_t)), "state init");
+  if (int st = capture(*D, true, &D->g_full)) return st;
+  if (int st = capture(*D, false, &D->g_prefill)) return st;
+  *out = D.release();
+  return EFG_OK;
+}
+
+int set_step(Decoder& D, int32_t token, size_t pos, int32_t n_fixed) {
+  const int32_t st[2] = {static_cast<int32_t>(pos), n_fixed};
+  EFG_TRY_CUDA(cudaMemcpyAsync(D.state, st, sizeof st, cudaMemcpyHostToDevice, D.stream), "state upload");
+  EFG_TRY_CUDA(cudaMemcpyAsync(D.tokens() + pos, &token, sizeof token, cudaMemcpyHostToDevice, D.stream),
+               "token upload");
+  return EFG_OK;
+}
+
+}  // namespace
+}  // namespace efg
+
+using efg::Decoder;
+using efg::fail;
+
+extern "C" {
+
+int efg_efq_check(const void* data, uint64_t size) {
+  if (!data && size) return fail(EFG_EINVAL, "efq_check: null data");
+  try {
+    (void)efg::efq::parse(static_cast<const uint8_t*>(data), size);
+  } catch (const efg::efq::FormatError& e) {
+    return fail(EFG_EFORMAT, "%s", e.what());
+  }
+  return EFG_OK;
+}
+
+int efg_decoder_open(const char* efq_path, size_t max_seq, efg_decoder** out) {
+  Decoder* d = nullptr;
+  const int st = efg::open_decoder(efq_path, max_seq, &d);
+  if (out) *out = reinterpret_cast<efg_decoder*>(d);
+  return st;
+}
+
+int efg_decoder_close(efg_decoder* h) {
+  efg::destroy(reinterpret_cast<Decoder*>(h));
+  return EFG_OK;
+}
+
+int efg_decoder_info(const efg_decoder* h, efg_model_info* info) {
+  if (!h || !info) return fail(EFG_EINVAL, "decoder_info: null argument");
+  const Decoder& D = *reinterpret_cast<const Decoder*>(h);
+  info->hidden = static_cast<int32_t>(D.c.hidden);
+  info->intermediate = static_cast<int32_t>(D.c.intermediate);
+  info->layers = static_cast<int32_t>(D.c.layers);
+  info->heads = static_cast<int32_t>(D.c.heads);
+  info->kv_heads = static_cast<int32_t>(D.c.kv_heads);
+  info->head_dim = static_cast<int32_t>(D.c.head_dim);
+  info->vocab = static_cast<int32_t>(D.c.vocab);
+  info->max_seq = static_cast<int32_t>(D.max_seq);
+  info->n_q4 = D.n_q4;
+  info->n_q8 = D.n_q8;
+  info->embed_type = D.embed.type;
+  info->bytes_per_token = D.bytes_per_token;
+  return EFG_OK;
+}
+
+int efg_decoder_reset(efg_decoder* h) {
+  if (!h) return fail(EFG_EINVAL, "decoder_reset: null handle");
+  reinterpret_cast<Decoder*>(h)->cached = 0;
+  return EFG_OK;
+}
+
+int efg_decoder_forward(efg_decoder* h, int32_t token, size_t pos, float* logits) {
+  if (!h) return fail(EFG_EINVAL, "forward: null handle");
+  Decoder& D = *reinterpret_cast<Decoder*>(h);
+  if (token < 0 || token >= D.c.vocab)
+    return fail(EFG_EINVAL, "forward: token id %d is outside [0, %lld)", token, static_cast<long long>(D.c.vocab));
+  if (pos >= D.max_seq)
+    return fail(EFG_ESTATE, "forward: position %zu exceeds the KV-cache capacity %zu", pos, D.max_seq);
+  if (pos > D.cached)
+    return fail(EFG_ESTATE, "forward: position %zu skips ahead of the %zu cached tokens", pos, D.cached);
+  if (int st = efg::set_step(D, token, pos, static_cast<int32_t>(pos + 1))) return st;
+  EFG_TRY_CUDA(cudaGraphLaunch(logits ? D.g_full : D.g_prefill, D.stream), "graph launch");
+  if (logits)
+    EFG_TRY_CUDA(cudaMemcpyAsync(logits, D.logits, D.c.vocab * sizeof(float), cudaMemcpyDeviceToHost, D.stream),
+                 "logits download");
+  EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+  D.cached = pos + 1;
+  return EFG_OK;
+}
+
+int efg_decoder_generate(efg_decoder* h, const int32_t* prompt, size_t n_prompt, size_t max_new, int32_t eos_id,
+                         const int32_t* forced, int32_t* tokens_out, size_t* n_tokens, float* step_logits,
+                         double* prefill_seconds, double* decode_seconds) {
+  if (!h || !prompt || !tokens_out) return fail(EFG_EINVAL, "generate: null argument");
+  Decoder& D = *reinterpret_cast<Decoder*>(h);
+  if (n_prompt == 0) return fail(EFG_EINVAL, "generate: empty prompt");
+  if (n_prompt + max_new > D.max_seq)
+    return fail(EFG_EINVAL, "generate: prompt (%zu) + max_new (%zu) exceeds the KV-cache capacity %zu", n_prompt,
+                max_new, D.max_seq);
+  for (size_t i = 0; i < n_prompt; ++i)
+    if (prompt[i] < 0 || prompt[i] >= D.c.vocab) return fail(EFG_EINVAL, "generate: token id %d out of range", prompt[i]);
+  // tokens[]: the prompt, then (teacher forcing) the forced continuation
+  const size_t n_fixed = n_prompt + (forced ? max_new : 0);
+  std::vector<int32_t> seq(prompt, prompt + n_prompt);
+  if (forced) seq.insert(seq.end(), forced, forced + max_new);
+  const int32_t st0[2] = {0, static_cast<int32_t>(n_fixed)};
+  EFG_TRY_CUDA(cudaMemcpyAsync(D.state, st0, sizeof st0, cudaMemcpyHostToDevice, D.stream), "state upload");
+  EFG_TRY_CUDA(cudaMemcpyAsync(D.tokens(), seq.data(), seq.size() * sizeof(int32_t), cudaMemcpyHostToDevice, D.stream),
+               "token upload");
+  cudaEvent_t e0, e1, e2;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventCreate(&e2);
+  cudaEventRecord(e0, D.stream);
+  for (size_t p = 0; p + 1 < n_prompt; ++p) EFG_TRY_CUDA(cudaGraphLaunch(D.g_prefill, D.stream), "graph launch");
+  EFG_TRY_CUDA(cudaGraphLaunch(D.g_full, D.stream), "graph launch");  // last prompt token: logits, next token
+  cudaEventRecord(e1, D.stream);
+  size_t n_out = 0;
+  bool stopped = false;
+  // generate_greedy (src/model.cpp:278-304): take argmax, stop at eos or max_new, else forward.
+  for (size_t step = 0; step < max_new && !stopped; ++step) {
+    if (eos_id >= 0) {  // the token decides whether to go on: read it back every step
+      int32_t tok = 0;
+      EFG_TRY_CUDA(cudaMemcpyAsync(&tok, D.out_tokens() + n_prompt - 1 + step, sizeof tok, cudaMemcpyDeviceToHost,
+                                   D.stream),
+                   "token download");
+      EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+      if (tok == eos_id) stopped = true;
+    }
+    ++n_out;
+    if (stopped || step + 1 == max_new) break;
+    EFG_TRY_CUDA(cudaGraphLaunch(D.g_full, D.stream), "graph launch");
+    if (step_logits)
+      EFG_TRY_CUDA(cudaMemcpyAsync(step_logits + step * D.c.vocab, D.logits, D.c.vocab * sizeof(float),
+                                   cudaMemcpyDeviceToHost, D.stream),
+                   "logits download");
+  }
+  cudaEventRecord(e2, D.stream);
+  EFG_TRY_CUDA(cudaMemcpyAsync(tokens_out, D.out_tokens() + n_prompt - 1, n_out * sizeof(int32_t),
+                               cudaMemcpyDeviceToHost, D.stream),
+               "token download");
+  EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+  float ms_pre = 0.f, ms_dec = 0.f;
+  cudaEventElapsedTime(&ms_pre, e0, e1);
+  cudaEventElapsedTime(&ms_dec, e1, e2);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaEventDestroy(e2);
+  if (prefill_seconds) *prefill_seconds = ms_pre / 1e3;
+  if (decode_seconds) *decode_seconds = ms_dec / 1e3;
+  if (n_tokens) *n_tokens = n_out;
+  D.cached = n_prompt + (n_out ? n_out - 1 : 0);
+  return EFG_OK;
+}
+
+}  // extern "C"

@@ -155,6 +155,46 @@ int efg_host_unregister_weights(const void* host);
 /* Drops every resident copy. */
 int efg_host_release_weights(void);
 
+/* ================================================================ .efq and the decode step */
+
+/* Validates an .efq file image in memory: magic, version, JSON header, tensor table (types,
+ * shapes, 64-byte offsets, bounds, overlaps), the exact tensor set the config requires and
+ * the precision policy. Replaces ef::parse_efq (include/ef/qfile.h:133, src/qfile.cpp:125-223);
+ * EFG_EFORMAT with the reference's message on the same faults. */
+int efg_efq_check(const void* data, uint64_t size);
+
+typedef struct efg_decoder efg_decoder;
+
+typedef struct {
+  int32_t hidden, intermediate, layers, heads, kv_heads, head_dim, vocab, max_seq;
+  int32_t n_q4, n_q8;       /* packed matrices of each type (embedding excluded) */
+  int32_t embed_type;       /* EFG_* type of the token embedding */
+  uint64_t bytes_per_token; /* weight bytes streamed per decoded token (src/qfile.cpp:237-241) */
+} efg_model_info;
+
+/* Loads an .efq (validated as efg_efq_check), uploads its data once to the current device,
+ * allocates an FP32 KV cache of max_seq positions and records the decode step as CUDA
+ * graphs. Replaces ef::Model::load_efq + the ef::Transformer constructor
+ * (src/model.cpp:66-111, 153-182). Layer matrices and lm_head must be Q4_0 or Q8_0. */
+int efg_decoder_open(const char* efq_path, size_t max_seq, efg_decoder** out);
+int efg_decoder_close(efg_decoder* d);
+int efg_decoder_info(const efg_decoder* d, efg_model_info* info);
+/* ef::Transformer::reset (include/ef/model.h:102). */
+int efg_decoder_reset(efg_decoder* d);
+/* ef::Transformer::forward (src/model.cpp:184-276): runs `token` at `pos` (pos <= cached, a
+ * smaller pos rewinds); writes the next-token logits to the host array `logits` (vocab
+ * floats) unless it is NULL, which skips lm_head like compute_logits = false. */
+int efg_decoder_forward(efg_decoder* d, int32_t token, size_t pos, float* logits);
+/* ef::generate_greedy (src/model.cpp:278-304): prefill the prompt from position 0, then
+ * argmax decoding of up to max_new tokens, stopping after eos_id (if >= 0). With `forced`
+ * (max_new ids) the decode steps are teacher-forced on those ids instead of the argmax,
+ * while tokens_out still receives each step's argmax. step_logits (NULL or a host array of
+ * (max_new - 1) * vocab floats) receives the logits after each decode forward. Times are
+ * device time of the prefill and of the decode loop. */
+int efg_decoder_generate(efg_decoder* d, const int32_t* prompt, size_t n_prompt, size_t max_new, int32_t eos_id,
+                         const int32_t* forced, int32_t* tokens_out, size_t* n_tokens, float* step_logits,
+                         double* prefill_seconds, double* decode_seconds);
+
 #ifdef __cplusplus
 }
 #endif

@@ -216,7 +216,7 @@ class Reference(_Lib):
         self._mv = self._fn("matvec", C.c_int, C.c_int, _vp, C.c_int, _fp, _u8, _fp, _sz, _sz)
         self._qrows = self._fn("quantize_rows", C.c_int, _vp, C.c_int, _fp, _sz, _sz, _vp, C.c_int)
         self._drows = self._fn("dequantize_rows", C.c_int, _vp, C.c_int, _vp, _sz, _sz, _fp)
-        self._qmodel = self._fn("quantize_model", C.c_int, C.c_char_p, C.c_char_p, C.c_char_p, C.c_uint)
+        self._qmodel = self._fn("quantize_model", C.c_int, C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_uint)
         self._dec_new = self._fn("decoder_new", _vp, C.c_char_p, _sz, C.c_uint)
         self._dec_free = self._fn("decoder_free", None, _vp)
         self._dec_reset = self._fn("decoder_reset", None, _vp)
@@ -255,8 +255,11 @@ class Reference(_Lib):
             raise RuntimeError(self.error())
         return out
 
-    def quantize_model(self, model_dir, out_file, policy="auto", threads=0):
-        if self._qmodel(str(model_dir).encode(), str(out_file).encode(), policy.encode(), threads) != 0:
+    def quantize_model(self, model_dir, out_file, policy="auto", overrides="", threads=0):
+        """quantize_model (src/quantizer.cpp:151-290): a named policy, or explicit overrides
+        in the reference's TENSOR=TYPE,... form."""
+        if self._qmodel(str(model_dir).encode(), str(out_file).encode(), policy.encode(), overrides.encode(),
+                        threads) != 0:
             raise RuntimeError(self.error())
 
     def decoder(self, efq_file, max_seq, threads=1):
@@ -310,3 +313,115 @@ class _Decoder:
 
 def reference_available() -> bool:
     return REF_SO.exists()
+
+
+# ---------------------------------------------------------------- the decode step on the C restatement
+
+
+class _Weight(C.Structure):
+    _fields_ = [("type", C.c_int), ("data", _vp), ("rows", _sz), ("cols", _sz)]
+
+
+class _Layer(C.Structure):
+    _fields_ = [(n, _Weight) for n in ("wq", "wk", "wv", "wo", "w_gate", "w_up", "w_down")] + [
+        ("attn_norm", _fp), ("ffn_norm", _fp)]
+
+
+class _Model(C.Structure):
+    _fields_ = [(n, _sz) for n in ("D", "F", "H", "KV", "hd", "V", "L", "max_seq")] + [
+        ("eps", C.c_float), ("rope_theta", C.c_float), ("embed", _Weight), ("lm_head", _Weight),
+        ("final_norm", _fp), ("layers", C.POINTER(_Layer))]
+
+
+_TYPES = {"F32": F32, "F16": F16, "BF16": BF16, "Q8_0": Q8_0, "Q4_0": Q4_0}
+
+
+def read_efq(path):
+    """(config dict, {name: (type, shape, uint8 view of the tensor's bytes)}) of an .efq file
+    (layout of src/qfile.cpp:79-123: "EFQ1", u32 version, u64 header length, JSON header,
+    tensors at absolute 64-byte aligned offsets)."""
+    import json
+
+    raw = np.fromfile(path, dtype=np.uint8)
+    if bytes(raw[:4]) != b"EFQ1":
+        raise ValueError("bad magic")
+    hlen = int(raw[8:16].view("<u8")[0])
+    hdr = json.loads(bytes(raw[16:16 + hlen]).decode())
+    tensors = {}
+    for t in hdr["tensors"]:
+        off, n = int(t["offset"]), int(t["bytes"])
+        tensors[t["name"]] = (_TYPES[t["type"].upper()], [int(s) for s in t["shape"]], raw[off:off + n])
+    return hdr["config"], tensors
+
+
+class OracleDecoder:
+    """efo_forward (oracle/efo.c, restating src/model.cpp:184-276) over an .efq file."""
+
+    def __init__(self, oracle: Oracle, efq_file, max_seq: int):
+        self.o = oracle
+        cfg, t = read_efq(efq_file)
+        self._keep = t
+        D, H = int(cfg["hidden_size"]), int(cfg["num_attention_heads"])
+        L = int(cfg["num_hidden_layers"])
+        self.vocab = int(cfg["vocab_size"])
+
+        def w(name):
+            ty, shape, data = t[name]
+            return _Weight(ty, data.ctypes.data, shape[0] if len(shape) == 2 else 1, shape[-1])
+
+        def v(name):
+            return C.cast(C.c_void_p(t[name][2].ctypes.data), _fp)
+
+        layers = (_Layer * L)()
+        for i in range(L):
+            p = f"model.layers.{i}."
+            layers[i] = _Layer(w(p + "self_attn.q_proj.weight"), w(p + "self_attn.k_proj.weight"),
+                               w(p + "self_attn.v_proj.weight"), w(p + "self_attn.o_proj.weight"),
+                               w(p + "mlp.gate_proj.weight"), w(p + "mlp.up_proj.weight"),
+                               w(p + "mlp.down_proj.weight"), v(p + "input_layernorm.weight"),
+                               v(p + "post_attention_layernorm.weight"))
+        self._layers = layers
+        tied = bool(cfg.get("tie_word_embeddings", False))
+        m = _Model(D, int(cfg["intermediate_size"]), H, int(cfg.get("num_key_value_heads", H)),
+                   int(cfg.get("head_dim", D // H)), self.vocab, L, int(max_seq), float(cfg["rms_norm_eps"]),
+                   float(cfg.get("rope_theta", 10000.0)), w("model.embed_tokens.weight"),
+                   w("model.embed_tokens.weight" if tied else "lm_head.weight"), v("model.norm.weight"), layers)
+        self._model = m
+        lib = oracle.lib
+        lib.efo_state_new.restype = _vp
+        lib.efo_state_new.argtypes = [C.POINTER(_Model)]
+        lib.efo_state_free.argtypes = [_vp]
+        lib.efo_forward.restype = C.c_int
+        lib.efo_forward.argtypes = [_vp, C.c_int32, _sz, _fp, C.c_int]
+        self._s = lib.efo_state_new(C.byref(m))
+        if not self._s:
+            raise MemoryError("efo_state_new failed")
+
+    def forward(self, token: int, pos: int, logits=True, threads=os.cpu_count() or 1):
+        out = np.zeros(self.vocab, np.float32) if logits else None
+        if self.o.lib.efo_forward(self._s, int(token), int(pos), _p(out, _fp) if logits else None, threads) != 0:
+            raise ValueError("efo_forward rejected the token or position")
+        return out
+
+    def close(self):
+        if self._s:
+            self.o.lib.efo_state_free(self._s)
+            self._s = None
+
+    def __del__(self):
+        self.close()
+
+    def run(self, prompt, forced, threads=os.cpu_count() or 1):
+        """Teacher-forced greedy run: the prompt, then the `forced` ids. Returns the logits
+        after the last prompt token and after each forced token but the last, as
+        [len(forced)][vocab] (the logits generate_greedy takes its argmax from)."""
+        out = []
+        pos = 0
+        for i, tok in enumerate(prompt):
+            lg = self.forward(tok, pos, logits=i + 1 == len(prompt), threads=threads)
+            pos += 1
+        out.append(lg)
+        for tok in list(forced)[:-1]:
+            out.append(self.forward(tok, pos, threads=threads))
+            pos += 1
+        return np.stack(out)

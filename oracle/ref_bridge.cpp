@@ -156,13 +156,18 @@ void efr_attention(float* out, const float* q, const float* k, const float* v, s
 
 // src/quantizer.cpp:92-115,151-290: quantize a model directory (config.json +
 // model.safetensors) into an .efq with the named policy ("auto", "uniform", ...).
-int efr_quantize_model(const char* model_dir, const char* out_file, const char* policy, unsigned threads) {
+int efr_quantize_model(const char* model_dir, const char* out_file, const char* policy, const char* overrides,
+                       unsigned threads) {
   return guarded([&] {
     const ef::ModelConfig cfg = ef::load_model_config(std::filesystem::path(model_dir) / "config.json");
-    const ef::PolicySelection sel = ef::select_policy(policy, cfg);
     ef::QuantizeOptions o;
-    o.overrides = sel.overrides;
-    o.policy_name = sel.name;
+    if (overrides && *overrides) {  // explicit per-tensor overrides (ef::parse_overrides)
+      o.overrides = ef::parse_overrides(overrides);
+    } else {
+      const ef::PolicySelection sel = ef::select_policy(policy, cfg);
+      o.overrides = sel.overrides;
+      o.policy_name = sel.name;
+    }
     o.threads = threads;
     ef::quantize_model(model_dir, out_file, o);
   });
