@@ -18,6 +18,7 @@ from .api import (  # noqa: F401
     efq_check,
     host_dequantize_row,
     host_matvec,
+    host_matvec_static,
     host_quantize_row,
     host_register_weights,
     host_unregister_weights,

@@ -62,6 +62,7 @@ SIGNATURES = {
     "efg_host_register_weights": (_i, [_vp, _sz]),
     "efg_host_unregister_weights": (_i, [_vp]),
     "efg_host_release_weights": (_i, []),
+    "efg_host_matvec_static": (_i, [_i, _vp, _vp, _vp, _sz, _sz]),
     "efg_efq_check": (_i, [_vp, _u64]),
     "efg_decoder_open": (_i, [C.c_char_p, _sz, C.POINTER(_vp)]),
     "efg_decoder_close": (_i, [_vp]),

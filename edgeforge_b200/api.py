@@ -187,6 +187,16 @@ def host_release_weights() -> None:
     check(load().efg_host_release_weights())
 
 
+def host_matvec_static(qtype: int, W: np.ndarray, x: np.ndarray, rows: int) -> np.ndarray:
+    """efg_host_matvec_static: host_matvec staged through the library's fixed 8 MiB device
+    area (no device allocation; calls must not overlap)."""
+    W, pw = _np(W, np.uint8)
+    x, px = _np(x, np.float32)
+    y = np.zeros(rows, dtype=np.float32)
+    check(load().efg_host_matvec_static(int(qtype), C.c_void_p(y.ctypes.data), pw, px, rows, x.size))
+    return y
+
+
 # ---------------------------------------------------------------- .efq and the decode step
 
 

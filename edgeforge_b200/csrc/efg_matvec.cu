@@ -596,6 +596,12 @@ bool matvec_fast_path_ok(const MatvecArgs& a) {
 int launch_matvec(const MatvecArgs& a, int* d_err, cudaStream_t stream) {
   DeviceInfo* dev = current_device();
   if (!dev) return EFG_ECUDA;
+  return launch_matvec_on(a, *dev, d_err, stream, false);
+}
+
+int launch_matvec_on(const MatvecArgs& a, const DeviceInfo& devinfo, int* d_err, cudaStream_t stream,
+                     bool direct_smem_attr) {
+  const DeviceInfo* dev = &devinfo;
   if (a.fmt != Fmt::Q4 && a.fmt != Fmt::Q8) return fail(EFG_EINVAL, "matvec: type must be Q4_0 or Q8_0");
   if (a.cols % 32 != 0) {
     return fail(EFG_EINVAL, "%s needs a row length divisible by 32, got %zu", a.fmt == Fmt::Q4 ? "Q4_0" : "Q8_0",
@@ -671,7 +677,13 @@ int launch_matvec(const MatvecArgs& a, int* d_err, cudaStream_t stream) {
     k.tiles_total = t;
     FastFn fn = pick_fast(a.fmt, static_cast<int>(pl.RB), a.epi, a.norm_w != nullptr);
     if (!fn) return fail(EFG_EINVAL, "matvec: no kernel for this configuration");
-    if (int st = ensure_smem_attr(reinterpret_cast<const void*>(fn), pl.smem)) return st;
+    if (direct_smem_attr) {
+      EFG_TRY_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(pl.smem)),
+                   "kernel shared-memory attribute");
+    } else if (int st = ensure_smem_attr(reinterpret_cast<const void*>(fn), pl.smem)) {
+      return st;
+    }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(std::min<uint32_t>(k.tiles_total, static_cast<uint32_t>(dev->sm_count)));
     cfg.blockDim = dim3(32 * (pl.G * pl.H * pl.RG + 1));

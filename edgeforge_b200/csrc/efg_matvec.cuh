@@ -39,6 +39,13 @@ struct MatvecArgs {
 // left in the thread-local error string.
 int launch_matvec(const MatvecArgs& a, int* d_err, cudaStream_t stream);
 
+// launch_matvec on a caller-described device. With direct_smem_attr the kernel's
+// shared-memory limit is set by cudaFuncSetAttribute on every launch instead of through
+// the library's per-kernel cache, so the call touches no library-owned state.
+struct DeviceInfo;
+int launch_matvec_on(const MatvecArgs& a, const DeviceInfo& dev, int* d_err, cudaStream_t stream,
+                     bool direct_smem_attr);
+
 // True when the fast (bulk-copy) kernel accepts these arguments; otherwise
 // launch_matvec uses the generic kernel (plain loads, any alignment).
 bool matvec_fast_path_ok(const MatvecArgs& a);

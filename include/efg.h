@@ -155,6 +155,14 @@ int efg_host_unregister_weights(const void* host);
 /* Drops every resident copy. */
 int efg_host_release_weights(void);
 
+/* efg_host_matvec without device allocation: x, y and W are staged through one static
+ * 8 MiB device area (its address taken once per device by the first call, which must come
+ * before any stream capture); calls needing more than the area are rejected (EFG_EINVAL).
+ * Overlapping calls race on the area and must be serialized by the caller. This entry
+ * point has no reference counterpart: the reference's kern::matvec_q4_0/q8_0 allocate
+ * nothing because they run on host memory. */
+int efg_host_matvec_static(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols);
+
 /* ================================================================ .efq and the decode step */
 
 /* Validates an .efq file image in memory: magic, version, JSON header, tensor table (types,
