@@ -289,6 +289,8 @@ def run_ours(args):
     gbs4 = algo_bytes(Q4_0, q4_rows, q4_cols) / (ms4 / 1e3) / 1e9
     del W4
 
+    dec = decode_extra(hbm_peak, with_cpu=not args.no_cpu_baseline) if world == 1 and not args.no_decode else None
+
     # DRAM bytes per launch of this kernel from the committed ncu capture summary
     traffic = None
     tpath = ROOT / "profiles" / "matvec_q8_0_32000x2048.json"
@@ -321,13 +323,81 @@ def run_ours(args):
             "clocks": clocks.summary(),
             "extra": {"config0_q4_0_matvec_5632x2048": {
                 "gbs": round(gbs4, 1), "frac_of_hbm": round(gbs4 / hbm_peak, 4), "us_per_launch": round(ms4 * 1e3, 3),
-                "bytes_per_launch": algo_bytes(Q4_0, q4_rows, q4_cols), "copies": q4_copies}},
+                "bytes_per_launch": algo_bytes(Q4_0, q4_rows, q4_cols), "copies": q4_copies},
+                "config2_decode_tinyllama": dec},
         }
         print(json.dumps(line))
     if world > 1:
         del g_full, g_rem
         torch.distributed.destroy_process_group()
     return 0
+
+
+def decode_model():
+    """The config-2 model: a random TinyLlama-1.1B-shaped checkpoint (seed 0) quantized by
+    this library's GPU writer with the reference's "auto" policy; cached in the temp dir."""
+    import tempfile
+
+    import edgeforge_b200 as efg
+    from edgeforge_b200 import synthetic
+
+    d = Path(os.environ.get("EFG_TEST_CACHE", tempfile.gettempdir())) / "efg_tinyllama_seed0"
+    if not (d / "model.safetensors").exists() or not (d / "config.json").exists():
+        synthetic.write_checkpoint(d, synthetic.TINYLLAMA, seed=0)
+    efq = d / "model-gpu.efq"
+    if not efq.exists():
+        part = d / "model-gpu.efq.part"
+        efg.quantize_model(d, part, policy="auto")
+        part.rename(efq)
+    return efq
+
+
+def decode_extra(hbm_peak, with_cpu, prompt_len=23, steps=32, reps=5):
+    """Config 2: a 23-token prompt, then 32 greedy decode steps (device time of the decode
+    loop, best of `reps` runs after one warm-up run)."""
+    import edgeforge_b200 as efg
+
+    efq = decode_model()
+    prompt = np.random.default_rng(2).integers(0, 32000, prompt_len).astype(np.int32)
+    with efg.Decoder(efq, prompt_len + steps) as dec:
+        dec.generate(prompt, steps)
+        runs = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            r = dec.generate(prompt, steps)
+            runs.append((r.decode_seconds, r.prefill_seconds, time.perf_counter() - t0))
+        bpt = dec.bytes_per_token
+        tokens = r.tokens
+    dsec, psec, wall = min(runs)
+    tok_s = (steps - 1) / dsec
+    out = {"decode_tok_s": round(tok_s, 1), "prefill_tok_s": round(prompt_len / psec, 1),
+           "weight_gbs": round(bpt * tok_s / 1e9, 1), "frac_of_hbm": round(bpt * tok_s / 1e9 / hbm_peak, 4),
+           "ms_per_token": round(dsec / (steps - 1) * 1e3, 4), "bytes_per_token": bpt,
+           "e2e_generate_s": round(wall, 5), "prompt": prompt_len, "steps": steps,
+           "model": "random TinyLlama-1.1B shape, .efq from efg_quantize_model (policy auto)"}
+    if with_cpu and (ROOT / "oracle" / "_ref" / "libefref.so").exists():
+        from oracle.oracle import Reference
+
+        threads = os.cpu_count() or 1
+        rd = Reference().decoder(efq, prompt_len + steps, threads=threads)
+        pos = 0
+        for i, t in enumerate(prompt):
+            lg = rd.forward(int(t), pos, 32000, logits=i + 1 == prompt_len)
+            pos += 1
+        t0 = time.perf_counter()
+        ref_tokens = []
+        for step in range(steps):
+            ref_tokens.append(int(np.argmax(lg)))
+            if step + 1 == steps:
+                break
+            lg = rd.forward(ref_tokens[-1], pos, 32000)
+            pos += 1
+        el = time.perf_counter() - t0
+        rd.close()
+        out["cpu_reference_tok_s"] = round((steps - 1) / el, 2)
+        out["cpu_reference_threads"] = threads
+        out["greedy_tokens_match_reference"] = ref_tokens == list(tokens)
+    return out
 
 
 def run_profile(args):
@@ -361,6 +431,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode measurement")
     ap.add_argument("--profile", choices=["q8", "q4", "q4big"], help="a few plain launches for ncu")
     args = ap.parse_args()
     if args.profile:

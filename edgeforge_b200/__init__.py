@@ -27,6 +27,7 @@ from .api import (  # noqa: F401
     matvec_jobs,
     matvec_q4_0,
     matvec_q8_0,
+    quantize_model,
     quantize_row,
     quantize_rows,
     row_bytes,

@@ -30,6 +30,13 @@ class MatvecJob(C.Structure):
     _fields_ = [("d_y", _vp), ("qtype", _i), ("d_W", _vp), ("rows", _sz), ("cols", _sz), ("d_x", _vp)]
 
 
+class QuantizeReport(C.Structure):
+    """efg_quantize_report (include/efg.h)."""
+
+    _fields_ = [("file_bytes", C.c_uint64), ("bytes_per_token", C.c_uint64), ("source_tensor_bytes", C.c_uint64),
+                ("override_extra_bytes", C.c_int64), ("n_tensors", C.c_int32), ("seconds", C.c_double)]
+
+
 class ModelInfo(C.Structure):
     """efg_model_info (include/efg.h)."""
 
@@ -64,6 +71,7 @@ SIGNATURES = {
     "efg_host_release_weights": (_i, []),
     "efg_host_matvec_static": (_i, [_i, _vp, _vp, _vp, _sz, _sz]),
     "efg_efq_check": (_i, [_vp, _u64]),
+    "efg_quantize_model": (_i, [C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(QuantizeReport)]),
     "efg_decoder_open": (_i, [C.c_char_p, _sz, C.POINTER(_vp)]),
     "efg_decoder_close": (_i, [_vp]),
     "efg_decoder_info": (_i, [_vp, C.POINTER(ModelInfo)]),

@@ -17,7 +17,7 @@ from enum import IntEnum
 
 import numpy as np
 
-from ._lib import EdgeForgeError, MatvecJob, ModelInfo, check, load
+from ._lib import EdgeForgeError, MatvecJob, ModelInfo, QuantizeReport, check, load
 
 
 class QType(IntEnum):
@@ -205,6 +205,15 @@ def efq_check(data: bytes | np.ndarray) -> None:
     EdgeForgeError carrying the reference's message on a malformed file."""
     buf = np.frombuffer(data, dtype=np.uint8) if isinstance(data, (bytes, bytearray)) else np.ascontiguousarray(data)
     check(load().efg_efq_check(C.c_void_p(buf.ctypes.data if buf.size else 0), buf.size))
+
+
+def quantize_model(model_dir, out_file, policy: str = "auto", overrides: str = "") -> QuantizeReport:
+    """ef::quantize_model (src/quantizer.cpp:151-290) on the GPU: config.json +
+    model.safetensors -> .efq, byte-identical to the reference's writer."""
+    rep = QuantizeReport()
+    check(load().efg_quantize_model(str(model_dir).encode(), str(out_file).encode(), policy.encode(),
+                                    overrides.encode(), C.byref(rep)))
+    return rep
 
 
 class GreedyResult:

@@ -265,6 +265,39 @@ __global__ void widen_kernel(int qtype, const uint8_t* __restrict__ in, float* _
   }
 }
 
+// Reconstruction statistics of one quantized row per thread (src/quantizer.cpp:131-147):
+// e = double(src) - double(dequantized), sse += e * e, ref += src^2 (double, column order,
+// no contraction) and the largest |e|, so the totals the writer forms from them are the
+// reference's to the last bit.
+__global__ void quant_stats_kernel(int qtype, const float* __restrict__ src, const uint8_t* __restrict__ q,
+                                   uint64_t rows, uint64_t cols, double* __restrict__ sse, double* __restrict__ ref,
+                                   double* __restrict__ mx) {
+  const uint64_t r = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const uint32_t bb = qtype == 4 ? 18 : 34;
+  const float* x = src + r * cols;
+  const uint8_t* row = q + r * (cols / 32) * bb;
+  double s = 0.0, rs = 0.0, m = 0.0;
+  for (uint64_t b = 0; b < cols / 32; ++b) {
+    const uint8_t* blk = row + b * bb;
+    const float d = fp16_to_f32(blk[0] | (blk[1] << 8));
+    for (int j = 0; j < 32; ++j) {
+      int code;
+      if (qtype == 4) code = (j < 16 ? (blk[2 + j] & 15) : (blk[2 + j - 16] >> 4)) - 8;
+      else code = static_cast<int8_t>(blk[2 + j]);
+      const double xv = static_cast<double>(__ldg(x + b * 32 + j));
+      const double e = __dsub_rn(xv, static_cast<double>(dequant_mul(code, d)));
+      s = __dadd_rn(s, __dmul_rn(e, e));
+      rs = __dadd_rn(rs, __dmul_rn(xv, xv));
+      const double ae = fabs(e);
+      m = m < ae ? ae : m;
+    }
+  }
+  sse[r] = s;
+  ref[r] = rs;
+  mx[r] = m;
+}
+
 // Row r of a [rows][cols] matrix as FP32 (src/qkernels.cpp:299-305): exact for
 // F32/F16/BF16, dequantized for Q8_0/Q4_0. r comes from *d_r when given (a token id
 // produced on the device); an out-of-range id records EFG_EINVAL in *err and writes
@@ -363,6 +396,16 @@ int launch_dequantize(int qtype, const void* in, uint64_t n_values, float* out, 
     cudaLaunchConfig_t c = config(grid, 256, s, attr, pdl);
     EFG_TRY_CUDA(cudaLaunchKernelEx(&c, widen_kernel, qtype, p, out, n_values), "dequantize launch");
   }
+  return EFG_OK;
+}
+
+int launch_quant_stats(int qtype, const float* src, const uint8_t* q, uint64_t rows, uint64_t cols, double* sse,
+                       double* ref, double* mx, cudaStream_t s) {
+  if (qtype != 3 && qtype != 4) return fail(EFG_EINVAL, "quant_stats: type must be Q8_0 or Q4_0");
+  if (cols % 32 != 0) return fail(EFG_EINVAL, "quant_stats: cols %% 32 != 0");
+  if (rows == 0) return EFG_OK;
+  quant_stats_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, s>>>(qtype, src, q, rows, cols, sse, ref, mx);
+  EFG_TRY_CUDA(cudaGetLastError(), "quant_stats launch");
   return EFG_OK;
 }
 

@@ -12,6 +12,10 @@ int launch_quantize(int qtype, const float* x, uint64_t n_values, void* out, boo
                     bool pdl = false);
 // Inverse, also for 0 = F32, 1 = F16, 2 = BF16 (exact widening).
 int launch_dequantize(int qtype, const void* in, uint64_t n_values, float* out, cudaStream_t s, bool pdl = false);
+// Per-row reconstruction statistics of a quantized [rows][cols] matrix against its FP32
+// source (the writer's rel_rmse / max_abs_err, src/quantizer.cpp:131-147).
+int launch_quant_stats(int qtype, const float* src, const uint8_t* q, uint64_t rows, uint64_t cols, double* sse,
+                       double* ref, double* mx, cudaStream_t s);
 // Row lookup (embedding): row *d_r (or r_host when d_r is null) of W as FP32.
 int launch_row_f32(int qtype, const uint8_t* W, uint64_t rows, uint64_t cols, const int32_t* d_r, uint64_t r_host,
                    float* out, cudaStream_t s, bool pdl = false);

@@ -171,6 +171,23 @@ int efg_host_matvec_static(int qtype, float* y, const uint8_t* W, const float* x
  * EFG_EFORMAT with the reference's message on the same faults. */
 int efg_efq_check(const void* data, uint64_t size);
 
+typedef struct {
+  uint64_t file_bytes, bytes_per_token, source_tensor_bytes;
+  int64_t override_extra_bytes; /* tensor bytes the overrides add versus the uniform policy */
+  int32_t n_tensors;
+  double seconds;
+} efg_quantize_report;
+
+/* Writes the .efq of a model directory (config.json + model.safetensors with BF16, F16 or
+ * F32 tensors), quantizing on the GPU. Byte-identical to ef::quantize_model
+ * (src/quantizer.cpp:151-290) for the same policy: `overrides` ("TENSOR=TYPE,...", or
+ * "none"; ef::parse_overrides, src/qfile.cpp:94-115) when non-empty, else the named policy
+ * `policy` ("auto", "uniform", "tinyllama-1.1b-chat-v1.0"; ef::select_policy,
+ * src/quantizer.cpp:92-115). `report` may be NULL. EFG_EFORMAT for a checkpoint that does
+ * not match its config, EFG_EINVAL for a bad policy or override. */
+int efg_quantize_model(const char* model_dir, const char* out_file, const char* policy, const char* overrides,
+                       efg_quantize_report* report);
+
 typedef struct efg_decoder efg_decoder;
 
 typedef struct {

@@ -73,3 +73,26 @@ def rel_dot_errors(oracle, qtype, W: np.ndarray, x: np.ndarray, rows: int, got: 
     """|got - exact| / sum|w x| per row (tests/test_qinfer.cpp:58-67 in the reference)."""
     exact, mag = oracle.exact_dots(qtype, W, x, rows)
     return np.abs(got.astype(np.float64) - exact) / np.maximum(mag, 1e-30)
+
+
+@pytest.fixture(scope="session")
+def tinyllama():
+    """A random TinyLlama-1.1B-shaped checkpoint (seed 0, BF16) and the reference's own .efq
+    of it (quantize_model, policy auto = the TinyLlama recipe). Cached across sessions in
+    $EFG_TEST_CACHE (default: the system temp directory). Returns (model_dir, efq_path)."""
+    import os
+    import tempfile
+
+    from edgeforge_b200 import synthetic
+    from oracle.oracle import REF_SO, Reference
+
+    if not REF_SO.exists():
+        pytest.fail("oracle/_ref/libefref.so is not built (make -C oracle)")
+    d = Path(os.environ.get("EFG_TEST_CACHE", tempfile.gettempdir())) / "efg_tinyllama_seed0"
+    efq = d / "model-auto.efq"
+    if not efq.exists():
+        synthetic.write_checkpoint(d, synthetic.TINYLLAMA, seed=0)
+        part = d / "model-auto.efq.part"
+        Reference().quantize_model(d, part, policy="auto")
+        part.rename(efq)
+    return d, efq

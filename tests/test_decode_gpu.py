@@ -10,14 +10,12 @@ absolute at every step.
 from __future__ import annotations
 
 import os
-import tempfile
 from pathlib import Path
 
 import numpy as np
 import pytest
 
 import edgeforge_b200 as efg
-from edgeforge_b200 import synthetic
 
 pytestmark = pytest.mark.gpu
 
@@ -117,27 +115,8 @@ FULL_PROMPT = 23
 FULL_STEPS = 32
 
 
-def _full_model_dir() -> Path:
-    return Path(os.environ.get("EFG_TEST_CACHE", tempfile.gettempdir())) / "efg_tinyllama_seed0"
-
-
-@pytest.fixture(scope="module")
-def full_model():
-    from oracle.oracle import REF_SO, Reference
-
-    if not REF_SO.exists():
-        pytest.fail("oracle/_ref/libefref.so is not built (make -C oracle)")
-    d = _full_model_dir()
-    efq = d / "model-auto.efq"
-    if not efq.exists():
-        synthetic.write_checkpoint(d, synthetic.TINYLLAMA, seed=0)
-        tmp = d / "model-auto.efq.part"
-        Reference().quantize_model(d, tmp, policy="auto")
-        tmp.rename(efq)
-    return efq
-
-
-def test_full_tinyllama_decode(full_model):
+def test_full_tinyllama_decode(tinyllama):
+    full_model = tinyllama[1]
     from oracle.oracle import Reference
 
     ref = Reference()
