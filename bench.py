@@ -290,6 +290,7 @@ def run_ours(args):
     del W4
 
     dec = decode_extra(hbm_peak, with_cpu=not args.no_cpu_baseline) if world == 1 and not args.no_decode else None
+    shard = None if args.no_sharded else sharded_extra(torch, efg, world, rank, hbm_peak)
 
     # DRAM bytes per launch of this kernel from the committed ncu capture summary
     traffic = None
@@ -324,7 +325,8 @@ def run_ours(args):
             "extra": {"config0_q4_0_matvec_5632x2048": {
                 "gbs": round(gbs4, 1), "frac_of_hbm": round(gbs4 / hbm_peak, 4), "us_per_launch": round(ms4 * 1e3, 3),
                 "bytes_per_launch": algo_bytes(Q4_0, q4_rows, q4_cols), "copies": q4_copies},
-                "config2_decode_tinyllama": dec},
+                "config2_decode_tinyllama": dec,
+                "config4_sharded_q4_0_131072x8192": shard},
         }
         print(json.dumps(line))
     if world > 1:
@@ -400,6 +402,56 @@ def decode_extra(hbm_peak, with_cpu, prompt_len=23, steps=32, reps=5):
     return out
 
 
+def sharded_extra(torch, efg, world, rank, hbm_peak, steps=200, warmup=10, rows=131072, cols=8192):
+    """Config 4: the Q4_0 131072 x 8192 matvec (604 MB) row-sharded over the job's GPUs, y
+    all-gathered over NVLink every step (efg_matvec_sharded). Strong scaling: the matrix is
+    fixed, each rank holds rows/world of it. Device time of `steps` steps, max over ranks."""
+    b, c = efg.shard_rows(rows, world, rank)
+    rb = cols // 32 * 18
+    W = torch.empty(max(c, 1) * rb, dtype=torch.uint8, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    for r0 in range(0, c, 8192):  # quantize the shard in 8192-row pieces (bounded FP32 temp)
+        n = min(8192, c - r0)
+        X = torch.randn(n, cols, generator=g, device="cuda") * 0.02
+        efg.quantize_rows(Q4_0, X, n, cols, W[r0 * rb:], True)
+    del X
+    x = torch.randn(cols, generator=torch.Generator(device="cuda").manual_seed(5), device="cuda")
+    y = torch.empty(rows, device="cuda")
+    comm = efg.Comm.from_torch() if world > 1 else efg.Comm(efg.Comm.unique_id(), 1, 0)
+
+    def timed(fn, n):
+        for _ in range(warmup):
+            fn()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(n):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        ms = s0.elapsed_time(s1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms / n
+
+    ms_all = timed(lambda: efg.matvec_sharded(Q4_0, y, W, x, rows, cols, comm), steps)
+    ms_local = timed(lambda: efg.matvec(Q4_0, y[b:], W, x, c, cols), steps)
+    comm.close()
+    assert efg.device_error() == 0
+    total = rows * rb + 4 * cols + 4 * rows
+    shard_bytes = c * rb + 4 * cols + 4 * c
+    del W
+    return {"us_per_step": round(ms_all * 1e3, 3), "gbs_total": round(total / (ms_all / 1e3) / 1e9, 1),
+            "local_matvec_us": round(ms_local * 1e3, 3),
+            "local_frac_of_hbm": round(shard_bytes / (ms_local / 1e3) / 1e9 / hbm_peak, 4),
+            "gather_bytes": 4 * rows, "ranks": world, "rows_per_rank": c, "matrix_bytes": rows * rb,
+            "scaling": "strong"}
+
+
 def run_profile(args):
     """A few plain launches of one matvec, for ncu (no graphs, no CPU legs):
     --profile q8  -> config 1 (Q8_0 32000x2048), --profile q4 -> config 0 (Q4_0 5632x2048),
@@ -432,6 +484,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode measurement")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the config-4 sharded matvec measurement")
     ap.add_argument("--profile", choices=["q8", "q4", "q4big"], help="a few plain launches for ncu")
     args = ap.parse_args()
     if args.profile:

@@ -6,6 +6,7 @@ include/efg.h); this package is the Python mirror of the reference's kernel API 
 from ._lib import EdgeForgeError, LIB_PATH, load  # noqa: F401
 from .api import (  # noqa: F401
     BLOCK_BYTES,
+    Comm,
     Decoder,
     GreedyResult,
     QK,
@@ -27,12 +28,14 @@ from .api import (  # noqa: F401
     matvec_jobs,
     matvec_q4_0,
     matvec_q8_0,
+    matvec_sharded,
     quantize_model,
     quantize_row,
     quantize_rows,
     row_bytes,
     row_f32,
     set_weight_prefetch,
+    shard_rows,
 )
 
 __version__ = "0.1.0"

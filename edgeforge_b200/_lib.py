@@ -70,6 +70,11 @@ SIGNATURES = {
     "efg_host_unregister_weights": (_i, [_vp]),
     "efg_host_release_weights": (_i, []),
     "efg_host_matvec_static": (_i, [_i, _vp, _vp, _vp, _sz, _sz]),
+    "efg_shard_rows": (_i, [_sz, _i, _i, C.POINTER(_sz), C.POINTER(_sz)]),
+    "efg_comm_unique_id": (_i, [_vp]),
+    "efg_comm_init": (_i, [_vp, _i, _i, C.POINTER(_vp)]),
+    "efg_comm_destroy": (_i, [_vp]),
+    "efg_matvec_sharded": (_i, [_i, _vp, _vp, _vp, _sz, _sz, _vp, _vp]),
     "efg_efq_check": (_i, [_vp, _u64]),
     "efg_quantize_model": (_i, [C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(QuantizeReport)]),
     "efg_decoder_open": (_i, [C.c_char_p, _sz, C.POINTER(_vp)]),

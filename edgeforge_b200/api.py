@@ -197,6 +197,63 @@ def host_matvec_static(qtype: int, W: np.ndarray, x: np.ndarray, rows: int) -> n
     return y
 
 
+# ---------------------------------------------------------------- row-sharded matvec
+
+
+def shard_rows(rows: int, nranks: int, rank: int) -> tuple[int, int]:
+    """(begin, count) of rank's contiguous rows (ef::ThreadPool::chunk_begin split)."""
+    b, c = C.c_size_t(0), C.c_size_t(0)
+    check(load().efg_shard_rows(int(rows), int(nranks), int(rank), C.byref(b), C.byref(c)))
+    return b.value, c.value
+
+
+class Comm:
+    """The library's NCCL communicator over the GPUs of one node (efg_comm_*)."""
+
+    ID_BYTES = 128
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_uint8 * Comm.ID_BYTES)()
+        check(load().efg_comm_unique_id(C.cast(buf, C.c_void_p)))
+        return bytes(buf)
+
+    def __init__(self, uid: bytes, nranks: int, rank: int):
+        if len(uid) != Comm.ID_BYTES:
+            raise EdgeForgeError(1, "a communicator id is 128 bytes")
+        buf = (C.c_uint8 * Comm.ID_BYTES).from_buffer_copy(uid)
+        h = C.c_void_p(0)
+        check(load().efg_comm_init(C.cast(buf, C.c_void_p), int(nranks), int(rank), C.byref(h)))
+        self._h, self.nranks, self.rank = h, nranks, rank
+
+    @classmethod
+    def from_torch(cls, group=None) -> "Comm":
+        """Every rank of a torch.distributed group joins one communicator (the id goes from
+        rank 0 to the others through the group)."""
+        import torch.distributed as dist
+
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        obj = [cls.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        return cls(obj[0], world, rank)
+
+    @property
+    def handle(self) -> C.c_void_p:
+        return self._h
+
+    def close(self) -> None:
+        if self._h:
+            check(load().efg_comm_destroy(self._h))
+            self._h = C.c_void_p(0)
+
+
+def matvec_sharded(qtype: int, y, W_shard, x, rows: int, cols: int, comm: Comm) -> None:
+    """Row-sharded matvec: W_shard = this rank's rows (shard_rows) of the packed [rows][cols]
+    matrix; y (rows floats) receives the full result on every rank."""
+    check(load().efg_matvec_sharded(int(qtype), _ptr(y), _ptr(W_shard), _ptr(x), rows, cols, comm.handle,
+                                    _stream()))
+
+
 # ---------------------------------------------------------------- .efq and the decode step
 
 

@@ -141,7 +141,7 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
 }
 
 // Global -> this CTA's shared memory, completion signalled on `bar` as tx bytes.
-// dst, src and bytes must all be multiples of 16. No multicast.
+// dst, src and bytes must all be multiples of 16. The copy lands in this CTA only.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(

@@ -1,0 +1,186 @@
+// efg_shard.cpp - the row-sharded packed matvec across the GPUs of one node.
+//
+// Rank r of n holds the contiguous rows [rows*r/n, rows*(r+1)/n) of W (the split of the
+// reference's ThreadPool::chunk_begin, include/ef/threadpool.h:52-54), computes that slice of
+// y into its place in a full-size y, and the slices are exchanged in place over NVLink:
+// one ncclAllGather when every rank holds the same number of rows, else one grouped
+// ncclBroadcast per rank. The communicator is the library's own (ncclCommInitRank from a
+// unique id the caller distributes); NCCL is loaded with dlopen on first use, so the
+// library has no link-time NCCL dependency and shares the NCCL already loaded in the
+// process (e.g. by torch) when there is one.
+#include <dlfcn.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include "../../include/efg.h"
+#include "efg_host.h"
+#include "efg_matvec.cuh"
+
+namespace efg {
+namespace {
+
+struct Nccl {
+  bool tried = false, ok = false;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*group_start)() = nullptr;
+  ncclResult_t (*group_end)() = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+Nccl g_nccl;
+std::mutex g_nccl_mu;
+
+template <class F>
+bool sym(void* h, const char* name, F& f) {
+  f = reinterpret_cast<F>(dlsym(h, name));
+  return f != nullptr;
+}
+
+int load_nccl(Nccl** out) {
+  std::lock_guard<std::mutex> lk(g_nccl_mu);
+  if (!g_nccl.tried) {
+    g_nccl.tried = true;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);  // the process's NCCL, if loaded
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (h) {
+      g_nccl.ok = sym(h, "ncclGetUniqueId", g_nccl.get_unique_id) && sym(h, "ncclCommInitRank", g_nccl.comm_init_rank) &&
+                  sym(h, "ncclCommDestroy", g_nccl.comm_destroy) && sym(h, "ncclAllGather", g_nccl.all_gather) &&
+                  sym(h, "ncclBroadcast", g_nccl.broadcast) && sym(h, "ncclGroupStart", g_nccl.group_start) &&
+                  sym(h, "ncclGroupEnd", g_nccl.group_end) && sym(h, "ncclGetErrorString", g_nccl.error_string);
+    }
+  }
+  if (!g_nccl.ok) return fail(EFG_ENCCL, "NCCL (libnccl.so.2) could not be loaded");
+  *out = &g_nccl;
+  return EFG_OK;
+}
+
+int nccl_check(Nccl* n, ncclResult_t r, const char* what) {
+  if (r == ncclSuccess) return EFG_OK;
+  return fail(EFG_ENCCL, "%s: %s", what, n->error_string ? n->error_string(r) : "NCCL error");
+}
+
+}  // namespace
+}  // namespace efg
+
+struct efg_comm {
+  ncclComm_t comm = nullptr;
+  int nranks = 0, rank = 0, device = -1;
+};
+
+using efg::fail;
+
+extern "C" {
+
+int efg_shard_rows(size_t rows, int nranks, int rank, size_t* begin, size_t* count) {
+  if (nranks < 1 || rank < 0 || rank >= nranks || !begin || !count)
+    return fail(EFG_EINVAL, "shard_rows: bad rank %d of %d", rank, nranks);
+  const uint64_t b = static_cast<uint64_t>(rows) * static_cast<uint64_t>(rank) / static_cast<uint64_t>(nranks);
+  const uint64_t e = static_cast<uint64_t>(rows) * static_cast<uint64_t>(rank + 1) / static_cast<uint64_t>(nranks);
+  *begin = static_cast<size_t>(b);
+  *count = static_cast<size_t>(e - b);
+  return EFG_OK;
+}
+
+int efg_comm_unique_id(void* id) {
+  if (!id) return fail(EFG_EINVAL, "comm_unique_id: null buffer");
+  efg::Nccl* n = nullptr;
+  if (int st = efg::load_nccl(&n)) return st;
+  ncclUniqueId u;
+  if (int st = efg::nccl_check(n, n->get_unique_id(&u), "ncclGetUniqueId")) return st;
+  std::memcpy(id, &u, sizeof u);
+  return EFG_OK;
+}
+
+int efg_comm_init(const void* id, int nranks, int rank, efg_comm** out) {
+  if (!id || !out) return fail(EFG_EINVAL, "comm_init: null argument");
+  *out = nullptr;
+  if (nranks < 1 || rank < 0 || rank >= nranks) return fail(EFG_EINVAL, "comm_init: bad rank %d of %d", rank, nranks);
+  efg::Nccl* n = nullptr;
+  if (int st = efg::load_nccl(&n)) return st;
+  auto* c = new efg_comm;
+  c->nranks = nranks;
+  c->rank = rank;
+  if (cudaGetDevice(&c->device) != cudaSuccess) {
+    delete c;
+    return fail(EFG_ECUDA, "comm_init: no current device");
+  }
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof u);
+  if (int st = efg::nccl_check(n, n->comm_init_rank(&c->comm, nranks, u, rank), "ncclCommInitRank")) {
+    delete c;
+    return st;
+  }
+  *out = c;
+  return EFG_OK;
+}
+
+int efg_comm_destroy(efg_comm* c) {
+  if (!c) return EFG_OK;
+  efg::Nccl* n = nullptr;
+  int st = EFG_OK;
+  if (c->comm && efg::load_nccl(&n) == EFG_OK) st = efg::nccl_check(n, n->comm_destroy(c->comm), "ncclCommDestroy");
+  delete c;
+  return st;
+}
+
+int efg_matvec_sharded(int qtype, float* d_y, const uint8_t* d_W_shard, const float* d_x, size_t rows, size_t cols,
+                       efg_comm* comm, void* stream) {
+  using namespace efg;
+  if (!comm || !comm->comm) return fail(EFG_EINVAL, "matvec_sharded: null communicator");
+  if (qtype != EFG_Q4_0 && qtype != EFG_Q8_0)
+    return fail(EFG_EINVAL, "matvec_sharded: type %d is not a packed type (Q4_0, Q8_0)", qtype);
+  if (cols % 32 != 0)
+    return fail(EFG_EINVAL, "%s needs a row length divisible by 32, got %zu", qtype == EFG_Q4_0 ? "Q4_0" : "Q8_0",
+                cols);
+  if (rows >= (1ull << 31)) return fail(EFG_EINVAL, "matvec_sharded: too many rows");
+  int dev = -1;
+  EFG_TRY_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != comm->device)
+    return fail(EFG_EINVAL, "matvec_sharded: current device %d is not the communicator's device %d", dev,
+                comm->device);
+  if (rows == 0) return EFG_OK;
+  if (!d_y) return fail(EFG_EINVAL, "matvec_sharded: null y");
+  size_t b = 0, cnt = 0;
+  if (int st = efg_shard_rows(rows, comm->nranks, comm->rank, &b, &cnt)) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  if (cnt) {
+    DeviceInfo* di = current_device();
+    if (!di) return EFG_ECUDA;
+    MatvecArgs a;
+    a.fmt = qtype == EFG_Q4_0 ? Fmt::Q4 : Fmt::Q8;
+    a.x = d_x;
+    a.cols = cols;
+    a.pdl = weight_prefetch_flag();
+    a.n_jobs = 1;
+    a.jobs[0] = MatvecJobDev{d_W_shard, d_y + b, static_cast<uint32_t>(cnt), 0};
+    if (int st = launch_matvec(a, di->d_err, s)) return st;
+  }
+  if (comm->nranks == 1) return EFG_OK;
+  Nccl* n = nullptr;
+  if (int st = load_nccl(&n)) return st;
+  if (rows % static_cast<size_t>(comm->nranks) == 0)  // in-place all-gather: send buffer = own slot
+    return nccl_check(n, n->all_gather(d_y + b, d_y, cnt, ncclFloat32, comm->comm, s), "ncclAllGather");
+  if (int st = nccl_check(n, n->group_start(), "ncclGroupStart")) return st;
+  for (int r = 0; r < comm->nranks; ++r) {
+    size_t rb = 0, rc = 0;
+    efg_shard_rows(rows, comm->nranks, r, &rb, &rc);
+    if (rc == 0) continue;
+    const ncclResult_t res = n->broadcast(d_y + rb, d_y + rb, rc, ncclFloat32, r, comm->comm, s);
+    if (res != ncclSuccess) {
+      n->group_end();
+      return nccl_check(n, res, "ncclBroadcast");
+    }
+  }
+  return nccl_check(n, n->group_end(), "ncclGroupEnd");
+}
+
+}  // extern "C"

@@ -163,6 +163,29 @@ int efg_host_release_weights(void);
  * nothing because they run on host memory. */
 int efg_host_matvec_static(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols);
 
+/* ================================================================ row-sharded matvec (several GPUs) */
+
+/* A communicator between the GPUs of one node, one rank per GPU and process (or thread).
+ * The library loads NCCL (libnccl.so.2) on first use. */
+typedef struct efg_comm efg_comm;
+
+/* Rows [*begin, *begin + *count) of a rows-row matrix belong to `rank` of `nranks`: the
+ * contiguous split of ef::ThreadPool::chunk_begin (include/ef/threadpool.h:52-54). */
+int efg_shard_rows(size_t rows, int nranks, int rank, size_t* begin, size_t* count);
+/* Writes a fresh 128-byte NCCL unique id to `id` (made on one rank, given to all). */
+int efg_comm_unique_id(void* id);
+/* Joins the communicator `id` as `rank` of `nranks` on the current device (collective). */
+int efg_comm_init(const void* id, int nranks, int rank, efg_comm** out);
+int efg_comm_destroy(efg_comm* comm);
+/* Row-sharded ef::kern::matvec (qkernels.h:66) for a matrix too large for one GPU's share:
+ * d_W_shard holds this rank's rows (efg_shard_rows) of the full [rows][cols] packed matrix,
+ * d_x the whole x; on return (stream-ordered) d_y holds all `rows` outputs on every rank,
+ * the slices exchanged in place over NVLink (one all-gather, or one broadcast per rank when
+ * the split is uneven). Every rank calls it with the same rows/cols. EFG_ENCCL on a
+ * collective failure. */
+int efg_matvec_sharded(int qtype, float* d_y, const uint8_t* d_W_shard, const float* d_x, size_t rows, size_t cols,
+                       efg_comm* comm, void* stream);
+
 /* ================================================================ .efq and the decode step */
 
 /* Validates an .efq file image in memory: magic, version, JSON header, tensor table (types,

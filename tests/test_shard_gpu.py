@@ -1,0 +1,112 @@
+"""efg_matvec_sharded on the GPU: one rank (the NCCL communicator of a single GPU), and
+two to four ranks, one process per GPU, when the machine has them. Each rank quantizes
+the same seeded matrix on its own GPU (bit-exact quantizer), keeps its row slice, and the
+gathered y must agree with the oracle (|y - exact| / sum|w x| <= 1e-5 per row) and be
+identical on every rank."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import edgeforge_b200 as efg
+from edgeforge_b200 import QType
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def _make(torch, qt, rows, cols, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    X = torch.randn(rows, cols, generator=g, device="cuda") * 0.02
+    rb = cols // 32 * (18 if qt == QType.Q4_0 else 34)
+    W = torch.empty(rows * rb, dtype=torch.uint8, device="cuda")
+    efg.quantize_rows(qt, X, rows, cols, W, True)
+    x = torch.randn(cols, generator=g, device="cuda")
+    return W.view(rows, rb), x
+
+
+def _check(oracle, qt, W, x, y, rows):
+    from conftest import rel_dot_errors
+
+    err = rel_dot_errors(oracle, qt, W.cpu().numpy(), x.cpu().numpy(), rows, y.cpu().numpy())
+    assert err.max() <= TOL, err.max()
+
+
+def test_single_rank(cuda, oracle):
+    import torch
+
+    comm = efg.Comm(efg.Comm.unique_id(), 1, 0)
+    try:
+        for qt, rows, cols in ((QType.Q4_0, 5632, 2048), (QType.Q8_0, 1001, 512)):
+            W, x = _make(torch, qt, rows, cols, 3)
+            y = torch.full((rows,), float("nan"), device="cuda")
+            efg.matvec_sharded(qt, y, W, x, rows, cols, comm)
+            ref = torch.empty(rows, device="cuda")
+            efg.matvec(qt, ref, W, x, rows, cols)
+            torch.cuda.synchronize()
+            assert torch.equal(y, ref)
+            _check(oracle, qt, W, x, y, rows)
+        with pytest.raises(efg.EdgeForgeError, match="divisible by 32"):
+            efg.matvec_sharded(QType.Q4_0, y, W, x, rows, 30, comm)
+    finally:
+        comm.close()
+    assert efg.device_error() == 0
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, cases, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    comm = efg.Comm.from_torch()
+    try:
+        for i, (qt, rows, cols) in enumerate(cases):
+            W, x = _make(torch, qt, rows, cols, 11)
+            b, c = efg.shard_rows(rows, world, rank)
+            shard = W[b:b + c].contiguous()
+            y = torch.full((rows,), float("nan"), device="cuda")
+            efg.matvec_sharded(qt, y, shard, x, rows, cols, comm)
+            torch.cuda.synchronize()
+            np.save(os.path.join(out_dir, f"y{i}_{rank}.npy"), y.cpu().numpy())
+            if rank == 0:
+                np.save(os.path.join(out_dir, f"W{i}.npy"), W.cpu().numpy())
+                np.save(os.path.join(out_dir, f"x{i}.npy"), x.cpu().numpy())
+        assert efg.device_error() == 0
+    finally:
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_multi_rank(tmp_path, oracle):
+    import torch
+    import torch.multiprocessing as mp
+
+    n = min(torch.cuda.device_count(), 4)
+    if n < 2:
+        pytest.skip("needs two GPUs")
+    cases = [(QType.Q4_0, 16384, 8192), (QType.Q4_0, 1001, 256), (QType.Q8_0, 4099, 2048)]
+    mp.start_processes(_rank_main, args=(n, _free_port(), cases, str(tmp_path)), nprocs=n, join=True,
+                       start_method="spawn")
+    from conftest import rel_dot_errors
+
+    for i, (qt, rows, cols) in enumerate(cases):
+        ys = [np.load(tmp_path / f"y{i}_{r}.npy") for r in range(n)]
+        for y in ys[1:]:
+            np.testing.assert_array_equal(y, ys[0])
+        W, x = np.load(tmp_path / f"W{i}.npy"), np.load(tmp_path / f"x{i}.npy")
+        err = rel_dot_errors(oracle, qt, W, x, rows, ys[0])
+        assert err.max() <= TOL, (i, err.max())
