@@ -197,6 +197,16 @@ def host_matvec_static(qtype: int, W: np.ndarray, x: np.ndarray, rows: int) -> n
     return y
 
 
+# ---------------------------------------------------------------- batched GEMM
+
+
+def gemm_q4_0(Y, W, X, M: int, K: int, B: int) -> None:
+    """Y[b][m] = sum_k W[m][k] X[b][k] on the tensor cores: W packed Q4_0 [M] rows, X FP32
+    [B][K], Y FP32 [B][M] (CUDA tensors). Each column equals ef::kern::matvec of that
+    column within 1e-5 of sum|w x|."""
+    check(load().efg_gemm_q4_0(_ptr(Y), _ptr(W), _ptr(X), M, K, B, _stream()))
+
+
 # ---------------------------------------------------------------- row-sharded matvec
 
 

@@ -163,6 +163,16 @@ int efg_host_release_weights(void);
  * nothing because they run on host memory. */
 int efg_host_matvec_static(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols);
 
+/* ================================================================ batched GEMM (tensor cores) */
+
+/* Y[b][m] = sum_k W[m][k] X[b][k] for b < B: the matvec of every column of a batch at once,
+ * on the tcgen05 tensor cores (W dequantized to an exact BF16 hi+lo pair, X split into two
+ * BF16 parts, FP32 accumulation in TMEM). Layout: W packed Q4_0 [M] rows, X FP32 [B][K]
+ * (each column contiguous, 16-byte aligned), Y FP32 [B][M]. The reference has no GEMM; it
+ * runs ef::kern::matvec (qkernels.h:66) once per column, which each Y column matches
+ * within 1e-5 of sum|w x|. */
+int efg_gemm_q4_0(float* d_Y, const uint8_t* d_W, const float* d_X, size_t M, size_t K, size_t B, void* stream);
+
 /* ================================================================ row-sharded matvec (several GPUs) */
 
 /* A communicator between the GPUs of one node, one rank per GPU and process (or thread).
