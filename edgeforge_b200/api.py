@@ -331,6 +331,16 @@ class Decoder:
         """ef::Model::weight_bytes_per_token (src/qfile.cpp:237-241)."""
         return int(self.info.bytes_per_token)
 
+    @property
+    def persistent(self) -> bool:
+        """True when the decode step runs as one persistent kernel; False (the default): a CUDA
+        graph of one kernel per operation."""
+        return load().efg_decoder_mode(self._h) == 1
+
+    @persistent.setter
+    def persistent(self, on: bool) -> None:
+        check(load().efg_decoder_set_mode(self._h, int(bool(on))))
+
     def reset(self) -> None:
         check(load().efg_decoder_reset(self._h))
 

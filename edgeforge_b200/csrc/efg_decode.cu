@@ -30,6 +30,7 @@
 #include "efg_efq.h"
 #include "efg_host.h"
 #include "efg_matvec.cuh"
+#include "efg_decode_mk.cuh"
 
 namespace efg {
 namespace {
@@ -291,6 +292,15 @@ struct Decoder {
   int n_q4 = 0, n_q8 = 0;
   cudaGraphExec_t g_full = nullptr, g_prefill = nullptr;
   int* d_err = nullptr;
+  // persistent decode kernel (efg_decode_mk.cuh)
+  bool mk_ok = false, use_mk = false;
+  std::string mk_why;  // why the persistent kernel cannot run this model (when !mk_ok)
+  mk::Phase* d_phases = nullptr;  // one token's phases
+  uint32_t n_phases = 0;
+  unsigned* d_bar = nullptr;      // [0] barrier counter, then ctl[2] as int32
+  float* d_keep = nullptr;        // per-step logits kept by generate
+  size_t keep_cap = 0;
+  int grid = 0;
   int32_t* pos_p() const { return state; }
   int32_t* nfix_p() const { return state + 1; }
   int32_t* tokens() const { return state + 2; }
@@ -468,6 +478,187 @@ int capture(Decoder& D, bool logits, cudaGraphExec_t* out) {
   return EFG_OK;
 }
 
+// ---------------------------------------------------------------- persistent kernel setup
+
+// Rows per batch and per tile of one matrix in the persistent kernel: 4 rows per batch
+// (2 for long Q8_0 rows), and as many batches per tile as one ring slot holds.
+bool mk_job(const Mat& m, float* y, uint32_t y_pos_stride, mk::Job& J) {
+  J.W = m.w;
+  J.y = y;
+  J.rows = m.rows;
+  J.rb = m.cols / 32 * (m.type == 4 ? 18 : 34);
+  J.y_pos_stride = y_pos_stride;
+  J.fmt = static_cast<uint32_t>(m.type);
+  if (J.rb % 16 != 0 || reinterpret_cast<uintptr_t>(m.w) % 16 != 0) return false;
+  // 2 rows per batch: the unrolled per-row code of one batch is what every phase runs
+  // once or twice, so it is kept small enough to stay in the instruction cache
+  J.RB = 2;
+  if (J.RB * J.rb > mk::kSlotBytes) return false;
+  // as many batches per tile as one ring slot holds (at most kMaxBatches): large bulk copies
+  // keep ~180 KB in flight per SM; the batches of a tile go to different warps
+  const uint32_t max_batches = std::min<uint32_t>(mk::kMaxBatches, mk::kSlotBytes / (J.RB * J.rb));
+  J.TR = J.RB * max_batches;
+  return true;
+}
+
+int build_mk(Decoder& D) {
+  const efq::Config& c = D.c;
+  D.mk_ok = false;
+  DeviceInfo* dev = current_device();
+  if (!dev) return EFG_ECUDA;
+  int coop = 0;
+  cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev->device);
+  auto no = [&](const char* why) {
+    D.mk_why = why;
+    return EFG_OK;
+  };
+  if (!coop) return no("the device has no cooperative launch");
+  if (dev->smem_optin < mk::smem_bytes()) return no("not enough shared memory per block");
+  if ((2 + mk::kAttnChunk) * static_cast<size_t>(c.head_dim) + D.max_seq > mk::kXsFloats)
+    return no("max_seq too long for the attention scratch");
+  if (c.hidden % 64 != 0 || c.intermediate % 64 != 0 || c.hidden / 64 > static_cast<int64_t>(mk::kMaxSlotsX) ||
+      c.intermediate / 64 > static_cast<int64_t>(mk::kMaxSlotsX))
+    return no("hidden and intermediate sizes must be multiples of 64 up to 6144");
+  EFG_TRY_CUDA(cudaFuncSetAttribute(mk::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(mk::smem_bytes())),
+               "decode kernel attribute");
+  int per_sm = 0;
+  EFG_TRY_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mk::decode_kernel, mk::kThreads, mk::smem_bytes()),
+               "decode kernel occupancy");
+  if (per_sm < 1) return no("the decode kernel does not fit on an SM");
+  const uint32_t grid = static_cast<uint32_t>(dev->sm_count);
+  D.grid = static_cast<int>(grid);
+  const uint32_t Dm = static_cast<uint32_t>(c.hidden), F = static_cast<uint32_t>(c.intermediate),
+                 kvd = static_cast<uint32_t>(c.kv_dim());
+  auto gof = [](uint32_t cols) { return (cols / 64 + 31) / 32; };
+  if (gof(Dm) > 3 || gof(F) > 3) return no("rows longer than 6144 columns");
+  auto mv = [&](uint32_t epi, uint32_t in_mode, const float* x, const float* x2, const float* nw, uint32_t cols) {
+    mk::Phase P{};
+    P.kind = mk::kMatvec;
+    P.epi = epi;
+    P.in_mode = in_mode;
+    P.x = x;
+    P.x2 = x2;
+    P.norm_w = nw;
+    P.cols = cols;
+    P.G = gof(cols);
+    return P;
+  };
+  std::vector<mk::Phase> full;
+  bool fit = true;
+  mk::Phase e{};
+  e.kind = mk::kEmbed;
+  full.push_back(e);
+  for (size_t l = 0; l < D.layers.size(); ++l) {
+    const Layer& Ly = D.layers[l];
+    float* vl = D.vc + l * D.max_seq * kvd;
+    mk::Phase qkv = mv(0, mk::kInNorm, D.x, nullptr, Ly.attn_norm, Dm);
+    const uint32_t rg = mk::kConsumerWarps / qkv.G;
+    qkv.n_jobs = 3;
+    fit = fit && mk_job(Ly.q, D.q, 0, qkv.jobs[0]) && mk_job(Ly.k, D.knew, 0, qkv.jobs[1]) &&
+          mk_job(Ly.v, vl, kvd, qkv.jobs[2]);
+    (void)rg;
+    full.push_back(qkv);
+    mk::Phase at{};
+    at.kind = mk::kAttn;
+    at.layer = static_cast<uint32_t>(l);
+    full.push_back(at);
+    mk::Phase o = mv(1, mk::kInPlain, D.ctx, nullptr, nullptr, Dm);
+    o.n_jobs = 1;
+    fit = fit && mk_job(Ly.o, D.x, 0, o.jobs[0]);
+    full.push_back(o);
+    mk::Phase gu = mv(0, mk::kInNorm, D.x, nullptr, Ly.ffn_norm, Dm);
+    gu.n_jobs = 2;
+    fit = fit && mk_job(Ly.gate, D.gate, 0, gu.jobs[0]) && mk_job(Ly.up, D.up, 0, gu.jobs[1]);
+    full.push_back(gu);
+    mk::Phase dn = mv(1, mk::kInSwiGLU, D.gate, D.up, nullptr, F);
+    dn.n_jobs = 1;
+    fit = fit && mk_job(Ly.down, D.x, 0, dn.jobs[0]);
+    full.push_back(dn);
+  }
+  mk::Phase lm = mv(0, mk::kInNorm, D.x, nullptr, D.final_norm, Dm);
+  lm.n_jobs = 1;
+  fit = fit && mk_job(D.lm_head, nullptr, 0, lm.jobs[0]);  // y: the launch's logits
+  full.push_back(lm);
+  mk::Phase am{};
+  am.kind = mk::kArgmax;
+  full.push_back(am);
+  if (!fit) return no("a matrix's rows are not 16-byte multiples");
+  if (full.size() > mk::kMaxPhases) return no("too many layers for the persistent kernel's phase list");
+  D.n_phases = static_cast<uint32_t>(full.size());
+  EFG_TRY_CUDA(cudaMalloc(&D.d_phases, full.size() * sizeof(mk::Phase)), "phase table allocation");
+  EFG_TRY_CUDA(cudaMemcpy(D.d_phases, full.data(), full.size() * sizeof(mk::Phase), cudaMemcpyHostToDevice),
+               "phase table upload");
+  EFG_TRY_CUDA(cudaMalloc(&D.d_bar, 16), "barrier allocation");
+  D.mk_ok = true;
+  return EFG_OK;
+}
+
+int32_t* mk_ctl(Decoder& D) { return reinterpret_cast<int32_t*>(D.d_bar + 1); }
+
+// One launch of the persistent kernel: n_pre steps without logits, then n_full steps with
+// logits and argmax (kept per step at `keep` when not null), stopping after `eos`.
+int launch_mk(Decoder& D, uint32_t n_pre, uint32_t n_full, float* keep, int32_t eos) {
+  if (n_pre + n_full == 0) return EFG_OK;
+  EFG_TRY_CUDA(cudaMemsetAsync(D.d_bar, 0, 16, D.stream), "barrier reset");
+  mk::Params p{};
+  p.phases = D.d_phases;
+  p.n_phases = D.n_phases;
+  p.n_prefill_steps = n_pre;
+  p.n_full_steps = n_full;
+  p.embed = D.embed.w;
+  p.embed_type = D.embed.type;
+  p.vocab = static_cast<uint32_t>(D.c.vocab);
+  p.dim = static_cast<uint32_t>(D.c.hidden);
+  p.H = static_cast<uint32_t>(D.c.heads);
+  p.KV = static_cast<uint32_t>(D.c.kv_heads);
+  p.hd = static_cast<uint32_t>(D.c.head_dim);
+  p.max_seq = static_cast<uint32_t>(D.max_seq);
+  p.kc = D.kc;
+  p.vc = D.vc;
+  p.rcos = D.rcos;
+  p.rsin = D.rsin;
+  p.q = D.q;
+  p.knew = D.knew;
+  p.ctx = D.ctx;
+  p.x = D.x;
+  p.logits = keep ? keep : D.logits;
+  p.logits_step_stride = keep ? static_cast<uint32_t>(D.c.vocab) : 0;
+  p.eps = static_cast<float>(D.c.rms_eps);
+  p.pos = D.pos_p();
+  p.n_fixed = D.nfix_p();
+  p.tokens = D.tokens();
+  p.out_tokens = D.out_tokens();
+  p.eos = eos;
+  p.ctl = mk_ctl(D);
+  p.bar = D.d_bar;
+  p.err = D.d_err;
+  cudaLaunchConfig_t cf{};
+  cf.gridDim = dim3(static_cast<unsigned>(D.grid));
+  cf.blockDim = dim3(mk::kThreads);
+  cf.dynamicSmemBytes = mk::smem_bytes();
+  cf.stream = D.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cf.attrs = attr;
+  cf.numAttrs = 1;
+  EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, mk::decode_kernel, p), "decode kernel launch");
+  return EFG_OK;
+}
+
+int device_status(Decoder& D) {
+  int e = 0;
+  EFG_TRY_CUDA(cudaMemcpyAsync(&e, D.d_err, sizeof e, cudaMemcpyDeviceToHost, D.stream), "error word read");
+  EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+  if (e != 0) {
+    cudaMemsetAsync(D.d_err, 0, sizeof(int), D.stream);
+    cudaStreamSynchronize(D.stream);
+    return fail(e, "decode: the device reported %s", efg_status_string(e));
+  }
+  return EFG_OK;
+}
+
 void destroy(Decoder* D) {
   if (!D) return;
   if (D->stream) cudaStreamSynchronize(D->stream);
@@ -475,7 +666,8 @@ void destroy(Decoder* D) {
   if (D->g_prefill) cudaGraphExecDestroy(D->g_prefill);
   for (void* p : {static_cast<void*>(D->d_data), static_cast<void*>(D->kc), static_cast<void*>(D->vc),
                   static_cast<void*>(D->rcos), static_cast<void*>(D->rsin), static_cast<void*>(D->x),
-                  static_cast<void*>(D->state)})
+                  static_cast<void*>(D->state), static_cast<void*>(D->d_phases), static_cast<void*>(D->d_bar),
+                  static_cast<void*>(D->d_keep)})
     if (p) cudaFree(p);
   if (D->stream) cudaStreamDestroy(D->stream);
   delete D;
@@ -608,6 +800,8 @@ int open_decoder(const char* path, size_t max_seq, Decoder** out) {
   EFG_TRY_CUDA(cudaMemset(D->state, 0, (2 + 2 * max_seq) * sizeof(int32_t)), "state init");
   if (int st = capture(*D, true, &D->g_full)) return st;
   if (int st = capture(*D, false, &D->g_prefill)) return st;
+  if (int st = build_mk(*D)) return st;
+  D->use_mk = false;  // the per-operation graphs are faster today; the persistent kernel is opt-in
   *out = D.release();
   return EFG_OK;
 }
@@ -684,11 +878,16 @@ int efg_decoder_forward(efg_decoder* h, int32_t token, size_t pos, float* logits
   if (pos > D.cached)
     return fail(EFG_ESTATE, "forward: position %zu skips ahead of the %zu cached tokens", pos, D.cached);
   if (int st = efg::set_step(D, token, pos, static_cast<int32_t>(pos + 1))) return st;
-  EFG_TRY_CUDA(cudaGraphLaunch(logits ? D.g_full : D.g_prefill, D.stream), "graph launch");
+  if (D.use_mk) {
+    if (int st = efg::launch_mk(D, logits ? 0 : 1, logits ? 1 : 0, nullptr, -1)) return st;
+  } else {
+    EFG_TRY_CUDA(cudaGraphLaunch(logits ? D.g_full : D.g_prefill, D.stream), "graph launch");
+  }
   if (logits)
     EFG_TRY_CUDA(cudaMemcpyAsync(logits, D.logits, D.c.vocab * sizeof(float), cudaMemcpyDeviceToHost, D.stream),
                  "logits download");
   EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+  if (int st = efg::device_status(D)) return st;
   D.cached = pos + 1;
   return EFG_OK;
 }
@@ -716,6 +915,57 @@ int efg_decoder_generate(efg_decoder* h, const int32_t* prompt, size_t n_prompt,
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
   cudaEventCreate(&e2);
+  if (D.use_mk) {  // two launches of the persistent kernel: the prompt, then the decode loop
+    float* keep = nullptr;
+    if (step_logits && max_new > 1) {
+      const size_t need = (max_new - 1) * static_cast<size_t>(D.c.vocab);
+      if (need > D.keep_cap) {
+        if (D.d_keep) cudaFree(D.d_keep);
+        D.d_keep = nullptr;
+        D.keep_cap = 0;
+        EFG_TRY_CUDA(cudaMalloc(&D.d_keep, need * sizeof(float)), "logits buffer");
+        D.keep_cap = need;
+      }
+      keep = D.d_keep;
+    }
+    cudaEventRecord(e0, D.stream);
+    if (int st = efg::launch_mk(D, static_cast<uint32_t>(n_prompt - 1), 1, nullptr, eos_id)) return st;
+    cudaEventRecord(e1, D.stream);
+    int32_t ctl[2] = {0, 0};
+    EFG_TRY_CUDA(cudaMemcpyAsync(ctl, efg::mk_ctl(D), sizeof ctl, cudaMemcpyDeviceToHost, D.stream), "state read");
+    EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+    if (int st = efg::device_status(D)) return st;
+    size_t n_out = max_new ? 1 : 0;
+    const bool decode = max_new > 1 && ctl[0] == 0;  // no eos straight after the prompt
+    if (decode) {
+      if (int st = efg::launch_mk(D, 0, static_cast<uint32_t>(max_new - 1), keep, eos_id)) return st;
+      EFG_TRY_CUDA(cudaMemcpyAsync(ctl, efg::mk_ctl(D), sizeof ctl, cudaMemcpyDeviceToHost, D.stream), "state read");
+    }
+    cudaEventRecord(e2, D.stream);
+    EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+    if (int st = efg::device_status(D)) return st;
+    if (decode) n_out += static_cast<size_t>(ctl[1]);  // one token per decode step
+    if (n_out)
+      EFG_TRY_CUDA(cudaMemcpyAsync(tokens_out, D.out_tokens() + n_prompt - 1, n_out * sizeof(int32_t),
+                                   cudaMemcpyDeviceToHost, D.stream),
+                   "token download");
+    if (step_logits && n_out > 1)
+      EFG_TRY_CUDA(cudaMemcpyAsync(step_logits, D.d_keep, (n_out - 1) * D.c.vocab * sizeof(float),
+                                   cudaMemcpyDeviceToHost, D.stream),
+                   "logits download");
+    EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+    float ms_pre = 0.f, ms_dec = 0.f;
+    cudaEventElapsedTime(&ms_pre, e0, e1);
+    cudaEventElapsedTime(&ms_dec, e1, e2);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaEventDestroy(e2);
+    if (prefill_seconds) *prefill_seconds = ms_pre / 1e3;
+    if (decode_seconds) *decode_seconds = ms_dec / 1e3;
+    if (n_tokens) *n_tokens = n_out;
+    D.cached = n_prompt + (n_out ? n_out - 1 : 0);
+    return EFG_OK;
+  }
   cudaEventRecord(e0, D.stream);
   for (size_t p = 0; p + 1 < n_prompt; ++p) EFG_TRY_CUDA(cudaGraphLaunch(D.g_prefill, D.stream), "graph launch");
   EFG_TRY_CUDA(cudaGraphLaunch(D.g_full, D.stream), "graph launch");  // last prompt token: logits, next token
@@ -756,6 +1006,20 @@ int efg_decoder_generate(efg_decoder* h, const int32_t* prompt, size_t n_prompt,
   if (n_tokens) *n_tokens = n_out;
   D.cached = n_prompt + (n_out ? n_out - 1 : 0);
   return EFG_OK;
+}
+
+int efg_decoder_set_mode(efg_decoder* h, int persistent) {
+  if (!h) return fail(EFG_EINVAL, "decoder_set_mode: null handle");
+  Decoder& D = *reinterpret_cast<Decoder*>(h);
+  if (persistent && !D.mk_ok)
+    return fail(EFG_EINVAL, "decoder_set_mode: the persistent kernel cannot run this model (%s)", D.mk_why.c_str());
+  D.use_mk = persistent != 0;
+  return EFG_OK;
+}
+
+int efg_decoder_mode(const efg_decoder* h) {
+  if (!h) return -1;
+  return reinterpret_cast<const Decoder*>(h)->use_mk ? 1 : 0;
 }
 
 }  // extern "C"

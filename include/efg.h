@@ -252,6 +252,13 @@ int efg_decoder_forward(efg_decoder* d, int32_t token, size_t pos, float* logits
 int efg_decoder_generate(efg_decoder* d, const int32_t* prompt, size_t n_prompt, size_t max_new, int32_t eos_id,
                          const int32_t* forced, int32_t* tokens_out, size_t* n_tokens, float* step_logits,
                          double* prefill_seconds, double* decode_seconds);
+/* How the decode step runs: 0 = a CUDA graph of one kernel per operation (the default),
+ * 1 = one persistent kernel per launch (one CTA per SM, the weights streamed through shared
+ * memory across grid barriers). Both follow the reference's arithmetic. EFG_EINVAL when 1 is
+ * asked for a model the persistent kernel cannot run. */
+int efg_decoder_set_mode(efg_decoder* d, int persistent);
+/* The current mode (0 or 1), -1 for a null handle. */
+int efg_decoder_mode(const efg_decoder* d);
 
 #ifdef __cplusplus
 }

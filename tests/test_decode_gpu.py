@@ -109,13 +109,78 @@ def test_rewind_recomputes(z):
         np.testing.assert_array_equal(lg, ref[1])
 
 
+def test_tiny_models_use_the_graph_path():
+    """36-byte rows cannot be bulk-copied: these models run the per-operation graphs."""
+    with efg.Decoder(GOLD / "decode_tiny_uniform.efq", MAX_SEQ) as dec:
+        assert not dec.persistent
+        with pytest.raises(efg.EdgeForgeError, match="persistent kernel cannot run"):
+            dec.persistent = True
+
+
+# ---------------------------------------------------------------- medium model, both modes
+
+MEDIUM_MIXED = "model.layers.0.self_attn.k_proj.weight=q8_0,model.layers.1.mlp.up_proj.weight=q8_0"
+
+
+@pytest.fixture(scope="module")
+def medium(tmp_path_factory):
+    """D=256 / F=512 / 4 heads of 64 / 2 KV heads / V=300, written by the GPU writer with
+    q/k and gate/up of mixed storage types; the oracle's decoder gives the reference logits."""
+    from edgeforge_b200 import synthetic
+    from oracle.oracle import Oracle, OracleDecoder
+
+    d = tmp_path_factory.mktemp("medium")
+    cfg = synthetic.tiny_config(hidden=256, intermediate=512, layers=2, heads=4, kv_heads=2, vocab=300, max_pos=128)
+    synthetic.write_checkpoint(d / "ckpt", cfg, seed=8)
+    efq = d / "m.efq"
+    efg.quantize_model(d / "ckpt", efq, overrides=MEDIUM_MIXED)
+    rng = np.random.default_rng(12)
+    prompt = rng.integers(0, 300, 9).astype(np.int32)
+    forced = rng.integers(0, 300, 12).astype(np.int32)
+    ref = OracleDecoder(Oracle(), efq, 64).run(prompt, forced, threads=4)
+    return efq, prompt, forced, ref
+
+
+@pytest.mark.parametrize("persistent", [True, False])
+def test_medium_forward_and_generate(medium, persistent):
+    efq, prompt, forced, ref = medium
+    with efg.Decoder(efq, 64) as dec:
+        assert not dec.persistent  # the per-operation graphs are the default
+        dec.persistent = persistent
+        got = _forward_run(dec, prompt, forced)
+        assert np.abs(got - ref).max() <= TOL, np.abs(got - ref).max()
+        r = dec.generate(prompt, len(forced), forced=forced, keep_step_logits=True)
+        assert np.abs(r.step_logits - ref[1:]).max() <= TOL
+        np.testing.assert_array_equal(np.array(r.tokens), np.argmax(ref, axis=1))
+        g = dec.generate(prompt, 10)
+        eos = g.tokens[3]
+        stop = g.tokens.index(eos)
+        e = dec.generate(prompt, 10, eos_id=eos)
+        assert e.tokens == g.tokens[: stop + 1]
+        first = dec.generate(prompt, 10, eos_id=g.tokens[0])  # eos straight after the prompt
+        assert first.tokens == g.tokens[:1]
+        assert dec.generate(prompt, 0).tokens == []
+        assert efg.device_error() == 0
+
+
+def test_medium_modes_agree(medium):
+    efq, prompt, forced, _ = medium
+    with efg.Decoder(efq, 64) as a, efg.Decoder(efq, 64) as b:
+        a.persistent = True
+        ra = a.generate(prompt, 12, forced=forced, keep_step_logits=True)
+        rb = b.generate(prompt, 12, forced=forced, keep_step_logits=True)
+        assert ra.tokens == rb.tokens
+        assert np.abs(ra.step_logits - rb.step_logits).max() <= TOL
+
+
 # ---------------------------------------------------------------- full TinyLlama shape
 
 FULL_PROMPT = 23
 FULL_STEPS = 32
 
 
-def test_full_tinyllama_decode(tinyllama):
+@pytest.mark.parametrize("persistent", [True, False])
+def test_full_tinyllama_decode(tinyllama, persistent):
     full_model = tinyllama[1]
     from oracle.oracle import Reference
 
@@ -140,6 +205,7 @@ def test_full_tinyllama_decode(tinyllama):
     rd.close()
     logits_ref = np.stack(logits_ref)
     with efg.Decoder(full_model, FULL_PROMPT + FULL_STEPS) as dec:
+        dec.persistent = persistent
         info = dec.info
         assert (info.n_q4, info.n_q8) == (148, 7)
         assert dec.bytes_per_token == bpt == 616_570_880
