@@ -49,6 +49,13 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def bf16_peak_tflops():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
+
+
 def rank_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -215,6 +222,7 @@ def run_ours(args):
 
     efg.set_weight_prefetch(True)  # static weights: stream them during the previous kernel's tail
     hbm_peak, peak_kind = peaks()
+    bf16_peak = bf16_peak_tflops()
     nbytes = algo_bytes(Q8_0, ROWS, COLS)
 
     Ws = make_weights(efg, torch, Q8_0, ROWS, COLS, N_COPIES, seed=1 + rank)
@@ -291,6 +299,7 @@ def run_ours(args):
 
     dec = decode_extra(hbm_peak, with_cpu=not args.no_cpu_baseline) if world == 1 and not args.no_decode else None
     shard = None if args.no_sharded else sharded_extra(torch, efg, world, rank, hbm_peak)
+    gemm = gemm_extra(torch, efg, bf16_peak) if world == 1 and not args.no_gemm else None
 
     # DRAM bytes per launch of this kernel from the committed ncu capture summary
     traffic = None
@@ -326,7 +335,8 @@ def run_ours(args):
                 "gbs": round(gbs4, 1), "frac_of_hbm": round(gbs4 / hbm_peak, 4), "us_per_launch": round(ms4 * 1e3, 3),
                 "bytes_per_launch": algo_bytes(Q4_0, q4_rows, q4_cols), "copies": q4_copies},
                 "config2_decode_tinyllama": dec,
-                "config4_sharded_q4_0_131072x8192": shard},
+                "config4_sharded_q4_0_131072x8192": shard,
+                "config3_gemm_q4_0": gemm},
         }
         print(json.dumps(line))
     if world > 1:
@@ -452,6 +462,35 @@ def sharded_extra(torch, efg, world, rank, hbm_peak, steps=200, warmup=10, rows=
             "scaling": "strong"}
 
 
+def gemm_extra(torch, efg, bf16_peak, reps=20):
+    """Config 3: Q4_0 GEMM Y[B][M] = W X^T on the tensor cores for (M, K) = gate/up and down
+    shapes and B in {1, 16, 64, 256}: device time per call, useful TFLOP/s (2 M K B) and
+    the tensor-pipe rate the three BF16 MMAs per product imply."""
+    out = {}
+    for M, K in ((5632, 2048), (2048, 5632)):
+        W = make_weights(efg, torch, Q4_0, M, K, 1, seed=7)[0]
+        for B in (1, 16, 64, 256):
+            X = torch.randn(B, K, generator=torch.Generator(device="cuda").manual_seed(8), device="cuda")
+            Y = torch.empty(B, M, device="cuda")
+            for _ in range(3):
+                efg.gemm_q4_0(Y, W, X, M, K, B)
+            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            for _ in range(reps):
+                efg.gemm_q4_0(Y, W, X, M, K, B)
+            s1.record()
+            torch.cuda.synchronize()
+            us = s0.elapsed_time(s1) / reps * 1e3
+            fl = 2.0 * M * K * B
+            out[f"{M}x{K}_B{B}"] = {"us": round(us, 2), "useful_tflops": round(fl / us / 1e6, 2),
+                                    "issued_tflops": round(3 * fl / us / 1e6, 2),
+                                    "issued_frac_of_bf16": round(3 * fl / us / 1e6 / bf16_peak, 4)}
+        del W
+    assert efg.device_error() == 0
+    return out
+
+
 def run_profile(args):
     """A few plain launches of one matvec, for ncu (no graphs, no CPU legs):
     --profile q8  -> config 1 (Q8_0 32000x2048), --profile q4 -> config 0 (Q4_0 5632x2048),
@@ -485,6 +524,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode measurement")
     ap.add_argument("--no-sharded", action="store_true", help="skip the config-4 sharded matvec measurement")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 GEMM measurement")
     ap.add_argument("--profile", choices=["q8", "q4", "q4big"], help="a few plain launches for ncu")
     args = ap.parse_args()
     if args.profile:

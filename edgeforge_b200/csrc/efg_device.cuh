@@ -140,6 +140,13 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return pol;
 }
 
+// L2 policy for data many CTAs read (activations shared by every output tile).
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 // Global -> this CTA's shared memory, completion signalled on `bar` as tx bytes.
 // dst, src and bytes must all be multiples of 16. The copy lands in this CTA only.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {

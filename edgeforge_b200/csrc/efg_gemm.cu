@@ -23,6 +23,7 @@
 // 32 (w % 4) ..) and writes Y with coalesced stores.
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -274,7 +275,357 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4_0_kernel(const __grid
   if (warp == 0) tmem_dealloc(tmem, ncols);
 }
 
+// ================================================================ warp-specialised kernel
+//
+// For K a multiple of 256 (every config-3 shape). Roles per CTA (11 warps):
+//   warp 0      streams the CTA's raw W rows, 256 columns (144 bytes) per row and chunk,
+//               into a 3-stage ring with 1-D bulk copies;
+//   warp 10     streams the B operand tiles: X is split once per call into BF16 hi / lo
+//               parts laid out tile by tile in the swizzled UMMA layout (split_x_kernel),
+//               so each 64-column tile is one contiguous bulk copy;
+//   warps 2..9  dequantize each 64-column sub-chunk of the raw ring into the W_hi / W_lo
+//               operand tiles, then run the epilogue;
+//   warp 1      allocates TMEM and issues the MMAs (one thread), committing each sub-chunk
+//               to the operand stage's "empty" barrier and the last one to "acc_full".
+// Split-K: a cluster of S CTAs along z shares an output tile; each accumulates its share of
+// K, writes the partial tile into its own shared memory, and after a cluster barrier CTA z
+// sums columns z of all S partials through distributed shared memory in rank order (fixed
+// order: the result does not depend on timing).
+constexpr int kWsWarps = 11;
+constexpr int kWsThreads = kWsWarps * 32;
+constexpr uint32_t kRawK = 256, kRawRow = 144, kRawBytes = kTileM * kRawRow;
+constexpr uint32_t kRawStages = 3, kOpStages = 2, kMaxTileN2 = 128;
+constexpr uint32_t kOpABytes = 2 * kATileBytes;  // W_hi + W_lo
+
+struct GemmWsParams {
+  const uint8_t* W;
+  const uint8_t* Xs;  // split X: [n_tiles][K/64][2][n_tile][128 B]
+  float* Y;
+  uint32_t M, K, B, rb, n_tile, S;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// X [B][K] FP32 -> the B operand tiles: for every n-tile and 64-column chunk, n_tile rows of
+// 128 bytes (8 chunks of 8 BF16), swizzled as the MMA reads them; hi part then lo part.
+__global__ void split_x_kernel(const float* __restrict__ X, uint32_t B, uint32_t K, uint32_t n_tile,
+                               uint8_t* __restrict__ out, uint32_t n_tiles) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const uint32_t kc_n = K / kChunkK;
+  const uint64_t items = static_cast<uint64_t>(n_tiles) * kc_n * n_tile * 8;  // 16-byte chunks per part
+  for (uint64_t it = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < items;
+       it += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t c = it % 8, n = (it / 8) % n_tile;
+    const uint32_t kc = (it / (8ull * n_tile)) % kc_n, nt = static_cast<uint32_t>(it / (8ull * n_tile * kc_n));
+    const uint32_t b = nt * n_tile + n, k = kc * kChunkK + c * 8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (b < B) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(X + static_cast<uint64_t>(b) * K + k));
+      const float4 d = __ldg(reinterpret_cast<const float4*>(X + static_cast<uint64_t>(b) * K + k + 4));
+      v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = d.x, v[5] = d.y, v[6] = d.z, v[7] = d.w;
+    }
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) split2(v[2 * e], v[2 * e + 1], hi[e], lo[e]);
+    const uint64_t tile = (static_cast<uint64_t>(nt) * kc_n + kc) * 2 * n_tile * 128;
+    const uint32_t off = sw128(n, c);
+    *reinterpret_cast<uint4*>(out + tile + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(out + tile + n_tile * 128 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+  }
+}
+
+__global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __grid_constant__ GemmWsParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t raw_full[kRawStages], raw_empty[kRawStages], a_full[kOpStages], b_full[kOpStages],
+      op_empty[kOpStages], acc_full;
+  __shared__ uint32_t tmem_slot;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t N = p.n_tile, m0 = blockIdx.x * kTileM, n0 = blockIdx.y * N;
+  const uint32_t z = p.S > 1 ? cluster_rank() : 0;
+  const uint32_t raw_total = p.K / kRawK;
+  const uint32_t rc0 = static_cast<uint32_t>(static_cast<uint64_t>(raw_total) * z / p.S);
+  const uint32_t rc1 = static_cast<uint32_t>(static_cast<uint64_t>(raw_total) * (z + 1) / p.S);
+  const uint32_t n_raw = rc1 - rc0, n_sub = n_raw * (kRawK / kChunkK);
+  const uint32_t valid_rows = min(static_cast<uint32_t>(kTileM), p.M - m0);
+  const uint32_t b_bytes = N * 128;
+  // 1024-byte aligned: operand stages (A_hi, A_lo, B1, B2) x 2, then the raw ring
+  const uint32_t raw_base_addr = smem_addr(smem_raw);
+  uint8_t* base = smem_raw + (((raw_base_addr + 1023u) & ~1023u) - raw_base_addr);
+  uint8_t* ops = base;
+  const uint32_t op_stage = kOpABytes + 2 * b_bytes;
+  uint8_t* raw = ops + kOpStages * op_stage;
+  uint32_t ncols = 32;
+  while (ncols < N) ncols <<= 1;
+
+  if (tid == 0) {
+    for (uint32_t i = 0; i < kRawStages; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 8);
+    }
+    for (uint32_t i = 0; i < kOpStages; ++i) {
+      mbar_init(&a_full[i], 8);
+      mbar_init(&b_full[i], 1);
+      mbar_init(&op_empty[i], 1);
+    }
+    mbar_init(&acc_full, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&tmem_slot, ncols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_wait();  // X (split by the previous kernel) and W are ready
+  const uint32_t tmem = tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- raw W producer
+    const uint64_t pol = l2_evict_first_policy();
+    uint32_t issued_raw = 0;
+    for (uint32_t rc = 0; rc < n_raw && ok; ++rc) {
+      const uint32_t rs = rc % kRawStages;
+      if (rc >= kRawStages) ok = mbar_wait(&raw_empty[rs], ((rc / kRawStages) - 1) & 1u, p.err);
+      if (!__all_sync(0xFFFFFFFFu, ok)) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], valid_rows * kRawRow);
+      __syncwarp();
+      for (uint32_t r = lane; r < valid_rows; r += 32)
+        bulk_g2s(raw + rs * kRawBytes + r * kRawRow, p.W + static_cast<uint64_t>(m0 + r) * p.rb + (rc0 + rc) * kRawRow,
+                 kRawRow, &raw_full[rs], pol);
+      issued_raw = rc + 1;
+    }
+    // copies issued into the ring land before the CTA may exit (bounded; immediate when done)
+    if (lane == 0)
+      for (uint32_t q = issued_raw > kRawStages ? issued_raw - kRawStages : 0; q < issued_raw; ++q)
+        mbar_drain(&raw_full[q % kRawStages], (q / kRawStages) & 1u, p.err);
+    __syncwarp();
+  } else if (warp == 10) {
+    // ---------------------------------------------------------- B tile producer
+    if (lane == 0) {
+      const uint32_t kc_n = p.K / kChunkK;
+      const uint64_t keep = l2_evict_last_policy();  // X tiles are read by every M-tile
+      uint32_t issued_b = 0;
+      for (uint32_t s = 0; s < n_sub && ok; ++s) {
+        const uint32_t os = s % kOpStages;
+        if (s >= kOpStages) ok = mbar_wait(&op_empty[os], ((s / kOpStages) - 1) & 1u, p.err);
+        if (!ok) break;
+        const uint32_t kc = rc0 * (kRawK / kChunkK) + s;
+        const uint8_t* src = p.Xs + (static_cast<uint64_t>(blockIdx.y) * kc_n + kc) * 2 * b_bytes;
+        mbar_arrive_expect_tx(&b_full[os], 2 * b_bytes);
+        bulk_g2s(ops + os * op_stage + kOpABytes, src, 2 * b_bytes, &b_full[os], keep);
+        issued_b = s + 1;
+      }
+      for (uint32_t q = issued_b > kOpStages ? issued_b - kOpStages : 0; q < issued_b; ++q)
+        mbar_drain(&b_full[q % kOpStages], (q / kOpStages) & 1u, p.err);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16(kTileM, N);
+      for (uint32_t s = 0; s < n_sub && ok; ++s) {
+        const uint32_t os = s % kOpStages, par = (s / kOpStages) & 1u;
+        ok = mbar_wait(&a_full[os], par, p.err) && mbar_wait(&b_full[os], par, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        uint8_t* st = ops + os * op_stage;
+        const uint64_t dah = smem_desc_sw128(smem_addr(st)), dal = smem_desc_sw128(smem_addr(st + kATileBytes));
+        const uint64_t db1 = smem_desc_sw128(smem_addr(st + kOpABytes)),
+                       db2 = smem_desc_sw128(smem_addr(st + kOpABytes + b_bytes));
+#pragma unroll
+        for (uint32_t ks = 0; ks < kChunkK / 16; ++ks) {
+          const uint64_t adv = 2ull * ks;
+          mma_bf16(tmem, dah + adv, db1 + adv, idesc, (s | ks) != 0);
+          mma_bf16(tmem, dah + adv, db2 + adv, idesc, 1);
+          mma_bf16(tmem, dal + adv, db1 + adv, idesc, 1);
+        }
+        mma_commit(&op_empty[os]);
+      }
+      mma_commit(&acc_full);  // after every MMA issued (or none)
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------- dequant (warps 2..9)
+    const uint32_t t = tid - 64, r = t >> 1, blk = t & 1;
+    for (uint32_t s = 0; s < n_sub && ok; ++s) {
+      const uint32_t rc = s / 4, sub = s % 4, rs = rc % kRawStages, os = s % kOpStages;
+      if (sub == 0) ok = mbar_wait(&raw_full[rs], (rc / kRawStages) & 1u, p.err);
+      if (ok && s >= kOpStages) ok = mbar_wait(&op_empty[os], ((s / kOpStages) - 1) & 1u, p.err);
+      if (!__all_sync(0xFFFFFFFFu, ok)) {
+        ok = false;
+        break;
+      }
+      uint8_t* st = ops + os * op_stage;
+      uint4 hi4[4], lo4[4];
+      if (r < valid_rows) {
+        const uint16_t* q = reinterpret_cast<const uint16_t*>(raw + rs * kRawBytes + r * kRawRow + (sub * 2 + blk) * 18);
+        const float d = fp16_to_f32(q[0]);
+        uint32_t qs[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) qs[i] = q[1 + 2 * i] | (static_cast<uint32_t>(q[2 + 2 * i]) << 16);
+        float w[32];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const uint32_t byte = (qs[j >> 2] >> (8 * (j & 3))) & 0xFFu;
+          w[j] = __fmul_rn(static_cast<float>(static_cast<int>(byte & 15u) - 8), d);
+          w[j + 16] = __fmul_rn(static_cast<float>(static_cast<int>(byte >> 4) - 8), d);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t h[4], l[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) split2(w[8 * c + 2 * e], w[8 * c + 2 * e + 1], h[e], l[e]);
+          hi4[c] = make_uint4(h[0], h[1], h[2], h[3]);
+          lo4[c] = make_uint4(l[0], l[1], l[2], l[3]);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) hi4[c] = lo4[c] = make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t off = sw128(r, blk * 4 + c);
+        *reinterpret_cast<uint4*>(st + off) = hi4[c];
+        *reinterpret_cast<uint4*>(st + kATileBytes + off) = lo4[c];
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a_full[os]);
+        if (sub == 3) mbar_arrive(&raw_empty[rs]);  // every read of this raw chunk is done
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ epilogue (warps 2..9)
+  // every warp, on every path, reaches the same barriers below
+  if (warp >= 2 && warp < 10) ok = mbar_drain(&acc_full, 0, p.err) && ok;
+  const int all_ok = __syncthreads_and(ok);
+  tc_fence_after();
+  float* part = reinterpret_cast<float*>(ops);  // [N][128] partial tile, reusing the operand stages
+  if (warp >= 2 && warp < 10) {
+    const uint32_t q = warp & 3u, half = (warp - 2) >> 2, row = 32 * q + lane;
+    for (uint32_t c0 = half * (N / 2); c0 < (half + 1) * (N / 2); c0 += 8) {
+      float v[8];
+      tmem_ld8(tmem + ((32 * q) << 16) + c0, v);
+      if (p.S == 1) {
+        if (all_ok && m0 + row < p.M)
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (n0 + c0 + e < p.B) p.Y[static_cast<uint64_t>(n0 + c0 + e) * p.M + m0 + row] = v[e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) part[(c0 + e) * kTileM + row] = v[e];
+      }
+    }
+  }
+  if (p.S > 1) {
+    cluster_sync();  // every partial tile of the cluster is in shared memory
+    const uint32_t c_lo = static_cast<uint32_t>(static_cast<uint64_t>(N) * z / p.S);
+    const uint32_t c_hi = static_cast<uint32_t>(static_cast<uint64_t>(N) * (z + 1) / p.S);
+    for (uint32_t i = tid; i < (c_hi - c_lo) * kTileM; i += kWsThreads) {
+      const uint32_t c = c_lo + i / kTileM, row = i % kTileM;
+      const uint32_t a = smem_addr(part + c * kTileM + row);
+      float acc = 0.f;
+      for (uint32_t q = 0; q < p.S; ++q) acc += ld_dsmem(a, q);
+      if (all_ok && m0 + row < p.M && n0 + c < p.B) p.Y[static_cast<uint64_t>(n0 + c) * p.M + m0 + row] = acc;
+    }
+    cluster_sync();  // peers keep their shared memory until every read is done
+  }
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, ncols);
+}
+
+// Per-device grow-only workspace for the split X (the only scratch the GEMM needs).
+struct GemmScratch {
+  std::mutex mu;
+  void* p = nullptr;
+  size_t cap = 0;
+};
+GemmScratch g_gemm_scratch[64];
+
 }  // namespace
+
+// The warp-specialised path (K % 256 == 0): split X, then the GEMM with split-K over a
+// cluster of S CTAs sized so that ~one wave covers the SMs.
+int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
+                   cudaStream_t s) {
+  DeviceInfo* dev = current_device();
+  if (!dev) return EFG_ECUDA;
+  const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN2, (B + 15) / 16 * 16));
+  const uint32_t n_tiles = static_cast<uint32_t>((B + n_tile - 1) / n_tile);
+  const uint32_t m_tiles = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
+  const size_t ws_bytes = static_cast<size_t>(n_tiles) * (K / kChunkK) * 2 * n_tile * 128;
+  GemmScratch& gs = g_gemm_scratch[dev->device];
+  std::lock_guard<std::mutex> lk(gs.mu);
+  if (ws_bytes > gs.cap) {
+    if (gs.p) cudaFree(gs.p);
+    gs.p = nullptr;
+    gs.cap = 0;
+    EFG_TRY_CUDA(cudaMalloc(&gs.p, ws_bytes), "gemm workspace");
+    gs.cap = ws_bytes;
+  }
+  {
+    const uint64_t items = static_cast<uint64_t>(n_tiles) * (K / kChunkK) * n_tile * 8;
+    const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((items + 255) / 256, 8ull * dev->sm_count));
+    split_x_kernel<<<grid, 256, 0, s>>>(X, static_cast<uint32_t>(B), static_cast<uint32_t>(K), n_tile,
+                                        static_cast<uint8_t*>(gs.p), n_tiles);
+    EFG_TRY_CUDA(cudaGetLastError(), "gemm split launch");
+  }
+  const size_t smem = 1024 + kOpStages * (kOpABytes + 2 * static_cast<size_t>(n_tile) * 128) + kRawStages * kRawBytes;
+  if (int st = ensure_smem_attr(reinterpret_cast<const void*>(gemm_q4_0_ws_kernel), smem)) return st;
+  const uint32_t raw_total = static_cast<uint32_t>(K / kRawK);
+  uint32_t S = std::max<uint32_t>(1, static_cast<uint32_t>(dev->sm_count) / (m_tiles * n_tiles));
+  S = std::min<uint32_t>({S, 8u, std::max<uint32_t>(1, raw_total / 2)});
+  GemmWsParams p{W, static_cast<const uint8_t*>(gs.p), Y, static_cast<uint32_t>(M), static_cast<uint32_t>(K),
+                 static_cast<uint32_t>(B), static_cast<uint32_t>(K / 32 * 18), n_tile, 1, d_err};
+  for (;; S /= 2) {  // the largest cluster the device can place
+    p.S = std::max(S, 1u);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(m_tiles, n_tiles, p.S);
+    cfg.blockDim = dim3(kWsThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = p.S;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (p.S > 1) {
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, gemm_q4_0_ws_kernel, &cfg) != cudaSuccess || clusters < 1) {
+        cudaGetLastError();
+        continue;
+      }
+    }
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, gemm_q4_0_ws_kernel, p), "gemm launch");
+    return EFG_OK;
+  }
+}
 
 int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
                      cudaStream_t s) {
@@ -289,6 +640,7 @@ int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
   if (reinterpret_cast<uintptr_t>(X) % 16 != 0 || reinterpret_cast<uintptr_t>(W) % 2 != 0 ||
       reinterpret_cast<uintptr_t>(Y) % 4 != 0)
     return fail(EFG_EINVAL, "gemm: X must be 16-byte aligned, W 2-byte aligned and Y 4-byte aligned");
+  if (K % kRawK == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0) return launch_gemm_ws(Y, W, X, M, K, B, d_err, s);
   const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN, (B + 15) / 16 * 16));
   GemmParams p{W, X, Y, static_cast<uint32_t>(M), static_cast<uint32_t>(K), static_cast<uint32_t>(B),
                static_cast<uint32_t>(K / 32 * 18), n_tile, d_err};
