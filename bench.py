@@ -300,6 +300,7 @@ def run_ours(args):
     dec = decode_extra(hbm_peak, with_cpu=not args.no_cpu_baseline) if world == 1 and not args.no_decode else None
     shard = None if args.no_sharded else sharded_extra(torch, efg, world, rank, hbm_peak)
     gemm = gemm_extra(torch, efg, bf16_peak) if world == 1 and not args.no_gemm else None
+    quant = quant_extra(torch, efg, hbm_peak) if world == 1 and not args.no_gemm else None
 
     # DRAM bytes per launch of this kernel from the committed ncu capture summary
     traffic = None
@@ -336,7 +337,8 @@ def run_ours(args):
                 "bytes_per_launch": algo_bytes(Q4_0, q4_rows, q4_cols), "copies": q4_copies},
                 "config2_decode_tinyllama": dec,
                 "config4_sharded_q4_0_131072x8192": shard,
-                "config3_gemm_q4_0": gemm},
+                "config3_gemm_q4_0": gemm,
+                "config1_quantize_round_trip": quant},
         }
         print(json.dumps(line))
     if world > 1:
@@ -460,6 +462,35 @@ def sharded_extra(torch, efg, world, rank, hbm_peak, steps=200, warmup=10, rows=
             "local_frac_of_hbm": round(shard_bytes / (ms_local / 1e3) / 1e9 / hbm_peak, 4),
             "gather_bytes": 4 * rows, "ranks": world, "rows_per_rank": c, "matrix_bytes": rows * rb,
             "scaling": "strong"}
+
+
+def quant_extra(torch, efg, hbm_peak, reps=5):
+    """Config 1's round trip: the 32000 x 2048 FP32 matrix quantized to Q4_0 (with the MSE
+    scale search) and Q8_0, and dequantized back, on the device (bit-exact kernels);
+    GB/s = bytes read + written per call."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    X = torch.randn(ROWS, COLS, generator=g, device="cuda") * 0.02
+    out = {}
+    for name, qt in (("q4_0", Q4_0), ("q8_0", Q8_0)):
+        rb = COLS // 32 * (18 if qt == Q4_0 else 34)
+        Wq = torch.empty(ROWS * rb, dtype=torch.uint8, device="cuda")
+        Xd = torch.empty_like(X)
+        for fn, label in ((lambda: efg.quantize_rows(qt, X, ROWS, COLS, Wq, True), "quantize"),
+                          (lambda: efg.dequantize_rows(qt, Wq, ROWS, COLS, Xd), "dequantize")):
+            fn()
+            torch.cuda.synchronize()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record()
+            for _ in range(reps):
+                fn()
+            s1.record()
+            torch.cuda.synchronize()
+            ms = s0.elapsed_time(s1) / reps
+            nb = X.numel() * 4 + Wq.numel()
+            out[f"{label}_{name}"] = {"ms": round(ms, 4), "gbs": round(nb / ms / 1e6, 1),
+                                      "frac_of_hbm": round(nb / ms / 1e6 / hbm_peak, 4)}
+    del X
+    return out
 
 
 def gemm_extra(torch, efg, bf16_peak, reps=20):
