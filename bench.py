@@ -523,14 +523,34 @@ def gemm_extra(torch, efg, bf16_peak, reps=20):
 
 
 def run_profile(args):
-    """A few plain launches of one matvec, for ncu (no graphs, no CPU legs):
-    --profile q8  -> config 1 (Q8_0 32000x2048), --profile q4 -> config 0 (Q4_0 5632x2048),
-    --profile q4big -> Q4_0 16384x8192 (302 MB, a slice of config 4's rows)."""
+    """A few plain launches for ncu (no CPU legs): --profile q8 -> config 1 (Q8_0 32000x2048),
+    q4 -> config 0 (Q4_0 5632x2048), q4big -> Q4_0 16384x8192 (302 MB, a slice of config 4's
+    rows), gemm -> config 3 (5632x2048, B=64), decode / decode_persistent -> config 2, four
+    single-token forwards in each decode mode."""
     import torch
 
     import edgeforge_b200 as efg
 
     torch.cuda.set_device(0)
+    if args.profile == "gemm":  # config 3, M=5632 K=2048 B=64: X split + GEMM, 3 calls
+        M, K, B = 5632, 2048, 64
+        W = make_weights(efg, torch, Q4_0, M, K, 1, seed=7)[0]
+        X = torch.randn(B, K, device="cuda")
+        Y = torch.empty(B, M, device="cuda")
+        for _ in range(3):
+            efg.gemm_q4_0(Y, W, X, M, K, B)
+        torch.cuda.synchronize()
+        assert efg.device_error() == 0
+        print(json.dumps({"profile": "gemm", "M": M, "K": K, "B": B, "calls": 3}))
+        return 0
+    if args.profile in ("decode", "decode_persistent"):  # config 2: 4 forwards, one token each
+        with efg.Decoder(decode_model(), 64) as dec:
+            dec.persistent = args.profile == "decode_persistent"
+            for i in range(4):
+                dec.forward(3 + i, i)
+        assert efg.device_error() == 0
+        print(json.dumps({"profile": args.profile, "forwards": 4}))
+        return 0
     qt, rows, cols, copies = {"q8": (Q8_0, ROWS, COLS, 3), "q4": (Q4_0, 5632, 2048, 24),
                               "q4big": (Q4_0, 16384, 8192, 1)}[args.profile]
     Ws = make_weights(efg, torch, qt, rows, cols, copies, seed=1)
@@ -556,7 +576,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode measurement")
     ap.add_argument("--no-sharded", action="store_true", help="skip the config-4 sharded matvec measurement")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 GEMM measurement")
-    ap.add_argument("--profile", choices=["q8", "q4", "q4big"], help="a few plain launches for ncu")
+    ap.add_argument("--profile", choices=["q8", "q4", "q4big", "gemm", "decode", "decode_persistent"],
+                    help="a few plain launches for ncu")
     args = ap.parse_args()
     if args.profile:
         return run_profile(args)
