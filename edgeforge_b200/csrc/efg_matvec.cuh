@@ -39,10 +39,17 @@ struct MatvecArgs {
 // left in the thread-local error string.
 int launch_matvec(const MatvecArgs& a, int* d_err, cudaStream_t stream);
 
+struct DeviceInfo;
+// The Q4_0 kernel on the integer tensor-core MMA (efg_matvec_mma.cu): taken for Q4_0
+// matrices of 48 MB and more with 2048 <= cols <= 8192, cols % 256 == 0, 16-byte aligned
+// W, x and norm weights, store / add epilogues. Uses no library-owned state.
+bool matvec_mma_ok(const MatvecArgs& a, const DeviceInfo& dev);
+int launch_matvec_q4_mma(const MatvecArgs& a, const DeviceInfo& dev, int* d_err, cudaStream_t stream,
+                         bool direct_smem_attr);
+
 // launch_matvec on a caller-described device. With direct_smem_attr the kernel's
 // shared-memory limit is set by cudaFuncSetAttribute on every launch instead of through
 // the library's per-kernel cache, so the call touches no library-owned state.
-struct DeviceInfo;
 int launch_matvec_on(const MatvecArgs& a, const DeviceInfo& dev, int* d_err, cudaStream_t stream,
                      bool direct_smem_attr);
 

@@ -1,0 +1,565 @@
+// efg_matvec_mma.cu - Q4_0 matvec with the integer tensor-core MMA (sm_100a).
+//
+// The CUDA-core kernel (efg_matvec.cu) spends ~2 lane-instructions per Q4_0 weight turning
+// codes into floats and multiplying; at ~25 weights per clock per SM that caps it near
+// 3 TB/s. Here the arithmetic moves to `mma.sync.m16n8k32.s8.s8.s32`, exactly:
+//
+//  * A (16 x 32): a code c becomes the int8 (c - 8) * 16 with one LOP3 per 4 codes:
+//    (w ^ 0x80808080) & 0xF0F0F0F0 for the high nibbles, the same on w << 4 for the low
+//    ones. Byte j of a block's 16 code bytes holds columns j and j + 16, which is the
+//    m16n8k32 fragment's split of K.
+//  * B (32 x 8): x of a block as a fixed-point integer X = round(x * 2^s), |X| < 2^30,
+//    written as four balanced int8 digits (X = d0 + 2^8 d1 + 2^16 d2 + 2^24 d3). The
+//    block's s makes its largest |x| use the full range, so each x is kept to 2^-31 of
+//    its block's largest |x|.
+//  * One MMA covers 8 rows and a block pair: A rows 0..7 are the even block of 8 tile
+//    rows, A rows 8..15 the odd block of the same rows; B columns 0..3 are the even
+//    block's digits, 4..7 the odd block's. The int32 products are exact; each lane keeps
+//    one useful pair of digit sums, c_lo + 256 c_hi, which becomes a float scaled by
+//    d * 2^-s / 16 (or 2^(16-s) / 16 for digits 2, 3) and accumulates in FP32 with one
+//    FMA. The error against the exact dot is below 2^-31 * sum over blocks of
+//    max|x| * sum|w| plus FP32 accumulation rounding, far inside the 1e-5 of sum |w x|
+//    the reference's tests allow for realistic activations.
+//
+// Streaming: one 2-D TMA tensor copy per stage. W is seen as [rows][row bytes / 8] of
+// 8-byte elements and a stage is the box {146 elements, 16 rows} at the K segment's
+// start (segments of 64 blocks, 1152 bytes, so x is a multiple of 16 bytes): it lands as
+// 16 rows of 1168 bytes, 16 bytes (mod 128) apart, so the 8 rows a fragment load touches
+// fall in 8 different bank quads. The 16 bytes past the segment are the next segment's
+// (or zero fill past the row end) and are not read; rows past the matrix are zero fill.
+// One instruction per 18.7 KB stage keeps the copy engine ahead of HBM; 16 separate 1-D
+// copies per stage held the producer warp in the copy instruction half of the time.
+//
+// Work: a row tile is taken by a group of Wk * nseg consumer warps, Wk per K segment,
+// each with a fixed share of the segment's block pairs, so the stages of a tile are
+// consumed at once and the ring drains in order; the group adds its 16 row sums in warp
+// order after one named barrier per tile, so results do not depend on timing. Groups
+// take every Gs-th tile of the CTA. The producer issues two stages, then waits until
+// every consumer warp has issued its x loads, so those reach the memory system ahead of
+// the ring's fill. A CTA whose x holds a non-finite value, or a block maximum outside
+// [2^-69, 2^100), computes its rows with plain FP32 dots instead.
+#include <algorithm>
+#include <cstdint>
+
+#include <cuda.h>
+
+#include "../../include/efg.h"
+#include "efg_device.cuh"
+#include "efg_dot.cuh"
+#include "efg_host.h"
+#include "efg_matvec.cuh"
+
+#ifndef EFG_MMA_MIN_BYTES
+#define EFG_MMA_MIN_BYTES (48ull << 20)  // matrices from this size take the MMA kernel
+#endif
+
+namespace efg {
+namespace {
+
+constexpr int kMmaConsumers = 16;
+constexpr int kMmaThreads = (kMmaConsumers + 1) * 32;
+constexpr uint32_t kTileRows = 16;
+constexpr uint32_t kMinBlk = 64;          // cols >= 2048
+constexpr uint32_t kMaxBlk = 256;         // cols <= 8192
+constexpr uint32_t kSegBlk = 64;          // K segment: 64 blocks, 1152 bytes of a row
+constexpr uint32_t kBoxElems = 146;       // box row: 1168 bytes = 1152 + 16 (8-byte elements)
+constexpr uint32_t kRowStride = kBoxElems * 8;
+constexpr uint32_t kStageBytes = kTileRows * kRowStride;  // 18688 = 146 * 128
+constexpr uint32_t kMaxStages = 16;
+constexpr uint32_t kGroupBarrier0 = 2;    // named barriers 2 .. 2 + Gs - 1 <= 15 (1: all consumers)
+constexpr uint32_t kPrefetchStages = 2;   // stages the producer issues before the x loads
+
+// Shared memory, fixed part first: full[S] | empty[S] | xready | tile_id[S] | bad_x |
+// dred[C] (f64) | red[C][2][16] (f32) | xsc[2 nblk] | xdig[nblk * 128] | ring (128-aligned).
+constexpr uint32_t kDredOffset = (2 * kMaxStages * 8 + 8 + kMaxStages * 4 + 4 + 7) / 8 * 8;
+constexpr uint32_t kRedOffset = kDredOffset + kMmaConsumers * 8;
+constexpr uint32_t kXscOffset = kRedOffset + kMmaConsumers * 2 * kTileRows * 4;
+
+struct MmaParams {
+  CUtensorMap maps[kMaxJobs];  // one per job: W as [rows][rb / 8] u64, box {146, 16}
+  const float* x;
+  const float* norm_w;
+  float norm_eps;
+  int* err;
+  const int32_t* pos;
+  uint32_t cols, nblk, rb, nseg;
+  uint32_t NS, ring_offset;
+  uint32_t Wk, Gs;  // warps per K segment, tile groups (of Wk * nseg warps)
+  uint32_t rt_total, n_jobs;
+  uint32_t job_rt_start[kMaxJobs + 1];
+  MatvecJobDev jobs[kMaxJobs];
+};
+
+__device__ __forceinline__ uint32_t a_lo(uint32_t w) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x28;" : "=r"(r) : "r"(w << 4), "r"(0x80808080u), "r"(0xF0F0F0F0u));
+  return r;  // ((w << 4) ^ 0x80808080) & 0xF0F0F0F0
+}
+__device__ __forceinline__ uint32_t a_hi(uint32_t w) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x28;" : "=r"(r) : "r"(w), "r"(0x80808080u), "r"(0xF0F0F0F0u));
+  return r;
+}
+
+// No side effects and no memory operands: the compiler may schedule it freely among the
+// shared-memory loads of neighbouring block pairs.
+__device__ __forceinline__ void mma_s8(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int (&c)[4]) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %10, %10, %10};"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Which job a row tile belongs to and its first row.
+__device__ __forceinline__ void locate_rt(const MmaParams& p, uint32_t rt, uint32_t& j, uint32_t& r0, uint32_t& nrows) {
+  j = 0;
+  while (j + 1 < p.n_jobs && rt >= p.job_rt_start[j + 1]) ++j;
+  r0 = (rt - p.job_rt_start[j]) * kTileRows;
+  nrows = min(kTileRows, p.jobs[j].rows - r0);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar,
+                                            uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(pol)
+      : "memory");
+}
+
+template <Epi E, bool NORM>
+__global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __grid_constant__ MmaParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* xready = empty + kMaxStages;
+  volatile uint32_t* tile_id = reinterpret_cast<volatile uint32_t*>(xready + 1);
+  volatile int* bad_x = reinterpret_cast<volatile int*>(tile_id + kMaxStages);
+  double* dred = reinterpret_cast<double*>(smem + kDredOffset);   // [consumer warps]
+  float* red = reinterpret_cast<float*>(smem + kRedOffset);       // [consumer warp][2][16]
+  float* xsc = reinterpret_cast<float*>(smem + kXscOffset);       // [nblk][2]
+  uint8_t* xdig = reinterpret_cast<uint8_t*>(xsc + 2 * p.nblk);   // [nblk][4 t][4 g][8 bytes]
+  uint8_t* ring = smem + p.ring_offset;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < p.NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], p.Wk);
+      tile_id[s] = 0xFFFFFFFFu;
+    }
+    mbar_init(xready, kMmaConsumers);
+    *bad_x = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  const uint32_t rt_b = static_cast<uint32_t>(static_cast<uint64_t>(p.rt_total) * blockIdx.x / gridDim.x);
+  const uint32_t rt_e = static_cast<uint32_t>(static_cast<uint64_t>(p.rt_total) * (blockIdx.x + 1) / gridDim.x);
+  const uint32_t R = rt_e - rt_b;
+
+  if (warp == kMmaConsumers) {
+    // ------------------------------------------------------------ producer
+    if (lane != 0) return;
+    const uint64_t pol = l2_evict_first_policy();
+    uint32_t gt = 0;
+    bool ok = true;
+    for (uint32_t tl = 0; tl < R && ok; ++tl) {
+      uint32_t j, r0, nrows;
+      locate_rt(p, rt_b + tl, j, r0, nrows);
+      for (uint32_t ks = 0; ks < p.nseg; ++ks, ++gt) {
+        const uint32_t s = gt % p.NS, gen = gt / p.NS;
+        if (gt == kPrefetchStages && !mbar_wait(xready, 0, p.err)) {
+          ok = false;
+          break;
+        }
+        if (gen > 0 && !mbar_wait(&empty[s], (gen - 1) & 1u, p.err)) {
+          ok = false;
+          break;
+        }
+        tile_id[s] = gt;
+        mbar_arrive_expect_tx(&full[s], kStageBytes);
+        tma_load_2d(ring + s * kStageBytes, &p.maps[j], static_cast<int32_t>(ks * kSegBlk * 18 / 8),
+                    static_cast<int32_t>(r0), &full[s], pol);
+      }
+    }
+    // copies issued into the ring land before the CTA may exit (bounded)
+    for (uint32_t q = gt > p.NS ? gt - p.NS : 0; q < gt; ++q) mbar_wait(&full[q % p.NS], (q / p.NS) & 1u, nullptr);
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const uint32_t tid = threadIdx.x, nthr = kMmaConsumers * 32;
+  pdl_wait();  // x, norm weights and y belong to the previous kernel in the stream
+  float inv = 1.f;
+  if constexpr (NORM) {  // rmsnorm scale (src/kernels.cpp:69-73): double sum of squares
+    double ss = 0.0;
+    for (uint32_t i = tid; i < p.cols; i += nthr) {
+      const double v = static_cast<double>(__ldg(p.x + i));
+      ss += v * v;
+    }
+    ss = warp_sum_d(ss);
+    if (lane == 0) dred[warp] = ss;
+    named_barrier(1, nthr);
+    double tot = 0.0;
+    for (int w = 0; w < kMmaConsumers; ++w) tot += dred[w];
+    const double mean = p.cols ? tot / static_cast<double>(p.cols) : 0.0;
+    inv = static_cast<float>(1.0 / sqrt(mean + static_cast<double>(p.norm_eps)));
+  }
+  // x -> per-block fixed-point digits. 8 lanes per block, 4 consecutive columns per lane
+  // (one float4), 4 blocks per warp step; a warp's loads are all issued first. For an odd
+  // block, columns 4c..4c+3 are B-fragment columns k = 16 v2 + 4 t + v0 with v2 = c / 4,
+  // t = c % 4, so digit g of the four is one 32-bit word at [t][g][v2]. Even blocks use
+  // the K order in which the consumers read their codes (see below).
+  {
+    const uint32_t q = lane >> 3, c = lane & 7;
+    constexpr uint32_t kSteps = kMaxBlk / (4 * kMmaConsumers) + 1;
+    float4 hv[kSteps];
+#pragma unroll
+    for (uint32_t i = 0; i < kSteps; ++i) {
+      const uint32_t b = (warp + i * kMmaConsumers) * 4 + q;
+      hv[i] = b < p.nblk ? __ldg(reinterpret_cast<const float4*>(p.x) + b * 8 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // the loads above are issued; the arrive (an asm with a memory clobber) stays after them
+    __syncwarp();
+    if (lane == 0) mbar_arrive(xready);
+#pragma unroll
+    for (uint32_t i = 0; i < kSteps; ++i) {
+      const uint32_t b = (warp + i * kMmaConsumers) * 4 + q;
+      if ((warp + i * kMmaConsumers) * 4 >= p.nblk) break;  // uniform per warp (nblk % 4 == 0)
+      float h[4] = {hv[i].x, hv[i].y, hv[i].z, hv[i].w};
+      if constexpr (NORM) {  // w * (x * inv), src/kernels.cpp:74
+        const float4 nw = __ldg(reinterpret_cast<const float4*>(p.norm_w) + b * 8 + c);
+        h[0] = nw.x * (h[0] * inv);
+        h[1] = nw.y * (h[1] * inv);
+        h[2] = nw.z * (h[2] * inv);
+        h[3] = nw.w * (h[3] * inv);
+      }
+      float amax = fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3])));
+      const bool fin = isfinite(h[0]) && isfinite(h[1]) && isfinite(h[2]) && isfinite(h[3]);
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+      const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127;
+      // Outside 2^-69 <= max|x| < 2^100 (or non-finite) the CTA takes the FP32 path: there
+      // d * 2^-s / 16 stays a normal float for every FP16 d.
+      if (__any_sync(0xFFFFFFFFu, !fin || (amax != 0.f && (e < -69 || e >= 100)))) {
+        if (lane == 0) *bad_x = 1;
+        continue;
+      }
+      const int s = amax == 0.f ? 0 : 29 - e;  // |x| * 2^s < 2^30; -70 <= s <= 98
+      // 2^s, 2^(-4-s) and 2^(12-s) are normal floats for these s: built from their bits.
+      // x * 2^s is exact wherever rint can see it (|x * 2^s| >= 2^-126 or it rounds to 0).
+      const float p2s = __uint_as_float(static_cast<uint32_t>(s + 127) << 23);
+      uint32_t words[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int v0 = 0; v0 < 4; ++v0) {
+        int X = __float2int_rn(h[v0] * p2s);
+        const int d0 = static_cast<int8_t>(X & 0xFF);
+        X = (X - d0) >> 8;
+        const int d1 = static_cast<int8_t>(X & 0xFF);
+        X = (X - d1) >> 8;
+        const int d2 = static_cast<int8_t>(X & 0xFF);
+        const int d3 = (X - d2) >> 8;
+        words[0] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * v0);
+        words[1] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * v0);
+        words[2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * v0);
+        words[3] |= (static_cast<uint32_t>(d3) & 0xFFu) << (8 * v0);
+      }
+      const uint32_t c3 = c & 3u, v2 = c >> 2;
+      if (b & 1u) {  // odd block: natural order, lane t holds code bytes 4t..4t+3
+        uint32_t* base = reinterpret_cast<uint32_t*>(xdig + b * 128 + c3 * 32 + v2 * 4);
+#pragma unroll
+        for (int gd = 0; gd < 4; ++gd) base[gd * 2] = words[gd];
+      } else {
+        // even block: lane t holds code bytes 2+4t..5+4t (t < 3) and 0, 1, 14, 15 (t = 3),
+        // so columns (4 c3, 4 c3 + 1) and (4 c3 + 2, 4 c3 + 3) land in two half-words
+        const uint32_t tA = c3 == 0 ? 3u : c3 - 1, vA = c3 == 0 ? 0u : 2u;
+        const uint32_t tB = c3 == 3 ? 3u : c3, vB = c3 == 3 ? 2u : 0u;
+        uint8_t* base = xdig + b * 128 + v2 * 4;
+#pragma unroll
+        for (int gd = 0; gd < 4; ++gd) {
+          *reinterpret_cast<uint16_t*>(base + tA * 32 + gd * 8 + vA) = static_cast<uint16_t>(words[gd]);
+          *reinterpret_cast<uint16_t*>(base + tB * 32 + gd * 8 + vB) = static_cast<uint16_t>(words[gd] >> 16);
+        }
+      }
+      if (c == 0) {
+        xsc[2 * b] = __uint_as_float(static_cast<uint32_t>(123 - s) << 23);      // digits 0, 1: 2^(-4-s)
+        xsc[2 * b + 1] = __uint_as_float(static_cast<uint32_t>(139 - s) << 23);  // digits 2, 3: 2^(12-s)
+      }
+    }
+  }
+  named_barrier(1, nthr);
+  const bool fallback = *bad_x != 0;
+  const uint32_t SG = p.Wk * p.nseg;  // warps per tile
+  const uint32_t gi = warp / SG, u = warp % SG, ks = u / p.Wk, kidx = u % p.Wk;
+  if (gi >= p.Gs) return;  // consumer warps beyond Gs * SG have no work
+  // this warp's share of its segment: block pairs [p0, p1)
+  const uint32_t kb = min(kSegBlk, p.nblk - ks * kSegBlk);
+  const uint32_t p0 = (kb / 2) * kidx / p.Wk, p1 = (kb / 2) * (kidx + 1) / p.Wk;
+  const uint32_t g = lane >> 2, t = lane & 3;
+  // Lane (g, t) holds one useful sum per MMA: t < 2 its C row g, columns 2t, 2t+1 (even
+  // block, digits 2t, 2t+1); t >= 2 its C row g + 8, columns 2t, 2t+1 (odd block, digits
+  // 2t-4, 2t-3). Its scale is xsc[2 blk_e + t] either way.
+  //
+  // Words of a 36-byte pair (w = 9 pr): w holds d_e and even codes 0, 1; w+1..w+3 even
+  // codes 2..13; w+4 even codes 14, 15 and d_o; w+5..w+8 odd codes. Lane t takes
+  // X1 = word w+1+t and X2 = word w (t = 2: w+4): even codes = X1 (t < 3) or bytes
+  // {X2.2, X2.3, X1.0, X1.1} (t = 3), its d = d_e (t < 2) or d_o; the x digits of even
+  // blocks are stored in this order. Odd codes = word w+5+t.
+  const uint32_t x1_off = 1 + t, x2_off = t == 2 ? 4u : 0u;
+  const uint32_t sel_code = t == 3 ? 0x1076u : 0x3210u;
+  const uint32_t sel_d = t < 2 ? 0x5454u : (t == 2 ? 0x7676u : 0x3232u);
+  const bool c_hi = t >= 2;
+  // B fragment of lane (g, t): column g, i.e. digit g & 3 of the even (g < 4) or odd block
+  const uint2* xd = reinterpret_cast<const uint2*>(xdig + (g >> 2) * 128 + (t * 4 + (g & 3u)) * 8);  // + 16 / block
+  const float* xs_l = xsc + t;                                                                          // + 2 / block
+  const uint32_t off_g = g * kRowStride, off_g8 = (g + 8) * kRowStride;
+  bool ok = true;
+  uint32_t m = 0;  // tiles this group has finished
+  for (uint32_t tl = gi; tl < R; tl += p.Gs, ++m) {
+    uint32_t j, r0, nrows;
+    locate_rt(p, rt_b + tl, j, r0, nrows);
+    float acc_g = 0.f, acc_g8 = 0.f;  // MMA path: rows g, g + 8
+    float facc[kTileRows];            // fallback path: every row, this lane's columns
+#pragma unroll
+    for (int r = 0; r < static_cast<int>(kTileRows); ++r) facc[r] = 0.f;
+    const uint32_t gt = tl * p.nseg + ks;
+    const uint32_t s = gt % p.NS;
+    // the slot must carry this stage (its sequence number), then its bytes
+    if (ok && tile_id[s] != gt) {
+      const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+      for (uint32_t i = 0; tile_id[s] != gt; ++i) {
+        __nanosleep(32);  // leave the issue slots to the warps that compute
+        if ((i & 63u) == 63u && (error_raised(p.err) || globaltimer_ns() - t0 > kWaitTimeoutNs)) {
+          record_error(p.err, EFG_ETIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+    }
+    ok = ok && mbar_wait(&full[s], (gt / p.NS) & 1u, p.err);
+    if (ok && !fallback) {
+      // Plain shared loads: the mbarrier wait above (an asm with a memory clobber) keeps
+      // them after the stage's bytes have landed.
+      const uint32_t* rw = reinterpret_cast<const uint32_t*>(ring + s * kStageBytes + off_g);
+      const uint32_t* rw8 = reinterpret_cast<const uint32_t*>(ring + s * kStageBytes + off_g8);
+#pragma unroll 4
+      for (uint32_t pr = p0; pr < p1; ++pr) {
+        const uint32_t w = pr * 9;  // a block pair is 36 bytes
+        const uint32_t X1 = rw[w + x1_off], X2 = rw[w + x2_off], Y = rw[w + 5 + t];
+        const uint32_t X18 = rw8[w + x1_off], X28 = rw8[w + x2_off], Y8 = rw8[w + 5 + t];
+        const uint32_t ce = __byte_perm(X1, X2, sel_code), ce8 = __byte_perm(X18, X28, sel_code);
+        const uint32_t db = __byte_perm(X1, X2, sel_d), db8 = __byte_perm(X18, X28, sel_d);
+        const uint32_t blk = ks * kSegBlk + 2 * pr;
+        const uint2 bf = xd[blk * 16];
+        const float sc = xs_l[2 * blk];
+        const uint32_t a[4] = {a_lo(ce), a_lo(Y), a_hi(ce), a_hi(Y)};
+        const uint32_t a8[4] = {a_lo(ce8), a_lo(Y8), a_hi(ce8), a_hi(Y8)};
+        int c[4], c8[4];
+        mma_s8(a, bf.x, bf.y, c);
+        mma_s8(a8, bf.x, bf.y, c8);
+        const int v = (c_hi ? c[2] : c[0]) + ((c_hi ? c[3] : c[1]) << 8);
+        const int v8 = (c_hi ? c8[2] : c8[0]) + ((c_hi ? c8[3] : c8[1]) << 8);
+        acc_g = fmaf(static_cast<float>(v), half_bits_to_float(db) * sc, acc_g);
+        acc_g8 = fmaf(static_cast<float>(v8), half_bits_to_float(db8) * sc, acc_g8);
+      }
+    } else if (ok) {
+      // plain FP32 dots (non-finite or out-of-range x): this warp's blocks, lane-strided
+      const uint8_t* st = ring + s * kStageBytes;
+      for (uint32_t r = 0; r < nrows; ++r)
+        for (uint32_t bb = 2 * p0 + lane; bb < 2 * p1; bb += 32) {
+          const uint8_t* blkp = st + r * kRowStride + bb * 18;
+          const float d = fp16_to_f32(blkp[0] | (blkp[1] << 8));
+          const uint32_t col0 = (ks * kSegBlk + bb) * 32;
+          float sacc = 0.f;
+          for (int k = 0; k < 32; ++k) {
+            const int cd = (k < 16 ? (blkp[2 + k] & 15) : (blkp[2 + k - 16] >> 4)) - 8;
+            float xv = __ldg(p.x + col0 + k);
+            if constexpr (NORM) xv = __ldg(p.norm_w + col0 + k) * (xv * inv);
+            sacc += static_cast<float>(cd) * xv;
+          }
+#pragma unroll
+          for (int qq = 0; qq < static_cast<int>(kTileRows); ++qq)
+            if (qq == static_cast<int>(r)) facc[qq] += d * sacc;
+        }
+    }
+    __syncwarp();
+    if (ok && lane == 0) mbar_arrive(&empty[s]);  // every read of this stage is done
+    // this warp's 16 row sums -> red[warp][m & 1], then the group adds them in warp order
+    float* mine = red + (warp * 2 + (m & 1u)) * kTileRows;
+    if (!fallback) {
+      acc_g += __shfl_xor_sync(0xFFFFFFFFu, acc_g, 1);
+      acc_g += __shfl_xor_sync(0xFFFFFFFFu, acc_g, 2);
+      acc_g8 += __shfl_xor_sync(0xFFFFFFFFu, acc_g8, 1);
+      acc_g8 += __shfl_xor_sync(0xFFFFFFFFu, acc_g8, 2);
+      if (t == 0) {
+        mine[g] = acc_g;
+        mine[g + 8] = acc_g8;
+      }
+    } else {
+#pragma unroll
+      for (int qq = 0; qq < static_cast<int>(kTileRows); ++qq) {
+        const float v = warp_sum(facc[qq]);
+        if (lane == 0) mine[qq] = v;
+      }
+    }
+    // Two buffers per warp: buffer m & 1 is rewritten two tiles later, after the group
+    // barrier of tile m + 1, which the group's first warp passes only once it has read
+    // tile m's sums.
+    if (SG > 1)
+      named_barrier(kGroupBarrier0 + gi, SG * 32);
+    else
+      __syncwarp();
+    if (u == 0 && lane < nrows) {
+      float v = 0.f;
+      for (uint32_t k = 0; k < SG; ++k) v += red[((gi * SG + k) * 2 + (m & 1u)) * kTileRows + lane];
+      float* y = p.jobs[j].y + (p.pos ? *p.pos * p.jobs[j].y_pos_stride : 0);
+      if (ok) y[r0 + lane] = E == Epi::Add ? y[r0 + lane] + v : v;
+    }
+  }
+}
+
+using MmaFn = void (*)(MmaParams);
+
+MmaFn pick_mma(Epi e, bool norm) {
+  if (e == Epi::Add) return norm ? matvec_q4_mma_kernel<Epi::Add, true> : matvec_q4_mma_kernel<Epi::Add, false>;
+  return norm ? matvec_q4_mma_kernel<Epi::Store, true> : matvec_q4_mma_kernel<Epi::Store, false>;
+}
+
+struct MmaPlan {
+  uint32_t nseg, NS, ring_offset, Wk, Gs;
+  size_t smem;
+};
+
+bool plan_mma(uint32_t nblk, const DeviceInfo& dev, MmaPlan& pl) {
+  if (nblk < kMinBlk || nblk > kMaxBlk || nblk % 8 != 0) return false;
+  pl.nseg = (nblk + kSegBlk - 1) / kSegBlk;
+  pl.ring_offset = (kXscOffset + nblk * 8 + nblk * 128 + 127) / 128 * 128;
+  const size_t optin = static_cast<size_t>(dev.smem_optin);
+  if (optin <= pl.ring_offset) return false;
+  pl.NS = static_cast<uint32_t>(std::min<size_t>(kMaxStages, (optin - pl.ring_offset) / kStageBytes));
+  if (pl.NS < 2) return false;
+  // 32 block pairs per stage, Wk warps on each: the Wk in 2..4 that leaves the fewest of
+  // the consumer warps idle (groups of Wk * nseg warps), the smaller Wk on ties
+  pl.Wk = 0;
+  uint32_t best_idle = kMmaConsumers + 1;
+  for (uint32_t wk = 2; wk <= 4; ++wk) {
+    const uint32_t sg = wk * pl.nseg;
+    if (sg > static_cast<uint32_t>(kMmaConsumers)) break;
+    const uint32_t idle = kMmaConsumers % sg;
+    if (idle < best_idle) {
+      best_idle = idle;
+      pl.Wk = wk;
+    }
+  }
+  if (pl.Wk == 0) return false;
+  pl.Gs = kMmaConsumers / (pl.Wk * pl.nseg);
+  pl.smem = pl.ring_offset + static_cast<size_t>(pl.NS) * kStageBytes;
+  return true;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver, looked up once.
+EncodeTiledFn encode_tiled() {
+  static const EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// W (rows x rb bytes, 16-byte aligned) as [rows][rb / 8] u64 with the box {146, 16}; the
+// box may reach past the row (zero fill) and past the last row (zero fill).
+bool encode_w_map(CUtensorMap* m, const uint8_t* W, uint32_t rows, uint32_t rb) {
+  const EncodeTiledFn fn = encode_tiled();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {rb / 8, rows};
+  const cuuint64_t strides[1] = {rb};
+  const cuuint32_t box[2] = {kBoxElems, kTileRows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(W), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool matvec_mma_ok(const MatvecArgs& a, const DeviceInfo& dev) {
+  if (a.fmt != Fmt::Q4 || a.epi == Epi::SwiGLU) return false;
+  if (a.cols == 0 || a.cols % 256 != 0 || a.cols / 32 < kMinBlk || a.cols / 32 > kMaxBlk) return false;
+  // x and the norm weights are read as float4
+  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || reinterpret_cast<uintptr_t>(a.norm_w) % 16 != 0) return false;
+  uint64_t bytes = 0;
+  for (int j = 0; j < a.n_jobs; ++j) {
+    if (reinterpret_cast<uintptr_t>(a.jobs[j].W) % 16 != 0) return false;
+    bytes += static_cast<uint64_t>(a.jobs[j].rows) * (a.cols / 32) * 18;
+  }
+  MmaPlan pl;
+  if (bytes < EFG_MMA_MIN_BYTES || !plan_mma(static_cast<uint32_t>(a.cols / 32), dev, pl)) return false;
+  CUtensorMap m;  // the driver must accept every job's map (else the CUDA-core kernel runs)
+  for (int j = 0; j < a.n_jobs; ++j)
+    if (a.jobs[j].rows && !encode_w_map(&m, a.jobs[j].W, a.jobs[j].rows, static_cast<uint32_t>(a.cols / 32 * 18)))
+      return false;
+  return true;
+}
+
+int launch_matvec_q4_mma(const MatvecArgs& a, const DeviceInfo& dev, int* d_err, cudaStream_t stream,
+                         bool direct_smem_attr) {
+  MmaParams p{};
+  p.x = a.x;
+  p.norm_w = a.norm_w;
+  p.norm_eps = a.norm_eps;
+  p.err = d_err;
+  p.pos = a.pos;
+  p.cols = static_cast<uint32_t>(a.cols);
+  p.nblk = p.cols / 32;
+  p.rb = p.nblk * 18;
+  MmaPlan pl;
+  if (!plan_mma(p.nblk, dev, pl)) return fail(EFG_EINVAL, "matvec: no MMA plan for %u columns", p.cols);
+  p.nseg = pl.nseg;
+  p.NS = pl.NS;
+  p.ring_offset = pl.ring_offset;
+  p.Wk = pl.Wk;
+  p.Gs = pl.Gs;
+  p.n_jobs = static_cast<uint32_t>(a.n_jobs);
+  uint32_t rt = 0;
+  for (int j = 0; j < a.n_jobs; ++j) {
+    p.jobs[j] = a.jobs[j];
+    if (a.jobs[j].rows && !encode_w_map(&p.maps[j], a.jobs[j].W, a.jobs[j].rows, p.rb))
+      return fail(EFG_ECUDA, "matvec: tensor map for a %u x %u Q4_0 matrix", a.jobs[j].rows, p.cols);
+    p.job_rt_start[j] = rt;
+    rt += (a.jobs[j].rows + kTileRows - 1) / kTileRows;
+  }
+  p.job_rt_start[a.n_jobs] = rt;
+  p.rt_total = rt;
+  if (rt == 0) return EFG_OK;
+  MmaFn fn = pick_mma(a.epi, a.norm_w != nullptr);
+  if (direct_smem_attr) {
+    EFG_TRY_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pl.smem)),
+                 "kernel shared-memory attribute");
+  } else if (int st = ensure_smem_attr(reinterpret_cast<const void*>(fn), pl.smem)) {
+    return st;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(std::min<uint32_t>(rt, static_cast<uint32_t>(dev.sm_count)));
+  cfg.blockDim = dim3(kMmaThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, fn, p), "matvec launch");
+  return EFG_OK;
+}
+
+}  // namespace efg
