@@ -452,6 +452,11 @@ def sharded_extra(torch, efg, world, rank, hbm_peak, steps=200, warmup=10, rows=
 
     ms_all = timed(lambda: efg.matvec_sharded(Q4_0, y, W, x, rows, cols, comm), steps)
     ms_local = timed(lambda: efg.matvec(Q4_0, y[b:], W, x, c, cols), steps)
+    efg.set_q4_mma(False)  # the same local matvec on the CUDA-core kernel, for comparison
+    try:
+        ms_local_cc = timed(lambda: efg.matvec(Q4_0, y[b:], W, x, c, cols), steps)
+    finally:
+        efg.set_q4_mma(True)
     comm.close()
     assert efg.device_error() == 0
     total = rows * rb + 4 * cols + 4 * rows
@@ -460,6 +465,9 @@ def sharded_extra(torch, efg, world, rank, hbm_peak, steps=200, warmup=10, rows=
     return {"us_per_step": round(ms_all * 1e3, 3), "gbs_total": round(total / (ms_all / 1e3) / 1e9, 1),
             "local_matvec_us": round(ms_local * 1e3, 3),
             "local_frac_of_hbm": round(shard_bytes / (ms_local / 1e3) / 1e9 / hbm_peak, 4),
+            "local_kernel": "int8 tensor-core MMA (efg_matvec_mma.cu)",
+            "local_matvec_us_cuda_cores": round(ms_local_cc * 1e3, 3),
+            "local_frac_of_hbm_cuda_cores": round(shard_bytes / (ms_local_cc / 1e3) / 1e9 / hbm_peak, 4),
             "gather_bytes": 4 * rows, "ranks": world, "rows_per_rank": c, "matrix_bytes": rows * rb,
             "scaling": "strong"}
 
@@ -524,8 +532,8 @@ def gemm_extra(torch, efg, bf16_peak, reps=20):
 
 def run_profile(args):
     """A few plain launches for ncu (no CPU legs): --profile q8 -> config 1 (Q8_0 32000x2048),
-    q4 -> config 0 (Q4_0 5632x2048), q4big -> Q4_0 16384x8192 (302 MB, a slice of config 4's
-    rows), gemm -> config 3 (5632x2048, B=64), decode / decode_persistent -> config 2, four
+    q4 -> config 0 (Q4_0 5632x2048), q4big -> Q4_0 65536x8192 (302 MB, half of config 4's
+    rows, on the tensor-core kernel), gemm -> config 3 (5632x2048, B=64), decode / decode_persistent -> config 2, four
     single-token forwards in each decode mode."""
     import torch
 
@@ -552,7 +560,7 @@ def run_profile(args):
         print(json.dumps({"profile": args.profile, "forwards": 4}))
         return 0
     qt, rows, cols, copies = {"q8": (Q8_0, ROWS, COLS, 3), "q4": (Q4_0, 5632, 2048, 24),
-                              "q4big": (Q4_0, 16384, 8192, 1)}[args.profile]
+                              "q4big": (Q4_0, 65536, 8192, 1)}[args.profile]
     Ws = make_weights(efg, torch, qt, rows, cols, copies, seed=1)
     x = torch.randn(cols, device="cuda")
     y = torch.empty(rows, device="cuda")

@@ -35,6 +35,7 @@ from .api import (  # noqa: F401
     quantize_rows,
     row_bytes,
     row_f32,
+    set_q4_mma,
     set_weight_prefetch,
     shard_rows,
 )

@@ -124,6 +124,13 @@ def row_f32(out, qtype: int, W, rows: int, cols: int, r: int | None = None, r_de
     check(load().efg_row_f32(_ptr(out), int(qtype), _ptr(W), rows, cols, rp, r or 0, _stream()))
 
 
+def set_q4_mma(enable: bool) -> bool:
+    """efg_set_q4_mma: large Q4_0 matvecs on this thread use the integer tensor-core
+    kernel (True, the default) or the CUDA-core kernel (False). Returns the previous
+    setting."""
+    return bool(load().efg_set_q4_mma(int(enable)))
+
+
 def set_weight_prefetch(enable: bool) -> bool:
     """efg_set_weight_prefetch: lets later matvec launches on this thread stream their
     weights while the previous kernel finishes (weights must not be written just

@@ -145,6 +145,12 @@ int efg_set_weight_prefetch(int enable) {
   return old ? 1 : 0;
 }
 
+int efg_set_q4_mma(int enable) {
+  const bool old = q4_mma_flag();
+  q4_mma_flag() = enable != 0;
+  return old ? 1 : 0;
+}
+
 uint64_t efg_row_bytes(int qtype, uint64_t cols) {
   switch (qtype) {
     case EFG_F32: return cols * 4;

@@ -20,6 +20,11 @@ bool& weight_prefetch_flag() {
   return on;
 }
 
+bool& q4_mma_flag() {
+  static thread_local bool on = true;
+  return on;
+}
+
 int ensure_smem_attr(const void* fn, size_t bytes) {
   static std::mutex mu;
   static std::map<std::pair<int, const void*>, size_t> done;

@@ -30,6 +30,9 @@ struct DeviceInfo {
 // Thread-local default for MatvecArgs::pdl in the C-ABI calls (efg_set_weight_prefetch).
 bool& weight_prefetch_flag();
 
+// Thread-local switch for the tensor-core Q4_0 matvec on large matrices (efg_set_q4_mma).
+bool& q4_mma_flag();
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel, size);
 // later calls are free, so launches can be captured into CUDA graphs.
 int ensure_smem_attr(const void* fn, size_t bytes);

@@ -56,7 +56,7 @@
 namespace efg {
 namespace {
 
-constexpr int kMmaConsumers = 16;
+constexpr int kMmaConsumers = 12;
 constexpr int kMmaThreads = (kMmaConsumers + 1) * 32;
 constexpr uint32_t kTileRows = 16;
 constexpr uint32_t kMinBlk = 64;          // cols >= 2048

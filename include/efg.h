@@ -72,6 +72,15 @@ int efg_device_error(int* code);
  * just before it, which holds for model weights loaded once. Returns the old setting. */
 int efg_set_weight_prefetch(int enable);
 
+/* Which kernel computes the Q4_0 matvec calls made afterwards on this thread for large
+ * matrices (48 MB and more, 2048 <= cols <= 8192, cols % 256 == 0, 16-byte aligned W, x
+ * and norm weights). 1 (the default): the integer tensor-core kernel, exact int8 x int8
+ * products of the codes and a 30-bit fixed-point x, which keeps HBM busier than the
+ * CUDA-core kernel can on B200. 0: the CUDA-core kernel for every size. Both meet the
+ * reference's tolerance (test_qinfer.cpp:58-67). Returns the old setting. No reference
+ * counterpart: the reference has one CPU kernel per format. */
+int efg_set_q4_mma(int enable);
+
 /* Bytes of one row of `cols` weights, or 0 with efg_last_error() set when a block type
  * gets cols % 32 != 0. Replaces ef::qtype_row_bytes (include/ef/quant.h:42,
  * src/quant.cpp:136-149), which throws in that case. */

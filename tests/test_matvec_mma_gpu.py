@@ -93,6 +93,27 @@ def test_mma_path_nan_x(cuda):
     assert efg.device_error() == 0
 
 
+def test_switch_to_cuda_cores(cuda, oracle):
+    """efg_set_q4_mma(0) sends the same call to the CUDA-core kernel: same tolerance, and
+    the two kernels agree to rounding."""
+    import torch
+
+    rows, cols = 16384, 8192
+    W = _weights(torch, rows, cols, 9)
+    x = torch.randn(cols, device="cuda")
+    y_mma, y_cc = torch.empty(rows, device="cuda"), torch.empty(rows, device="cuda")
+    efg.matvec_q4_0(y_mma, W, x, rows, cols)
+    assert efg.set_q4_mma(False) is True
+    try:
+        efg.matvec_q4_0(y_cc, W, x, rows, cols)
+    finally:
+        assert efg.set_q4_mma(True) is False
+    torch.cuda.synchronize()
+    _check(oracle, W, x, rows, y_cc)
+    _check(oracle, W, x, rows, y_mma)
+    assert not torch.equal(y_mma, y_cc)  # different arithmetic, so the switch took effect
+
+
 def test_unaligned_x_takes_the_other_kernel(cuda, oracle):
     """x at a 4-byte offset cannot be read as float4: the CUDA-core kernel runs instead."""
     import torch
