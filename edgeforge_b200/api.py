@@ -358,6 +358,15 @@ class Decoder:
                                          C.c_void_p(out.ctypes.data) if out is not None else None))
         return out
 
+    def prefill(self, tokens, pos0: int = 0, compute_logits: bool = True) -> np.ndarray | None:
+        """efg_decoder_prefill: tokens at positions pos0.. as one batch (Q4_0 projections on
+        the tensor-core GEMM); the last token's logits or None."""
+        arr = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(self.vocab, np.float32) if compute_logits else None
+        check(load().efg_decoder_prefill(self._h, C.c_void_p(arr.ctypes.data), len(arr), int(pos0),
+                                         C.c_void_p(out.ctypes.data) if out is not None else None))
+        return out
+
     def generate(self, prompt, max_new: int, eos_id: int = -1, forced=None,
                  keep_step_logits: bool = False) -> GreedyResult:
         """ef::generate_greedy (src/model.cpp:278-304). `forced` (max_new ids) teacher-forces

@@ -28,6 +28,7 @@
 #include "../../include/efg.h"
 #include "efg_device.cuh"
 #include "efg_efq.h"
+#include "efg_gemm.cuh"
 #include "efg_host.h"
 #include "efg_matvec.cuh"
 #include "efg_decode_mk.cuh"
@@ -50,7 +51,25 @@ cudaLaunchConfig_t cfg_of(dim3 grid, dim3 block, size_t smem, cudaStream_t s, cu
   return c;
 }
 
-// x = row tokens[*pos] of the embedding table (src/qkernels.cpp:299-305).
+// Bytes of one embedding row and element i of it as float (src/qkernels.cpp:299-305).
+__device__ __forceinline__ uint64_t embed_row_bytes(int type, uint32_t dim) {
+  return type == 0 ? 4ull * dim : type <= 2 ? 2ull * dim : dim / 32ull * (type == 3 ? 34 : 18);
+}
+__device__ __forceinline__ float embed_value(const uint8_t* __restrict__ row, int type, uint32_t i) {
+  if (type == 2) return bf16_to_f32(row[2 * i] | (row[2 * i + 1] << 8));
+  if (type == 1) return fp16_to_f32(row[2 * i] | (row[2 * i + 1] << 8));
+  if (type == 0)
+    return __uint_as_float(row[4 * i] | (row[4 * i + 1] << 8) | (row[4 * i + 2] << 16) |
+                           (static_cast<uint32_t>(row[4 * i + 3]) << 24));
+  const uint8_t* blk = row + (i / 32) * (type == 3 ? 34 : 18);
+  const int j = i % 32;
+  const float d = fp16_to_f32(blk[0] | (blk[1] << 8));
+  const int code = type == 4 ? (j < 16 ? (blk[2 + j] & 15) : (blk[2 + j - 16] >> 4)) - 8
+                             : static_cast<int8_t>(blk[2 + j]);
+  return __fmul_rn(static_cast<float>(code), d);
+}
+
+// x = row tokens[*pos] of the embedding table.
 __global__ void embed_kernel(const uint8_t* __restrict__ table, int type, uint32_t vocab, uint32_t dim,
                              const int32_t* __restrict__ tokens, const int32_t* __restrict__ pos,
                              float* __restrict__ x, int* err) {
@@ -61,71 +80,47 @@ __global__ void embed_kernel(const uint8_t* __restrict__ table, int type, uint32
     if (threadIdx.x == 0 && blockIdx.x == 0) record_error(err, EFG_EINVAL);
     return;
   }
-  const uint64_t rb = type == 0 ? 4ull * dim : type <= 2 ? 2ull * dim : dim / 32ull * (type == 3 ? 34 : 18);
-  const uint8_t* row = table + static_cast<uint64_t>(tok) * rb;
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
-    float v;
-    if (type == 2) {
-      v = bf16_to_f32(row[2 * i] | (row[2 * i + 1] << 8));
-    } else if (type == 1) {
-      v = fp16_to_f32(row[2 * i] | (row[2 * i + 1] << 8));
-    } else if (type == 0) {
-      v = __uint_as_float(row[4 * i] | (row[4 * i + 1] << 8) | (row[4 * i + 2] << 16) |
-                          (static_cast<uint32_t>(row[4 * i + 3]) << 24));
-    } else {
-      const uint8_t* blk = row + (i / 32) * (type == 3 ? 34 : 18);
-      const int j = i % 32;
-      const float d = fp16_to_f32(blk[0] | (blk[1] << 8));
-      const int code = type == 4 ? (j < 16 ? (blk[2 + j] & 15) : (blk[2 + j - 16] >> 4)) - 8
-                                 : static_cast<int8_t>(blk[2 + j]);
-      v = __fmul_rn(static_cast<float>(code), d);
-    }
-    x[i] = v;
-  }
+  const uint8_t* row = table + static_cast<uint64_t>(tok) * embed_row_bytes(type, dim);
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+    x[i] = embed_value(row, type, i);
 }
 
-// One query head per CTA (src/kernels.cpp:133-174): RoPE of q and of the new key (half-split
-// rotation, HF order a*c - b*s, b*c + a*s), the key written to the cache at pos by the first
-// head of each KV group, scores scaled by 1/sqrt(hd), softmax with a double sum, then the
-// probability-weighted sum of the cached values in position order.
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(
-    const float* __restrict__ q, const float* __restrict__ knew, float* __restrict__ k_layer,
-    const float* __restrict__ v_layer, float* __restrict__ ctx, const float* __restrict__ rope_cos,
-    const float* __restrict__ rope_sin, const int32_t* __restrict__ pos_p, int H, int KV, int hd, int max_seq,
-    int* err) {
-  extern __shared__ float sm[];
-  float* qh = sm;            // [hd]
-  float* kn = qh + hd;       // [hd]
-  float* sc = kn + hd;       // [max_seq]
-  __shared__ float red_f[kAttnThreads / 32];
-  __shared__ double red_d[kAttnThreads / 32];
+// Batched prefill: row b of xb = embedding row of tokens[b], b < n (grid.y = n).
+__global__ void embed_rows_kernel(const uint8_t* __restrict__ table, int type, uint32_t vocab, uint32_t dim,
+                                  const int32_t* __restrict__ tokens, float* __restrict__ xb, int* err) {
   pdl_wait();
   pdl_launch_dependents();
-  const int pos = *pos_p;
-  if (pos < 0 || pos >= max_seq) {
-    if (threadIdx.x == 0) record_error(err, EFG_ESTATE);
+  const int32_t tok = tokens[blockIdx.y];
+  if (tok < 0 || static_cast<uint32_t>(tok) >= vocab) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) record_error(err, EFG_EINVAL);
     return;
   }
-  const int h = blockIdx.x, group = H / KV, kv = h / group, half = hd / 2, kvd = KV * hd;
+  const uint8_t* row = table + static_cast<uint64_t>(tok) * embed_row_bytes(type, dim);
+  float* x = xb + static_cast<size_t>(blockIdx.y) * dim;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+    x[i] = embed_value(row, type, i);
+}
+
+// q_h and k_h rotated by RoPE at position pos (half-split rotation, HF order a*c - b*s,
+// b*c + a*s; src/kernels.cpp:133-147).
+__device__ __forceinline__ void rope_pair(float a, float b, float c, float s, float& ra, float& rb) {
+  ra = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+  rb = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+}
+
+// Softmax attention of one rotated query head qh (shared memory) over the cached keys and
+// values of positions 0..n_pos-1 of KV head kv (src/kernels.cpp:148-174): scores scaled by
+// 1/sqrt(hd), softmax with a double sum, then the probability-weighted sum of the values in
+// position order into out[0..hd). The key of position n_pos-1 is read from k_last.
+__device__ void attend_head(const float* __restrict__ qh, const float* __restrict__ k_layer,
+                            const float* __restrict__ v_layer, const float* __restrict__ k_last, int kv, int hd,
+                            int kvd, int n_pos, float* __restrict__ sc, float* red_f, double* red_d,
+                            float* __restrict__ out) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  const float* c = rope_cos + static_cast<size_t>(pos) * half;
-  const float* s = rope_sin + static_cast<size_t>(pos) * half;
-  for (int i = tid; i < half; i += blockDim.x) {
-    const float a = q[h * hd + i], b = q[h * hd + i + half];
-    qh[i] = __fsub_rn(__fmul_rn(a, c[i]), __fmul_rn(b, s[i]));
-    qh[i + half] = __fadd_rn(__fmul_rn(b, c[i]), __fmul_rn(a, s[i]));
-    const float ka = knew[kv * hd + i], kb = knew[kv * hd + i + half];
-    kn[i] = __fsub_rn(__fmul_rn(ka, c[i]), __fmul_rn(kb, s[i]));
-    kn[i + half] = __fadd_rn(__fmul_rn(kb, c[i]), __fmul_rn(ka, s[i]));
-  }
-  __syncthreads();
-  if (h % group == 0)
-    for (int i = tid; i < hd; i += blockDim.x) k_layer[static_cast<size_t>(pos) * kvd + kv * hd + i] = kn[i];
   const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));
-  const int n_pos = pos + 1;
   float mx = -INFINITY;
   for (int t = tid; t < n_pos; t += blockDim.x) {
-    const float* kt = t == pos ? kn : k_layer + static_cast<size_t>(t) * kvd + kv * hd;
+    const float* kt = t == n_pos - 1 ? k_last : k_layer + static_cast<size_t>(t) * kvd + kv * hd;
     // dot with 8 partial sums combined pairwise (src/kernels.cpp:28-43)
     float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     int i = 0;
@@ -163,8 +158,87 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
     float acc = 0.f;
     for (int t = 0; t < n_pos; ++t)
       acc = __fadd_rn(acc, __fmul_rn(sc[t], v_layer[static_cast<size_t>(t) * kvd + kv * hd + d]));
-    ctx[h * hd + d] = acc;
+    out[d] = acc;
   }
+}
+
+// One query head per CTA: RoPE of q and of the new key, the key written to the cache at pos
+// by the first head of each KV group, then attend_head over pos + 1 positions.
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(
+    const float* __restrict__ q, const float* __restrict__ knew, float* __restrict__ k_layer,
+    const float* __restrict__ v_layer, float* __restrict__ ctx, const float* __restrict__ rope_cos,
+    const float* __restrict__ rope_sin, const int32_t* __restrict__ pos_p, int H, int KV, int hd, int max_seq,
+    int* err) {
+  extern __shared__ float sm[];
+  float* qh = sm;            // [hd]
+  float* kn = qh + hd;       // [hd]
+  float* sc = kn + hd;       // [max_seq]
+  __shared__ float red_f[kAttnThreads / 32];
+  __shared__ double red_d[kAttnThreads / 32];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pos = *pos_p;
+  if (pos < 0 || pos >= max_seq) {
+    if (threadIdx.x == 0) record_error(err, EFG_ESTATE);
+    return;
+  }
+  const int h = blockIdx.x, group = H / KV, kv = h / group, half = hd / 2, kvd = KV * hd;
+  const int tid = threadIdx.x;
+  const float* c = rope_cos + static_cast<size_t>(pos) * half;
+  const float* s = rope_sin + static_cast<size_t>(pos) * half;
+  for (int i = tid; i < half; i += blockDim.x) {
+    rope_pair(q[h * hd + i], q[h * hd + i + half], c[i], s[i], qh[i], qh[i + half]);
+    rope_pair(knew[kv * hd + i], knew[kv * hd + i + half], c[i], s[i], kn[i], kn[i + half]);
+  }
+  __syncthreads();
+  if (h % group == 0)
+    for (int i = tid; i < hd; i += blockDim.x) k_layer[static_cast<size_t>(pos) * kvd + kv * hd + i] = kn[i];
+  attend_head(qh, k_layer, v_layer, kn, kv, hd, kvd, pos + 1, sc, red_f, red_d, ctx + h * hd);
+}
+
+// Batched prefill: rotate the keys of positions p0..p0+n-1, written unrotated into the
+// cache by the k projection, in place (grid.x = n, one position per CTA).
+__global__ void rope_keys_kernel(float* __restrict__ k_layer, const float* __restrict__ rope_cos,
+                                 const float* __restrict__ rope_sin, int p0, int KV, int hd) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int pos = p0 + static_cast<int>(blockIdx.x), half = hd / 2, kvd = KV * hd;
+  const float* c = rope_cos + static_cast<size_t>(pos) * half;
+  const float* s = rope_sin + static_cast<size_t>(pos) * half;
+  float* kr = k_layer + static_cast<size_t>(pos) * kvd;
+  for (int e = threadIdx.x; e < KV * half; e += blockDim.x) {
+    const int kv = e / half, i = e % half;
+    float ra, rb;
+    rope_pair(kr[kv * hd + i], kr[kv * hd + i + half], c[i], s[i], ra, rb);
+    kr[kv * hd + i] = ra;
+    kr[kv * hd + i + half] = rb;
+  }
+}
+
+// Batched prefill: query head blockIdx.x of token blockIdx.y (position p0 + blockIdx.y),
+// RoPE of q, then attend_head over the cache, which holds every rotated key up to its
+// position (causal: later tokens of the batch are not read).
+__global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(
+    const float* __restrict__ qb, const float* __restrict__ k_layer, const float* __restrict__ v_layer,
+    float* __restrict__ ctxb, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, int p0, int H,
+    int KV, int hd, int dim) {
+  extern __shared__ float sm[];
+  float* qh = sm;       // [hd]
+  float* sc = qh + hd;  // [max_seq]
+  __shared__ float red_f[kAttnThreads / 32];
+  __shared__ double red_d[kAttnThreads / 32];
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.y, pos = p0 + b;
+  const int h = blockIdx.x, group = H / KV, kv = h / group, half = hd / 2, kvd = KV * hd;
+  const float* q = qb + static_cast<size_t>(b) * dim;
+  const float* c = rope_cos + static_cast<size_t>(pos) * half;
+  const float* s = rope_sin + static_cast<size_t>(pos) * half;
+  for (int i = threadIdx.x; i < half; i += blockDim.x)
+    rope_pair(q[h * hd + i], q[h * hd + i + half], c[i], s[i], qh[i], qh[i + half]);
+  __syncthreads();
+  attend_head(qh, k_layer, v_layer, k_layer + static_cast<size_t>(pos) * kvd + kv * hd, kv, hd, kvd, pos + 1, sc,
+              red_f, red_d, ctxb + static_cast<size_t>(b) * dim + h * hd);
 }
 
 // out = silu(gate) * up (src/kernels.cpp:94-99), for the unfused path.
@@ -178,13 +252,10 @@ __global__ void swiglu_kernel(float* __restrict__ out, const float* __restrict__
   }
 }
 
-// h = w * (x * inv) with inv = float(1 / sqrt(mean(x^2) + eps)) (src/kernels.cpp:69-75), for
-// the unfused path; one CTA.
-__global__ void rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ x, const float* __restrict__ w,
-                               uint32_t n, float eps) {
-  __shared__ double red[32];
-  pdl_wait();
-  pdl_launch_dependents();
+// h = w * (x * inv) with inv = float(1 / sqrt(mean(x^2) + eps)) (src/kernels.cpp:69-75), by
+// one CTA.
+__device__ __forceinline__ void rmsnorm_row(float* __restrict__ h, const float* __restrict__ x,
+                                            const float* __restrict__ w, uint32_t n, float eps, double* red) {
   double ss = 0.0;
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss += static_cast<double>(x[i]) * static_cast<double>(x[i]);
   ss = warp_sum_d(ss);
@@ -194,6 +265,34 @@ __global__ void rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ 
   for (uint32_t k = 0; k < blockDim.x / 32; ++k) tot += red[k];
   const float inv = static_cast<float>(1.0 / sqrt((n ? tot / n : 0.0) + static_cast<double>(eps)));
   for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) h[i] = __fmul_rn(w[i], __fmul_rn(x[i], inv));
+}
+
+// RMSNorm for the unfused path; one CTA.
+__global__ void rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ x, const float* __restrict__ w,
+                               uint32_t n, float eps) {
+  __shared__ double red[32];
+  pdl_wait();
+  pdl_launch_dependents();
+  rmsnorm_row(h, x, w, n, eps, red);
+}
+
+// Batched prefill: RMSNorm of every row of xb into hb (one CTA per row).
+__global__ void rmsnorm_rows_kernel(float* __restrict__ hb, const float* __restrict__ xb,
+                                    const float* __restrict__ w, uint32_t n, float eps) {
+  __shared__ double red[32];
+  pdl_wait();
+  pdl_launch_dependents();
+  const size_t o = static_cast<size_t>(blockIdx.x) * n;
+  rmsnorm_row(hb + o, xb + o, w, n, eps, red);
+}
+
+// Residual add x += y (src/model.cpp:247-249, 260-262), elementwise.
+__global__ void add_kernel(float* __restrict__ x, const float* __restrict__ y, size_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    x[i] = __fadd_rn(x[i], y[i]);
 }
 
 // Index of the first maximum of logits (src/kernels.cpp:105-111); records it, makes it the
@@ -301,6 +400,11 @@ struct Decoder {
   float* d_keep = nullptr;        // per-step logits kept by generate
   size_t keep_cap = 0;
   int grid = 0;
+  // batched prefill (prefill_tokens): [P][hidden] x5, [P][intermediate] x3, allocated on first use
+  float* pb = nullptr;
+  float *xb = nullptr, *hb = nullptr, *qb = nullptr, *cb = nullptr, *ob = nullptr, *gb = nullptr, *ub = nullptr,
+        *ab = nullptr;
+  size_t pb_rows = 0;
   int32_t* pos_p() const { return state; }
   int32_t* nfix_p() const { return state + 1; }
   int32_t* tokens() const { return state + 2; }
@@ -313,6 +417,40 @@ int check_mat(const Mat& m, const char* name) {
   if (m.type != 3 && m.type != 4)
     return fail(EFG_EINVAL, "matrix '%s' is stored as %s; the B200 decode step runs Q4_0 and Q8_0 matrices", name,
                 efq::type_name(m.type));
+  return EFG_OK;
+}
+
+// logits = lm_head . rmsnorm(x, final_norm) (src/model.cpp:266-270).
+int enqueue_lm_head(Decoder& D, const float* x, cudaStream_t s) {
+  cudaLaunchAttribute attr[1];
+  const uint32_t Dm = static_cast<uint32_t>(D.c.hidden);
+  MatvecArgs a;
+  a.fmt = D.lm_head.type == 4 ? Fmt::Q4 : Fmt::Q8;
+  a.x = x;
+  a.norm_w = D.final_norm;
+  a.norm_eps = static_cast<float>(D.c.rms_eps);
+  a.cols = Dm;
+  a.pdl = true;
+  a.n_jobs = 1;
+  a.jobs[0] = MatvecJobDev{D.lm_head.w, D.logits, D.lm_head.rows, 0};
+  if (!matvec_fast_path_ok(a)) {
+    cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(256), 0, s, attr);
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rmsnorm_kernel, D.h, x, D.final_norm, Dm, static_cast<float>(D.c.rms_eps)),
+                 "rmsnorm launch");
+    a.x = D.h;
+    a.norm_w = nullptr;
+  }
+  return launch_matvec(a, D.d_err, s);
+}
+
+// Next token = argmax(logits) at the device-side position, which then advances.
+int enqueue_argmax(Decoder& D, cudaStream_t s) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(1024), 0, s, attr);
+  EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, argmax_kernel, static_cast<const float*>(D.logits),
+                                  static_cast<uint32_t>(D.c.vocab), D.tokens(), D.out_tokens(), D.pos_p(),
+                                  static_cast<const int32_t*>(D.nfix_p()), static_cast<int>(D.max_seq)),
+               "argmax launch");
   return EFG_OK;
 }
 
@@ -432,29 +570,8 @@ int enqueue_step(Decoder& D, bool logits, cudaStream_t s) {
     }
   }
   if (logits) {
-    MatvecArgs a;
-    a.fmt = D.lm_head.type == 4 ? Fmt::Q4 : Fmt::Q8;
-    a.x = D.x;
-    a.norm_w = D.final_norm;
-    a.norm_eps = static_cast<float>(D.c.rms_eps);
-    a.cols = Dm;
-    a.pdl = true;
-    a.n_jobs = 1;
-    a.jobs[0] = MatvecJobDev{D.lm_head.w, D.logits, D.lm_head.rows, 0};
-    if (!matvec_fast_path_ok(a)) {
-      cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(256), 0, s, attr);
-      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rmsnorm_kernel, D.h, static_cast<const float*>(D.x), D.final_norm, Dm,
-                                      static_cast<float>(D.c.rms_eps)),
-                   "rmsnorm launch");
-      a.x = D.h;
-      a.norm_w = nullptr;
-    }
-    if (int st = launch_matvec(a, D.d_err, s)) return st;
-    cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(1024), 0, s, attr);
-    EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, argmax_kernel, static_cast<const float*>(D.logits), V, D.tokens(),
-                                    D.out_tokens(), D.pos_p(), static_cast<const int32_t*>(D.nfix_p()),
-                                    static_cast<int>(D.max_seq)),
-                 "argmax launch");
+    if (int st = enqueue_lm_head(D, D.x, s)) return st;
+    if (int st = enqueue_argmax(D, s)) return st;
   } else {
     cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(32), 0, s, attr);
     EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, advance_kernel, D.pos_p()), "advance launch");
@@ -664,6 +781,7 @@ void destroy(Decoder* D) {
   if (D->stream) cudaStreamSynchronize(D->stream);
   if (D->g_full) cudaGraphExecDestroy(D->g_full);
   if (D->g_prefill) cudaGraphExecDestroy(D->g_prefill);
+  if (D->pb) cudaFree(D->pb);
   for (void* p : {static_cast<void*>(D->d_data), static_cast<void*>(D->kc), static_cast<void*>(D->vc),
                   static_cast<void*>(D->rcos), static_cast<void*>(D->rsin), static_cast<void*>(D->x),
                   static_cast<void*>(D->state), static_cast<void*>(D->d_phases), static_cast<void*>(D->d_bar),
@@ -756,10 +874,14 @@ int open_decoder(const char* path, size_t max_seq, Decoder** out) {
   const size_t attn_smem = (2 * static_cast<size_t>(c.head_dim) + max_seq) * sizeof(float);
   if (attn_smem > 227 * 1024)
     return fail(EFG_EINVAL, "decoder: max_seq %zu is too long for the attention kernel", max_seq);
-  if (attn_smem > 48 * 1024)
+  if (attn_smem > 48 * 1024) {
     EFG_TRY_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(attn_smem)),
                  "attention smem attribute");
+    EFG_TRY_CUDA(cudaFuncSetAttribute(attention_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(attn_smem)),
+                 "attention smem attribute");
+  }
   const size_t cache = static_cast<size_t>(c.layers) * max_seq * kvd;
   EFG_TRY_CUDA(cudaMalloc(&D->kc, cache * sizeof(float)), "KV cache allocation");
   EFG_TRY_CUDA(cudaMalloc(&D->vc, cache * sizeof(float)), "KV cache allocation");
@@ -803,6 +925,123 @@ int open_decoder(const char* path, size_t max_seq, Decoder** out) {
   if (int st = build_mk(*D)) return st;
   D->use_mk = false;  // the per-operation graphs are faster today; the persistent kernel is opt-in
   *out = D.release();
+  return EFG_OK;
+}
+
+// ---------------------------------------------------------------- batched prefill
+// The prompt through the same layers as a batch of tokens (README.md:89-90 names the
+// token-by-token prompt as the reference's limit): the Q4_0 projections of every token in
+// one tensor-core GEMM per matrix, Q8_0 projections one matvec per token, then batched
+// RMSNorm, key RoPE, causal attention, SwiGLU and residual adds. Equivalent to forward() at
+// positions p0..p0+n-1 in turn.
+constexpr size_t kPrefillRows = 64;  // tokens per pass
+
+int ensure_prefill_buffers(Decoder& D) {
+  if (D.pb) return EFG_OK;
+  const size_t P = std::min(kPrefillRows, D.max_seq), Dm = static_cast<size_t>(D.c.hidden),
+               F = static_cast<size_t>(D.c.intermediate);
+  auto al = [](size_t n) { return (n * sizeof(float) + 255) / 256 * 256; };
+  EFG_TRY_CUDA(cudaMalloc(&D.pb, al(P * Dm) * 5 + al(P * F) * 3), "prefill buffer allocation");
+  uint8_t* a = reinterpret_cast<uint8_t*>(D.pb);
+  size_t o = 0;
+  for (float** b : {&D.xb, &D.hb, &D.qb, &D.cb, &D.ob}) *b = reinterpret_cast<float*>(a + o), o += al(P * Dm);
+  for (float** b : {&D.gb, &D.ub, &D.ab}) *b = reinterpret_cast<float*>(a + o), o += al(P * F);
+  D.pb_rows = P;
+  return EFG_OK;
+}
+
+// Y[b] = M . X[b] for b < n (X [n][M.cols], Y [n][M.rows]).
+int batched_proj(Decoder& D, const Mat& M, const float* X, float* Y, size_t n, cudaStream_t s) {
+  if (M.type == 4) return launch_gemm_q4_0(Y, M.w, X, M.rows, M.cols, n, D.d_err, s);
+  for (size_t b = 0; b < n; ++b) {
+    MatvecArgs a;
+    a.fmt = Fmt::Q8;
+    a.x = X + b * M.cols;
+    a.cols = M.cols;
+    a.pdl = true;
+    a.n_jobs = 1;
+    a.jobs[0] = MatvecJobDev{M.w, Y + b * M.rows, M.rows, 0};
+    if (int st = launch_matvec(a, D.d_err, s)) return st;
+  }
+  return EFG_OK;
+}
+
+// Tokens tokens()[p0..p0+n) (already on the device), n <= pb_rows; with `logits`, the last
+// token's logits in D.logits.
+int prefill_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s) {
+  cudaLaunchAttribute attr[1];
+  const uint32_t Dm = static_cast<uint32_t>(D.c.hidden), F = static_cast<uint32_t>(D.c.intermediate),
+                 V = static_cast<uint32_t>(D.c.vocab);
+  const size_t kvd = static_cast<size_t>(D.c.kv_dim());
+  const int H = static_cast<int>(D.c.heads), KV = static_cast<int>(D.c.kv_heads), hd = static_cast<int>(D.c.head_dim);
+  const float eps = static_cast<float>(D.c.rms_eps);
+  const unsigned nb = static_cast<unsigned>(n);
+  auto grid_for = [](size_t count) { return dim3(static_cast<unsigned>(std::max<size_t>(1, std::min<size_t>(592, (count + 255) / 256)))); };
+  {
+    cudaLaunchConfig_t cf = cfg_of(dim3(std::max(1u, std::min(16u, (Dm + 255) / 256)), nb), dim3(256), 0, s, attr);
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, embed_rows_kernel, D.embed.w, D.embed.type, V, Dm,
+                                    static_cast<const int32_t*>(D.tokens() + p0), D.xb, D.d_err),
+                 "embed launch");
+  }
+  for (size_t l = 0; l < D.layers.size(); ++l) {
+    const Layer& Ly = D.layers[l];
+    float* kl = D.kc + l * D.max_seq * kvd;
+    float* vl = D.vc + l * D.max_seq * kvd;
+    cudaLaunchConfig_t cn = cfg_of(dim3(nb), dim3(256), 0, s, attr);
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cn, rmsnorm_rows_kernel, D.hb, static_cast<const float*>(D.xb), Ly.attn_norm, Dm,
+                                    eps),
+                 "rmsnorm launch");
+    if (int st = batched_proj(D, Ly.q, D.hb, D.qb, n, s)) return st;
+    if (int st = batched_proj(D, Ly.k, D.hb, kl + p0 * kvd, n, s)) return st;  // unrotated keys, rotated below
+    if (int st = batched_proj(D, Ly.v, D.hb, vl + p0 * kvd, n, s)) return st;
+    {
+      cudaLaunchConfig_t cf = cfg_of(dim3(nb), dim3(128), 0, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rope_keys_kernel, kl, static_cast<const float*>(D.rcos),
+                                      static_cast<const float*>(D.rsin), static_cast<int>(p0), KV, hd),
+                   "rope launch");
+    }
+    {
+      const size_t smem = (hd + D.max_seq) * sizeof(float);
+      cudaLaunchConfig_t cf = cfg_of(dim3(H, nb), dim3(kAttnThreads), smem, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, attention_rows_kernel, static_cast<const float*>(D.qb),
+                                      static_cast<const float*>(kl), static_cast<const float*>(vl), D.cb,
+                                      static_cast<const float*>(D.rcos), static_cast<const float*>(D.rsin),
+                                      static_cast<int>(p0), H, KV, hd, static_cast<int>(Dm)),
+                   "attention launch");
+    }
+    if (int st = batched_proj(D, Ly.o, D.cb, D.ob, n, s)) return st;
+    {
+      cudaLaunchConfig_t cf = cfg_of(grid_for(n * Dm), dim3(256), 0, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, add_kernel, D.xb, static_cast<const float*>(D.ob), n * Dm), "add launch");
+    }
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cn, rmsnorm_rows_kernel, D.hb, static_cast<const float*>(D.xb), Ly.ffn_norm, Dm,
+                                    eps),
+                 "rmsnorm launch");
+    if (int st = batched_proj(D, Ly.gate, D.hb, D.gb, n, s)) return st;
+    if (int st = batched_proj(D, Ly.up, D.hb, D.ub, n, s)) return st;
+    {
+      cudaLaunchConfig_t cf = cfg_of(grid_for(n * F), dim3(256), 0, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, swiglu_kernel, D.ab, static_cast<const float*>(D.gb),
+                                      static_cast<const float*>(D.ub), static_cast<uint32_t>(n * F)),
+                   "swiglu launch");
+    }
+    if (int st = batched_proj(D, Ly.down, D.ab, D.ob, n, s)) return st;
+    {
+      cudaLaunchConfig_t cf = cfg_of(grid_for(n * Dm), dim3(256), 0, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, add_kernel, D.xb, static_cast<const float*>(D.ob), n * Dm), "add launch");
+    }
+  }
+  if (logits) return enqueue_lm_head(D, D.xb + (n - 1) * Dm, s);
+  return EFG_OK;
+}
+
+// Positions p0..p0+n-1 in passes of pb_rows tokens; logits of the last token when asked.
+int prefill_tokens(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s) {
+  if (int st = ensure_prefill_buffers(D)) return st;
+  for (size_t c0 = 0; c0 < n; c0 += D.pb_rows) {
+    const size_t cn = std::min(D.pb_rows, n - c0);
+    if (int st = prefill_pass(D, p0 + c0, cn, logits && c0 + cn == n, s)) return st;
+  }
   return EFG_OK;
 }
 
@@ -892,6 +1131,29 @@ int efg_decoder_forward(efg_decoder* h, int32_t token, size_t pos, float* logits
   return EFG_OK;
 }
 
+int efg_decoder_prefill(efg_decoder* h, const int32_t* tokens, size_t n, size_t pos0, float* logits) {
+  if (!h || (!tokens && n)) return fail(EFG_EINVAL, "prefill: null argument");
+  Decoder& D = *reinterpret_cast<Decoder*>(h);
+  if (n == 0) return fail(EFG_EINVAL, "prefill: no tokens");
+  if (pos0 > D.cached)
+    return fail(EFG_ESTATE, "prefill: position %zu skips ahead of the %zu cached tokens", pos0, D.cached);
+  if (pos0 + n > D.max_seq)
+    return fail(EFG_ESTATE, "prefill: positions up to %zu exceed the KV-cache capacity %zu", pos0 + n - 1, D.max_seq);
+  for (size_t i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= D.c.vocab)
+      return fail(EFG_EINVAL, "prefill: token id %d is outside [0, %lld)", tokens[i], static_cast<long long>(D.c.vocab));
+  EFG_TRY_CUDA(cudaMemcpyAsync(D.tokens() + pos0, tokens, n * sizeof(int32_t), cudaMemcpyHostToDevice, D.stream),
+               "token upload");
+  if (int st = efg::prefill_tokens(D, pos0, n, logits != nullptr, D.stream)) return st;
+  if (logits)
+    EFG_TRY_CUDA(cudaMemcpyAsync(logits, D.logits, D.c.vocab * sizeof(float), cudaMemcpyDeviceToHost, D.stream),
+                 "logits download");
+  EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+  if (int st = efg::device_status(D)) return st;
+  D.cached = pos0 + n;
+  return EFG_OK;
+}
+
 int efg_decoder_generate(efg_decoder* h, const int32_t* prompt, size_t n_prompt, size_t max_new, int32_t eos_id,
                          const int32_t* forced, int32_t* tokens_out, size_t* n_tokens, float* step_logits,
                          double* prefill_seconds, double* decode_seconds) {
@@ -967,8 +1229,11 @@ int efg_decoder_generate(efg_decoder* h, const int32_t* prompt, size_t n_prompt,
     return EFG_OK;
   }
   cudaEventRecord(e0, D.stream);
-  for (size_t p = 0; p + 1 < n_prompt; ++p) EFG_TRY_CUDA(cudaGraphLaunch(D.g_prefill, D.stream), "graph launch");
-  EFG_TRY_CUDA(cudaGraphLaunch(D.g_full, D.stream), "graph launch");  // last prompt token: logits, next token
+  // the prompt as one batch; then the last prompt token's argmax at position n_prompt - 1
+  if (int st = efg::prefill_tokens(D, 0, n_prompt, true, D.stream)) return st;
+  const int32_t st1[2] = {static_cast<int32_t>(n_prompt - 1), static_cast<int32_t>(n_fixed)};
+  EFG_TRY_CUDA(cudaMemcpyAsync(D.state, st1, sizeof st1, cudaMemcpyHostToDevice, D.stream), "state upload");
+  if (int st = efg::enqueue_argmax(D, D.stream)) return st;
   cudaEventRecord(e1, D.stream);
   size_t n_out = 0;
   bool stopped = false;

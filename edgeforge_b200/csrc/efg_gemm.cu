@@ -30,6 +30,7 @@
 
 #include "../../include/efg.h"
 #include "efg_device.cuh"
+#include "efg_gemm.cuh"
 #include "efg_host.h"
 
 namespace efg {

@@ -1,0 +1,15 @@
+// efg_gemm.cuh - the batched Q4_0 GEMM (efg_gemm.cu) for other library code.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace efg {
+
+// Y[b][m] = sum_k W[m][k] * X[b][k] for b < B (W Q4_0 M x K, X [B][K] FP32 16-byte aligned,
+// Y [B][M]); the tcgen05 kernels of efg_gemm.cu. Returns an EFG_* status.
+int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
+                     cudaStream_t s);
+
+}  // namespace efg

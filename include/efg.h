@@ -252,8 +252,15 @@ int efg_decoder_reset(efg_decoder* d);
  * smaller pos rewinds); writes the next-token logits to the host array `logits` (vocab
  * floats) unless it is NULL, which skips lm_head like compute_logits = false. */
 int efg_decoder_forward(efg_decoder* d, int32_t token, size_t pos, float* logits);
+/* The prompt as one batch: tokens[0..n) at positions pos0..pos0+n-1 (pos0 <= the cached
+ * count), the same as n forward calls in turn (src/model.cpp:184-270), with the Q4_0
+ * projections of all n tokens in one tensor-core GEMM per matrix instead of one matvec per
+ * token (the reference prefills token by token, README.md:89-90). Writes the last token's
+ * logits to `logits` (vocab floats) unless it is NULL. */
+int efg_decoder_prefill(efg_decoder* d, const int32_t* tokens, size_t n, size_t pos0, float* logits);
 /* ef::generate_greedy (src/model.cpp:278-304): prefill the prompt from position 0, then
- * argmax decoding of up to max_new tokens, stopping after eos_id (if >= 0). With `forced`
+ * argmax decoding of up to max_new tokens, stopping after eos_id (if >= 0). In the graph
+ * mode the prompt goes through efg_decoder_prefill's batched path. With `forced`
  * (max_new ids) the decode steps are teacher-forced on those ids instead of the argmax,
  * while tokens_out still receives each step's argmax. step_logits (NULL or a host array of
  * (max_new - 1) * vocab floats) receives the logits after each decode forward. Times are

@@ -55,6 +55,39 @@ def test_forward_matches_reference(z, tag):
 
 
 @pytest.mark.parametrize("tag", ["uniform", "mixed"])
+def test_batched_prefill_matches_reference(z, tag):
+    """The prompt as one batch gives the reference's logits after the prompt, and the KV
+    cache it writes carries the teacher-forced steps that follow; a prompt split in two
+    batches (the second at pos0 > 0) agrees."""
+    ref = z[f"{tag}_scalar"]
+    prompt, forced = z["prompt"], z["forced"]
+    with efg.Decoder(GOLD / f"decode_tiny_{tag}.efq", MAX_SEQ) as dec:
+        got = [dec.prefill(prompt)]
+        pos = len(prompt)
+        for t in forced[:-1]:
+            got.append(dec.forward(int(t), pos))
+            pos += 1
+        assert np.abs(np.stack(got) - ref).max() <= TOL
+        dec.reset()
+        k = len(prompt) // 2
+        assert dec.prefill(prompt[:k], compute_logits=False) is None
+        assert np.abs(dec.prefill(prompt[k:], pos0=k) - ref[0]).max() <= TOL
+        assert efg.device_error() == 0
+
+
+def test_batched_prefill_errors(z):
+    with efg.Decoder(GOLD / "decode_tiny_uniform.efq", 16) as dec:
+        with pytest.raises(efg.EdgeForgeError, match="skips ahead"):
+            dec.prefill(np.array([1, 2], np.int32), pos0=1)
+        with pytest.raises(efg.EdgeForgeError, match="KV-cache capacity"):
+            dec.prefill(np.arange(17, dtype=np.int32))
+        with pytest.raises(efg.EdgeForgeError, match="outside"):
+            dec.prefill(np.array([1, 96], np.int32))
+        with pytest.raises(efg.EdgeForgeError, match="no tokens"):
+            dec.prefill(np.array([], np.int32))
+
+
+@pytest.mark.parametrize("tag", ["uniform", "mixed"])
 def test_generate_teacher_forced(z, tag):
     ref = z[f"{tag}_scalar"]
     with efg.Decoder(GOLD / f"decode_tiny_{tag}.efq", MAX_SEQ) as dec:
@@ -141,6 +174,24 @@ def medium(tmp_path_factory):
     return efq, prompt, forced, ref
 
 
+def test_medium_batched_prefill(medium):
+    """q/k and gate/up of mixed storage types (GEMM and per-token matvecs in one layer):
+    the batched prompt gives the reference's logits; a 100-token prompt (two passes) agrees
+    with our token-by-token forward, and so does the step after it."""
+    efq, prompt, forced, ref = medium
+    with efg.Decoder(efq, 128) as dec:
+        assert np.abs(dec.prefill(prompt) - ref[0]).max() <= TOL
+        long = np.random.default_rng(5).integers(0, 300, 100).astype(np.int32)
+        dec.reset()
+        for i, t in enumerate(long):
+            want = dec.forward(int(t), i, compute_logits=i + 1 == len(long))
+        nxt = dec.forward(7, len(long))
+        dec.reset()
+        assert np.abs(dec.prefill(long) - want).max() <= TOL
+        assert np.abs(dec.forward(7, len(long)) - nxt).max() <= TOL
+        assert efg.device_error() == 0
+
+
 @pytest.mark.parametrize("persistent", [True, False])
 def test_medium_forward_and_generate(medium, persistent):
     efq, prompt, forced, ref = medium
@@ -214,6 +265,8 @@ def test_full_tinyllama_decode(tinyllama, persistent):
         assert err <= TOL, err
         first = dec.forward(int(prompt[-1]), FULL_PROMPT - 1)  # logits after the prompt
         assert np.abs(first - logits_ref[0]).max() <= TOL
+        dec.reset()
+        assert np.abs(dec.prefill(prompt) - logits_ref[0]).max() <= TOL  # batched prompt
         # free-running greedy decode agrees with the reference's tokens up to the first
         # step whose top-2 logit margin is within the tolerance (a legitimate near-tie)
         g = dec.generate(prompt, FULL_STEPS)
