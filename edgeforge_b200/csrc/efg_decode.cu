@@ -108,30 +108,61 @@ __device__ __forceinline__ void rope_pair(float a, float b, float c, float s, fl
   rb = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
 }
 
+// Positions staged per round in shared memory by attend_head (keys padded to hd + 1 floats).
+constexpr int kAttnChunkPos = 64;
+__host__ __device__ constexpr size_t attn_stage_floats(int hd) {
+  return static_cast<size_t>(kAttnChunkPos) * (hd + 1) + static_cast<size_t>(kAttnChunkPos) * hd;
+}
+
 // Softmax attention of one rotated query head qh (shared memory) over the cached keys and
 // values of positions 0..n_pos-1 of KV head kv (src/kernels.cpp:148-174): scores scaled by
 // 1/sqrt(hd), softmax with a double sum, then the probability-weighted sum of the values in
-// position order into out[0..hd). The key of position n_pos-1 is read from k_last.
+// position order into out[0..hd). The key of position n_pos-1 is read from k_last. Keys
+// and values come through `stage` (attn_stage_floats(hd) floats) in rounds of
+// kAttnChunkPos positions, each round one set of coalesced float4 loads; hd % 4 == 0,
+// hd <= 2 * blockDim.x.
 __device__ void attend_head(const float* __restrict__ qh, const float* __restrict__ k_layer,
                             const float* __restrict__ v_layer, const float* __restrict__ k_last, int kv, int hd,
-                            int kvd, int n_pos, float* __restrict__ sc, float* red_f, double* red_d,
-                            float* __restrict__ out) {
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+                            int kvd, int n_pos, float* __restrict__ sc, float* __restrict__ stage, float* red_f,
+                            double* red_d, float* __restrict__ out) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, h4 = hd / 4;
+  float* kch = stage;                                // [kAttnChunkPos][hd + 1]
+  float* vch = stage + kAttnChunkPos * (hd + 1);     // [kAttnChunkPos][hd]
   const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));
   float mx = -INFINITY;
-  for (int t = tid; t < n_pos; t += blockDim.x) {
-    const float* kt = t == n_pos - 1 ? k_last : k_layer + static_cast<size_t>(t) * kvd + kv * hd;
-    // dot with 8 partial sums combined pairwise (src/kernels.cpp:28-43)
-    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    int i = 0;
-    for (; i + 8 <= hd; i += 8)
+  // up to kAttnChunkPos positions: the values are staged with the keys, in one round of loads
+  const bool one_round = n_pos <= kAttnChunkPos;
+  for (int c0 = 0; c0 < n_pos; c0 += kAttnChunkPos) {
+    const int cn = min(kAttnChunkPos, n_pos - c0);
+    for (int e = tid; e < cn * h4; e += blockDim.x) {
+      const int t = e / h4, i4 = e % h4;
+      const float* src = c0 + t == n_pos - 1 ? k_last : k_layer + static_cast<size_t>(c0 + t) * kvd + kv * hd;
+      const float4 v = reinterpret_cast<const float4*>(src)[i4];
+      float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (one_round) w = reinterpret_cast<const float4*>(v_layer + static_cast<size_t>(t) * kvd + kv * hd)[i4];
+      float* d = kch + t * (hd + 1) + 4 * i4;
+      d[0] = v.x;
+      d[1] = v.y;
+      d[2] = v.z;
+      d[3] = v.w;
+      if (one_round) reinterpret_cast<float4*>(vch + t * hd)[i4] = w;
+    }
+    __syncthreads();
+    for (int t = tid; t < cn; t += blockDim.x) {
+      const float* kt = kch + t * (hd + 1);
+      // dot with 8 partial sums combined pairwise (src/kernels.cpp:28-43)
+      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      int i = 0;
+      for (; i + 8 <= hd; i += 8)
 #pragma unroll
-      for (int k = 0; k < 8; ++k) a[k] = __fadd_rn(a[k], __fmul_rn(qh[i + k], kt[i + k]));
-    for (; i < hd; ++i) a[0] = __fadd_rn(a[0], __fmul_rn(qh[i], kt[i]));
-    const float dot = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
-                                __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
-    sc[t] = __fmul_rn(dot, scale);
-    mx = fmaxf(mx, sc[t]);
+        for (int k = 0; k < 8; ++k) a[k] = __fadd_rn(a[k], __fmul_rn(qh[i + k], kt[i + k]));
+      for (; i < hd; ++i) a[0] = __fadd_rn(a[0], __fmul_rn(qh[i], kt[i]));
+      const float dot = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
+                                  __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
+      sc[c0 + t] = __fmul_rn(dot, scale);
+      mx = fmaxf(mx, sc[c0 + t]);
+    }
+    __syncthreads();  // kch is rewritten by the next round
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
@@ -153,13 +184,27 @@ __device__ void attend_head(const float* __restrict__ qh, const float* __restric
   for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) tot += red_d[w];
   const float inv = static_cast<float>(1.0 / tot);
   for (int t = tid; t < n_pos; t += blockDim.x) sc[t] = __fmul_rn(sc[t], inv);
-  __syncthreads();
-  for (int d = tid; d < hd; d += blockDim.x) {
-    float acc = 0.f;
-    for (int t = 0; t < n_pos; ++t)
-      acc = __fadd_rn(acc, __fmul_rn(sc[t], v_layer[static_cast<size_t>(t) * kvd + kv * hd + d]));
-    out[d] = acc;
+  // weighted sum of the values in position order; thread tid owns d = tid and tid + blockDim
+  float acc0 = 0.f, acc1 = 0.f;
+  const int d0 = tid, d1 = tid + static_cast<int>(blockDim.x);
+  for (int c0 = 0; c0 < n_pos; c0 += kAttnChunkPos) {
+    const int cn = min(kAttnChunkPos, n_pos - c0);
+    __syncthreads();  // sc is final; vch is free (or, in one round, already staged)
+    if (!one_round) {
+      for (int e = tid; e < cn * h4; e += blockDim.x) {
+        const int t = e / h4, i4 = e % h4;
+        reinterpret_cast<float4*>(vch + t * hd)[i4] =
+            reinterpret_cast<const float4*>(v_layer + static_cast<size_t>(c0 + t) * kvd + kv * hd)[i4];
+      }
+      __syncthreads();
+    }
+    if (d0 < hd)
+      for (int t = 0; t < cn; ++t) acc0 = __fadd_rn(acc0, __fmul_rn(sc[c0 + t], vch[t * hd + d0]));
+    if (d1 < hd)
+      for (int t = 0; t < cn; ++t) acc1 = __fadd_rn(acc1, __fmul_rn(sc[c0 + t], vch[t * hd + d1]));
   }
+  if (d0 < hd) out[d0] = acc0;
+  if (d1 < hd) out[d1] = acc1;
 }
 
 // One query head per CTA: RoPE of q and of the new key, the key written to the cache at pos
@@ -172,7 +217,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
   extern __shared__ float sm[];
   float* qh = sm;            // [hd]
   float* kn = qh + hd;       // [hd]
-  float* sc = kn + hd;       // [max_seq]
+  float* stage = kn + hd;    // [attn_stage_floats(hd)]
+  float* sc = stage + attn_stage_floats(hd);  // [max_seq]
   __shared__ float red_f[kAttnThreads / 32];
   __shared__ double red_d[kAttnThreads / 32];
   pdl_wait();
@@ -193,7 +239,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
   __syncthreads();
   if (h % group == 0)
     for (int i = tid; i < hd; i += blockDim.x) k_layer[static_cast<size_t>(pos) * kvd + kv * hd + i] = kn[i];
-  attend_head(qh, k_layer, v_layer, kn, kv, hd, kvd, pos + 1, sc, red_f, red_d, ctx + h * hd);
+  attend_head(qh, k_layer, v_layer, kn, kv, hd, kvd, pos + 1, sc, stage, red_f, red_d, ctx + h * hd);
 }
 
 // Batched prefill: rotate the keys of positions p0..p0+n-1, written unrotated into the
@@ -223,8 +269,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(
     float* __restrict__ ctxb, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, int p0, int H,
     int KV, int hd, int dim) {
   extern __shared__ float sm[];
-  float* qh = sm;       // [hd]
-  float* sc = qh + hd;  // [max_seq]
+  float* qh = sm;                             // [hd]
+  float* stage = qh + hd;                     // [attn_stage_floats(hd)]
+  float* sc = stage + attn_stage_floats(hd);  // [max_seq]
   __shared__ float red_f[kAttnThreads / 32];
   __shared__ double red_d[kAttnThreads / 32];
   pdl_wait();
@@ -238,7 +285,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(
     rope_pair(q[h * hd + i], q[h * hd + i + half], c[i], s[i], qh[i], qh[i + half]);
   __syncthreads();
   attend_head(qh, k_layer, v_layer, k_layer + static_cast<size_t>(pos) * kvd + kv * hd, kv, hd, kvd, pos + 1, sc,
-              red_f, red_d, ctxb + static_cast<size_t>(b) * dim + h * hd);
+              stage, red_f, red_d, ctxb + static_cast<size_t>(b) * dim + h * hd);
 }
 
 // out = silu(gate) * up (src/kernels.cpp:94-99), for the unfused path.
@@ -501,7 +548,7 @@ int enqueue_step(Decoder& D, bool logits, cudaStream_t s) {
       if (int st = launch_matvec(a, D.d_err, s)) return st;
     }
     {
-      const size_t smem = (2 * hd + D.max_seq) * sizeof(float);
+      const size_t smem = (2 * hd + attn_stage_floats(hd) + D.max_seq) * sizeof(float);
       cudaLaunchConfig_t cf = cfg_of(dim3(H), dim3(kAttnThreads), smem, s, attr);
       EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, attention_kernel, static_cast<const float*>(D.q),
                                       static_cast<const float*>(D.knew), kl, static_cast<const float*>(vl), D.ctx,
@@ -869,9 +916,11 @@ int open_decoder(const char* path, size_t max_seq, Decoder** out) {
   if (c.tie_embeddings) D->bytes_per_token += D->L.at("model.embed_tokens.weight").bytes;
 
   const size_t kvd = static_cast<size_t>(c.kv_dim()), half = static_cast<size_t>(c.head_dim / 2);
-  if (c.head_dim % 2 != 0 || c.heads % c.kv_heads != 0)
-    return fail(EFG_EINVAL, "decoder: head_dim must be even and heads a multiple of kv_heads");
-  const size_t attn_smem = (2 * static_cast<size_t>(c.head_dim) + max_seq) * sizeof(float);
+  if (c.head_dim % 4 != 0 || c.head_dim > 2 * kAttnThreads || c.heads % c.kv_heads != 0)
+    return fail(EFG_EINVAL, "decoder: head_dim must be a multiple of 4 up to %d and heads a multiple of kv_heads",
+                2 * kAttnThreads);
+  const size_t attn_smem =
+      (2 * static_cast<size_t>(c.head_dim) + attn_stage_floats(static_cast<int>(c.head_dim)) + max_seq) * sizeof(float);
   if (attn_smem > 227 * 1024)
     return fail(EFG_EINVAL, "decoder: max_seq %zu is too long for the attention kernel", max_seq);
   if (attn_smem > 48 * 1024) {
@@ -1001,7 +1050,7 @@ int prefill_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s) {
                    "rope launch");
     }
     {
-      const size_t smem = (hd + D.max_seq) * sizeof(float);
+      const size_t smem = (hd + attn_stage_floats(hd) + D.max_seq) * sizeof(float);
       cudaLaunchConfig_t cf = cfg_of(dim3(H, nb), dim3(kAttnThreads), smem, s, attr);
       EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, attention_rows_kernel, static_cast<const float*>(D.qb),
                                       static_cast<const float*>(kl), static_cast<const float*>(vl), D.cb,

@@ -50,6 +50,7 @@ struct KParams {
   int* err;
   const int32_t* pos;
   uint32_t cols, rb_words, S, G, H, RG, TR, BPS, NS, stage_bytes, n_jobs, tiles_total;
+  uint32_t x_vec4;  // x and norm_w are 16-byte aligned: staged with float4 loads
   uint32_t job_tile_start[kMaxJobs + 1];
   MatvecJobDev jobs[kMaxJobs];
 };
@@ -158,26 +159,83 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
 
   // x is read once per CTA with coalesced loads into a padded shared array (65 floats
   // per 64-column slot, so the per-lane reads below hit 32 different banks), with the
-  // RMSNorm folded in: h = w * (x * inv) exactly as src/kernels.cpp:74.
-  const uint32_t tid = threadIdx.x;  // consumers are threads [0, nc * 32)
-  for (uint32_t i = tid; i < p.cols; i += nc * 32) xs[(i >> 6) * 65 + (i & 63)] = p.x[i];
+  // RMSNorm folded in: h = w * (x * inv) exactly as src/kernels.cpp:74. Each thread
+  // issues up to kXv float4 loads before it uses any (one memory latency, not one per
+  // element), and fetches its norm weights the same way once inv is known.
+  const uint32_t tid = threadIdx.x, nthr = nc * 32;  // consumers are threads [0, nthr)
+  constexpr uint32_t kXv = 4;
+  double ss = 0.0;
+  if (p.x_vec4) {
+    const float4* x4 = reinterpret_cast<const float4*>(p.x);
+    const uint32_t n4 = p.cols / 4;
+    for (uint32_t base = tid; base < n4; base += kXv * nthr) {
+      float4 v[kXv];
+#pragma unroll
+      for (uint32_t u = 0; u < kXv; ++u) {
+        const uint32_t i = base + u * nthr;
+        v[u] = i < n4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (uint32_t u = 0; u < kXv; ++u) {
+        const uint32_t i = base + u * nthr;
+        if (i < n4) {
+          float* d = xs + ((4 * i) >> 6) * 65 + ((4 * i) & 63);
+          d[0] = v[u].x;
+          d[1] = v[u].y;
+          d[2] = v[u].z;
+          d[3] = v[u].w;
+          if constexpr (NORM) {
+            ss += static_cast<double>(v[u].x) * static_cast<double>(v[u].x);
+            ss += static_cast<double>(v[u].y) * static_cast<double>(v[u].y);
+            ss += static_cast<double>(v[u].z) * static_cast<double>(v[u].z);
+            ss += static_cast<double>(v[u].w) * static_cast<double>(v[u].w);
+          }
+        }
+      }
+    }
+  } else {
+    for (uint32_t i = tid; i < p.cols; i += nthr) {
+      const float v = p.x[i];
+      xs[(i >> 6) * 65 + (i & 63)] = v;
+      if constexpr (NORM) ss += static_cast<double>(v) * static_cast<double>(v);
+    }
+  }
   if constexpr (NORM) {
     // rmsnorm scale from the whole x (src/kernels.cpp:69-73): double sum of squares.
-    double ss = 0.0;
-    for (uint32_t i = tid; i < p.cols; i += nc * 32) {
-      const double v = static_cast<double>(xs[(i >> 6) * 65 + (i & 63)]);
-      ss += v * v;
-    }
     ss = warp_sum_d(ss);
     if (lane == 0) norm_red[warp] = ss;
-    named_barrier(kNormBarrier, nc * 32);
+    named_barrier(kNormBarrier, nthr);
     double tot = 0.0;
     for (uint32_t w = 0; w < nc; ++w) tot += norm_red[w];
     const double mean = p.cols ? tot / static_cast<double>(p.cols) : 0.0;
     const float inv = static_cast<float>(1.0 / sqrt(mean + static_cast<double>(p.norm_eps)));
-    for (uint32_t i = tid; i < p.cols; i += nc * 32) {
-      float& h = xs[(i >> 6) * 65 + (i & 63)];
-      h = p.norm_w[i] * (h * inv);
+    if (p.x_vec4) {
+      const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+      const uint32_t n4 = p.cols / 4;
+      for (uint32_t base = tid; base < n4; base += kXv * nthr) {
+        float4 w[kXv];
+#pragma unroll
+        for (uint32_t u = 0; u < kXv; ++u) {
+          const uint32_t i = base + u * nthr;
+          w[u] = i < n4 ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (uint32_t u = 0; u < kXv; ++u) {
+          const uint32_t i = base + u * nthr;
+          if (i < n4) {
+            float* d = xs + ((4 * i) >> 6) * 65 + ((4 * i) & 63);
+            d[0] = w[u].x * (d[0] * inv);
+            d[1] = w[u].y * (d[1] * inv);
+            d[2] = w[u].z * (d[2] * inv);
+            d[3] = w[u].w * (d[3] * inv);
+          }
+        }
+      }
+    } else {
+      for (uint32_t i = tid; i < p.cols; i += nthr) {
+        float& h = xs[(i >> 6) * 65 + (i & 63)];
+        h = p.norm_w[i] * (h * inv);
+      }
     }
   }
   named_barrier(kNormBarrier, nc * 32);
@@ -477,6 +535,7 @@ int launch_matvec_on(const MatvecArgs& a, const DeviceInfo& devinfo, int* d_err,
   KParams k{};
   k.x = a.x;
   k.norm_w = a.norm_w;
+  k.x_vec4 = reinterpret_cast<uintptr_t>(a.x) % 16 == 0 && reinterpret_cast<uintptr_t>(a.norm_w) % 16 == 0 ? 1u : 0u;
   k.norm_eps = a.norm_eps;
   k.err = d_err;
   k.pos = a.pos;
