@@ -120,11 +120,12 @@ __host__ __device__ constexpr size_t attn_stage_floats(int hd) {
 // position order into out[0..hd). The key of position n_pos-1 is read from k_last. Keys
 // and values come through `stage` (attn_stage_floats(hd) floats) in rounds of
 // kAttnChunkPos positions, each round one set of coalesced float4 loads; hd % 4 == 0,
-// hd <= 2 * blockDim.x.
+// hd <= 2 * blockDim.x. With `staged` (n_pos <= kAttnChunkPos only) the caller has already
+// put every key and value row in `stage` and attend_head loads nothing.
 __device__ void attend_head(const float* __restrict__ qh, const float* __restrict__ k_layer,
                             const float* __restrict__ v_layer, const float* __restrict__ k_last, int kv, int hd,
                             int kvd, int n_pos, float* __restrict__ sc, float* __restrict__ stage, float* red_f,
-                            double* red_d, float* __restrict__ out) {
+                            double* red_d, float* __restrict__ out, bool staged = false) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, h4 = hd / 4;
   float* kch = stage;                                // [kAttnChunkPos][hd + 1]
   float* vch = stage + kAttnChunkPos * (hd + 1);     // [kAttnChunkPos][hd]
@@ -134,7 +135,7 @@ __device__ void attend_head(const float* __restrict__ qh, const float* __restric
   const bool one_round = n_pos <= kAttnChunkPos;
   for (int c0 = 0; c0 < n_pos; c0 += kAttnChunkPos) {
     const int cn = min(kAttnChunkPos, n_pos - c0);
-    for (int e = tid; e < cn * h4; e += blockDim.x) {
+    for (int e = tid; e < (staged ? 0 : cn * h4); e += blockDim.x) {
       const int t = e / h4, i4 = e % h4;
       const float* src = c0 + t == n_pos - 1 ? k_last : k_layer + static_cast<size_t>(c0 + t) * kvd + kv * hd;
       const float4 v = reinterpret_cast<const float4*>(src)[i4];
@@ -221,25 +222,58 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
   float* sc = stage + attn_stage_floats(hd);  // [max_seq]
   __shared__ float red_f[kAttnThreads / 32];
   __shared__ double red_d[kAttnThreads / 32];
-  pdl_wait();
-  pdl_launch_dependents();
+  // The position, the RoPE tables and the cached keys and values of earlier positions
+  // were written before this step began (graph launches are stream-ordered), so they
+  // are read before waiting for the q/k/v projection; only q, the new key and the new
+  // value are read after.
   const int pos = *pos_p;
   if (pos < 0 || pos >= max_seq) {
+    pdl_wait();
+    pdl_launch_dependents();
     if (threadIdx.x == 0) record_error(err, EFG_ESTATE);
     return;
   }
-  const int h = blockIdx.x, group = H / KV, kv = h / group, half = hd / 2, kvd = KV * hd;
+  const int h = blockIdx.x, group = H / KV, kv = h / group, half = hd / 2, kvd = KV * hd, h4 = hd / 4;
   const int tid = threadIdx.x;
-  const float* c = rope_cos + static_cast<size_t>(pos) * half;
-  const float* s = rope_sin + static_cast<size_t>(pos) * half;
-  for (int i = tid; i < half; i += blockDim.x) {
-    rope_pair(q[h * hd + i], q[h * hd + i + half], c[i], s[i], qh[i], qh[i + half]);
-    rope_pair(knew[kv * hd + i], knew[kv * hd + i + half], c[i], s[i], kn[i], kn[i + half]);
+  const bool staged = pos + 1 <= kAttnChunkPos;
+  float* kch = stage;
+  float* vch = stage + kAttnChunkPos * (hd + 1);
+  if (staged)
+    for (int e = tid; e < pos * h4; e += blockDim.x) {
+      const int t = e / h4, i4 = e % h4;
+      const size_t row = static_cast<size_t>(t) * kvd + kv * hd;
+      const float4 kv4 = reinterpret_cast<const float4*>(k_layer + row)[i4];
+      reinterpret_cast<float4*>(vch + t * hd)[i4] = reinterpret_cast<const float4*>(v_layer + row)[i4];
+      float* d = kch + t * (hd + 1) + 4 * i4;
+      d[0] = kv4.x;
+      d[1] = kv4.y;
+      d[2] = kv4.z;
+      d[3] = kv4.w;
+    }
+  float cs = 0.f, sn = 0.f;
+  if (tid < half) {
+    cs = rope_cos[static_cast<size_t>(pos) * half + tid];
+    sn = rope_sin[static_cast<size_t>(pos) * half + tid];
   }
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = tid; i < half; i += blockDim.x) {
+    const float c = i == tid ? cs : rope_cos[static_cast<size_t>(pos) * half + i];
+    const float sv = i == tid ? sn : rope_sin[static_cast<size_t>(pos) * half + i];
+    rope_pair(q[h * hd + i], q[h * hd + i + half], c, sv, qh[i], qh[i + half]);
+    rope_pair(knew[kv * hd + i], knew[kv * hd + i + half], c, sv, kn[i], kn[i + half]);
+  }
+  if (staged)
+    for (int i4 = tid; i4 < h4; i4 += blockDim.x)  // the new value row (written by the projection)
+      reinterpret_cast<float4*>(vch + pos * hd)[i4] =
+          reinterpret_cast<const float4*>(v_layer + static_cast<size_t>(pos) * kvd + kv * hd)[i4];
   __syncthreads();
   if (h % group == 0)
     for (int i = tid; i < hd; i += blockDim.x) k_layer[static_cast<size_t>(pos) * kvd + kv * hd + i] = kn[i];
-  attend_head(qh, k_layer, v_layer, kn, kv, hd, kvd, pos + 1, sc, stage, red_f, red_d, ctx + h * hd);
+  if (staged)
+    for (int i = tid; i < hd; i += blockDim.x) kch[pos * (hd + 1) + i] = kn[i];
+  __syncthreads();
+  attend_head(qh, k_layer, v_layer, kn, kv, hd, kvd, pos + 1, sc, stage, red_f, red_d, ctx + h * hd, staged);
 }
 
 // Batched prefill: rotate the keys of positions p0..p0+n-1, written unrotated into the

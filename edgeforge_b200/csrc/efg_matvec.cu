@@ -155,19 +155,30 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
   const uint32_t g = warp % p.G, h = (warp / p.G) % p.H, rg = warp / (p.G * p.H);
   const uint32_t slot = g * 32 + lane;
   const bool active = slot < p.S;
-  pdl_wait();  // x, norm weights and y belong to the previous kernel in the stream
 
   // x is read once per CTA with coalesced loads into a padded shared array (65 floats
   // per 64-column slot, so the per-lane reads below hit 32 different banks), with the
   // RMSNorm folded in: h = w * (x * inv) exactly as src/kernels.cpp:74. Each thread
   // issues up to kXv float4 loads before it uses any (one memory latency, not one per
-  // element), and fetches its norm weights the same way once inv is known.
+  // element). The norm weights are model constants: when x fits in one pass they are
+  // loaded before waiting for the previous kernel, which wrote x (and y).
   const uint32_t tid = threadIdx.x, nthr = nc * 32;  // consumers are threads [0, nthr)
   constexpr uint32_t kXv = 4;
+  const uint32_t n4 = p.cols / 4;
+  const bool one_pass = p.x_vec4 && n4 <= kXv * nthr;
+  float4 wv[kXv];
+  if (NORM && one_pass) {
+    const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+#pragma unroll
+    for (uint32_t u = 0; u < kXv; ++u) {
+      const uint32_t i = tid + u * nthr;
+      wv[u] = i < n4 ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  pdl_wait();  // x and y belong to the previous kernel in the stream
   double ss = 0.0;
   if (p.x_vec4) {
     const float4* x4 = reinterpret_cast<const float4*>(p.x);
-    const uint32_t n4 = p.cols / 4;
     for (uint32_t base = tid; base < n4; base += kXv * nthr) {
       float4 v[kXv];
 #pragma unroll
@@ -211,13 +222,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
     const float inv = static_cast<float>(1.0 / sqrt(mean + static_cast<double>(p.norm_eps)));
     if (p.x_vec4) {
       const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
-      const uint32_t n4 = p.cols / 4;
       for (uint32_t base = tid; base < n4; base += kXv * nthr) {
         float4 w[kXv];
 #pragma unroll
         for (uint32_t u = 0; u < kXv; ++u) {
           const uint32_t i = base + u * nthr;
-          w[u] = i < n4 ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+          w[u] = one_pass ? wv[u] : (i < n4 ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f));
         }
 #pragma unroll
         for (uint32_t u = 0; u < kXv; ++u) {

@@ -26,7 +26,8 @@ struct MatvecArgs {
   Fmt fmt = Fmt::Q4;
   Epi epi = Epi::Store;
   const float* x = nullptr;
-  const float* norm_w = nullptr;  // when set, x is replaced by rmsnorm(x) * norm_w first
+  const float* norm_w = nullptr;  // when set, x is replaced by rmsnorm(x) * norm_w first; with pdl,
+                                  // read before the previous kernel ends (model weights only)
   float norm_eps = 1e-5f;
   const int32_t* pos = nullptr;   // device-side position for y_pos_stride (decode step)
   size_t cols = 0;
