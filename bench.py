@@ -150,7 +150,7 @@ def run_reference_arm(args):
     if rank != 0:
         return 0
     if not (ROOT / "oracle" / "_ref" / "libefref.so").exists():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libefref.so was not built"}))
+        emit({"impl": "reference", "unavailable": "oracle/_ref/libefref.so was not built"})
         return 0
     # W untimed warm-up steps, then K timed steps (each one CPU matvec of the workload;
     # stopped after 150 s, in which case "steps" reports the count actually timed)
@@ -167,7 +167,7 @@ def run_reference_arm(args):
                          "sample": f"{n} matvecs of the reference AVX2 kernel, ThreadPool({threads})"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line))
+    emit(line)
     return 0
 
 
@@ -340,7 +340,7 @@ def run_ours(args):
                 "config3_gemm_q4_0": gemm,
                 "config1_quantize_round_trip": quant},
         }
-        print(json.dumps(line))
+        emit(line)
     if world > 1:
         del g_full, g_rem
         torch.distributed.destroy_process_group()
@@ -573,6 +573,18 @@ def run_profile(args):
     return 0
 
 
+_RESULT_FD = None
+
+
+def emit(line: dict) -> None:
+    """Writes the JSON result line to the process's original stdout. Everything else that
+    the run prints (libraries included, e.g. NCCL's version banner) goes to stderr, so
+    stdout carries exactly one JSON line."""
+    out = os.fdopen(os.dup(_RESULT_FD), "w") if _RESULT_FD is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -587,6 +599,10 @@ def main():
     ap.add_argument("--profile", choices=["q8", "q4", "q4big", "gemm", "decode", "decode_persistent"],
                     help="a few plain launches for ncu")
     args = ap.parse_args()
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)  # the JSON line goes here; fd 1 then points at stderr
+    os.dup2(2, 1)
     if args.profile:
         return run_profile(args)
     if args.warmup < 3:
