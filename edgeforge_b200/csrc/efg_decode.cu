@@ -388,15 +388,36 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
   pdl_launch_dependents();
   float best = -INFINITY;
   uint32_t idx = 0xFFFFFFFFu;
-  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = logits[i];
-    if (v > best || (idx == 0xFFFFFFFFu && !(v != v))) {  // first non-NaN candidate, then strictly greater
-      if (idx == 0xFFFFFFFFu || v > best) {
-        best = v;
-        idx = i;
+  // each thread scans its elements in increasing index order: the first non-NaN value,
+  // then strictly greater ones (ties keep the lower index)
+  auto take = [&](float v, uint32_t i) {
+    if (idx == 0xFFFFFFFFu ? !(v != v) : v > best) {
+      best = v;
+      idx = i;
+    }
+  };
+  // float4 chunks, up to 8 loads in flight per thread, then the scalar tail
+  const uint32_t n4 = reinterpret_cast<uintptr_t>(logits) % 16 == 0 ? n / 4 : 0;
+  const float4* l4 = reinterpret_cast<const float4*>(logits);
+  for (uint32_t base = threadIdx.x; base < n4; base += 8 * blockDim.x) {
+    float4 v[8];
+#pragma unroll
+    for (uint32_t u = 0; u < 8; ++u) {
+      const uint32_t c = base + u * blockDim.x;
+      v[u] = c < n4 ? l4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (uint32_t u = 0; u < 8; ++u) {
+      const uint32_t c = base + u * blockDim.x;
+      if (c < n4) {
+        take(v[u].x, 4 * c);
+        take(v[u].y, 4 * c + 1);
+        take(v[u].z, 4 * c + 2);
+        take(v[u].w, 4 * c + 3);
       }
     }
   }
+  for (uint32_t i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) take(logits[i], i);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
