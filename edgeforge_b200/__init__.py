@@ -29,6 +29,8 @@ from .api import (  # noqa: F401
     matvec_jobs,
     matvec_q4_0,
     matvec_q8_0,
+    argmax,
+    lm_head_argmax_sharded,
     matvec_sharded,
     quantize_model,
     quantize_row,

@@ -77,6 +77,8 @@ SIGNATURES = {
     "efg_comm_init": (_i, [_vp, _i, _i, C.POINTER(_vp)]),
     "efg_comm_destroy": (_i, [_vp]),
     "efg_matvec_sharded": (_i, [_i, _vp, _vp, _vp, _sz, _sz, _vp, _vp]),
+    "efg_argmax": (_i, [_vp, _sz, _vp, _vp]),
+    "efg_lm_head_argmax_sharded": (_i, [C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_float, _sz, _sz, _vp, _vp]),
     "efg_efq_check": (_i, [_vp, _u64]),
     "efg_quantize_model": (_i, [C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(QuantizeReport)]),
     "efg_decoder_open": (_i, [C.c_char_p, _sz, C.POINTER(_vp)]),

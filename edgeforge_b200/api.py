@@ -271,6 +271,27 @@ def matvec_sharded(qtype: int, y, W_shard, x, rows: int, cols: int, comm: Comm) 
                                     _stream()))
 
 
+def argmax(x, out=None):
+    """efg_argmax (ef::kern::argmax): index of the first maximum of the CUDA float tensor x,
+    written to `out` (a CUDA int32 tensor of one element, made if None); returns `out`."""
+    import torch
+
+    if out is None:
+        out = torch.empty(1, dtype=torch.int32, device=x.device)
+    check(load().efg_argmax(_ptr(x), x.numel(), _ptr(out), _stream()))
+    return out
+
+
+def lm_head_argmax_sharded(qtype: int, logits_shard, token, W_shard, x, norm_w, eps: float, rows: int, cols: int,
+                           comm: Comm) -> None:
+    """Row-sharded lm_head with the greedy argmax: this rank's logits into logits_shard, the
+    argmax over all rows into token (CUDA int32, one element) on every rank."""
+    check(load().efg_lm_head_argmax_sharded(int(qtype), _ptr(logits_shard) if logits_shard is not None else None,
+                                            _ptr(token), _ptr(W_shard) if W_shard is not None else None, _ptr(x),
+                                            _ptr(norm_w) if norm_w is not None else None, float(eps), rows, cols,
+                                            comm.handle, _stream()))
+
+
 # ---------------------------------------------------------------- .efq and the decode step
 
 

@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "../../include/efg.h"
+#include "efg_argmax.cuh"
 #include "efg_device.cuh"
 #include "efg_efq.h"
 #include "efg_gemm.cuh"
@@ -382,65 +383,12 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
                                                       int32_t* __restrict__ tokens, int32_t* __restrict__ out_tokens,
                                                       int32_t* __restrict__ pos_p, const int32_t* __restrict__ n_fixed,
                                                       int max_seq) {
-  __shared__ float bv[32];
-  __shared__ uint32_t bi[32];
   pdl_wait();
   pdl_launch_dependents();
-  float best = -INFINITY;
-  uint32_t idx = 0xFFFFFFFFu;
-  // each thread scans its elements in increasing index order: the first non-NaN value,
-  // then strictly greater ones (ties keep the lower index)
-  auto take = [&](float v, uint32_t i) {
-    if (idx == 0xFFFFFFFFu ? !(v != v) : v > best) {
-      best = v;
-      idx = i;
-    }
-  };
-  // float4 chunks, up to 8 loads in flight per thread, then the scalar tail
-  const uint32_t n4 = reinterpret_cast<uintptr_t>(logits) % 16 == 0 ? n / 4 : 0;
-  const float4* l4 = reinterpret_cast<const float4*>(logits);
-  for (uint32_t base = threadIdx.x; base < n4; base += 8 * blockDim.x) {
-    float4 v[8];
-#pragma unroll
-    for (uint32_t u = 0; u < 8; ++u) {
-      const uint32_t c = base + u * blockDim.x;
-      v[u] = c < n4 ? l4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (uint32_t u = 0; u < 8; ++u) {
-      const uint32_t c = base + u * blockDim.x;
-      if (c < n4) {
-        take(v[u].x, 4 * c);
-        take(v[u].y, 4 * c + 1);
-        take(v[u].z, 4 * c + 2);
-        take(v[u].w, 4 * c + 3);
-      }
-    }
-  }
-  for (uint32_t i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) take(logits[i], i);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-    const uint32_t oi = __shfl_xor_sync(0xFFFFFFFFu, idx, o);
-    if (oi != 0xFFFFFFFFu && (idx == 0xFFFFFFFFu || ov > best || (ov == best && oi < idx))) {
-      best = ov;
-      idx = oi;
-    }
-  }
-  if ((threadIdx.x & 31) == 0) {
-    bv[threadIdx.x >> 5] = best;
-    bi[threadIdx.x >> 5] = idx;
-  }
-  __syncthreads();
+  float best;
+  uint32_t idx;
+  block_argmax(logits, n, best, idx);
   if (threadIdx.x == 0) {
-    best = bv[0];
-    idx = bi[0];
-    for (uint32_t w = 1; w < blockDim.x / 32; ++w) {
-      if (bi[w] != 0xFFFFFFFFu && (idx == 0xFFFFFFFFu || bv[w] > best || (bv[w] == best && bi[w] < idx))) {
-        best = bv[w];
-        idx = bi[w];
-      }
-    }
     // The reference starts from index 0 and takes strictly greater values, so a NaN at
     // index 0 is never replaced (all comparisons with it are false).
     const float first = logits[0];

@@ -18,6 +18,7 @@
 #include <nccl.h>
 
 #include "../../include/efg.h"
+#include "efg_argmax.cuh"
 #include "efg_host.h"
 #include "efg_matvec.cuh"
 
@@ -74,6 +75,7 @@ int nccl_check(Nccl* n, ncclResult_t r, const char* what) {
 struct efg_comm {
   ncclComm_t comm = nullptr;
   int nranks = 0, rank = 0, device = -1;
+  efg::ArgmaxPair* d_pairs = nullptr;  // one per rank: the row-sharded argmax's exchange
 };
 
 using efg::fail;
@@ -119,6 +121,11 @@ int efg_comm_init(const void* id, int nranks, int rank, efg_comm** out) {
     delete c;
     return st;
   }
+  if (cudaMalloc(&c->d_pairs, sizeof(efg::ArgmaxPair) * static_cast<size_t>(nranks)) != cudaSuccess) {
+    n->comm_destroy(c->comm);
+    delete c;
+    return fail(EFG_ECUDA, "comm_init: exchange buffer allocation");
+  }
   *out = c;
   return EFG_OK;
 }
@@ -128,6 +135,7 @@ int efg_comm_destroy(efg_comm* c) {
   efg::Nccl* n = nullptr;
   int st = EFG_OK;
   if (c->comm && efg::load_nccl(&n) == EFG_OK) st = efg::nccl_check(n, n->comm_destroy(c->comm), "ncclCommDestroy");
+  if (c->d_pairs) cudaFree(c->d_pairs);
   delete c;
   return st;
 }
@@ -181,6 +189,52 @@ int efg_matvec_sharded(int qtype, float* d_y, const uint8_t* d_W_shard, const fl
     }
   }
   return nccl_check(n, n->group_end(), "ncclGroupEnd");
+}
+
+int efg_lm_head_argmax_sharded(int qtype, float* d_logits_shard, int32_t* d_token, const uint8_t* d_W_shard,
+                               const float* d_x, const float* d_norm_w, float eps, size_t rows, size_t cols,
+                               efg_comm* comm, void* stream) {
+  using namespace efg;
+  if (!comm || !comm->comm) return fail(EFG_EINVAL, "lm_head_argmax_sharded: null communicator");
+  if (qtype != EFG_Q4_0 && qtype != EFG_Q8_0)
+    return fail(EFG_EINVAL, "lm_head_argmax_sharded: type %d is not a packed type (Q4_0, Q8_0)", qtype);
+  if (cols % 32 != 0)
+    return fail(EFG_EINVAL, "%s needs a row length divisible by 32, got %zu", qtype == EFG_Q4_0 ? "Q4_0" : "Q8_0",
+                cols);
+  if (rows == 0 || rows >= (1ull << 31)) return fail(EFG_EINVAL, "lm_head_argmax_sharded: bad row count %zu", rows);
+  if (!d_token || !d_x) return fail(EFG_EINVAL, "lm_head_argmax_sharded: null pointer");
+  int dev = -1;
+  EFG_TRY_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != comm->device)
+    return fail(EFG_EINVAL, "lm_head_argmax_sharded: current device %d is not the communicator's device %d", dev,
+                comm->device);
+  size_t b = 0, cnt = 0;
+  if (int st = efg_shard_rows(rows, comm->nranks, comm->rank, &b, &cnt)) return st;
+  auto s = static_cast<cudaStream_t>(stream);
+  if (cnt) {
+    if (!d_logits_shard || !d_W_shard) return fail(EFG_EINVAL, "lm_head_argmax_sharded: null shard pointer");
+    DeviceInfo* di = current_device();
+    if (!di) return EFG_ECUDA;
+    MatvecArgs a;
+    a.fmt = qtype == EFG_Q4_0 ? Fmt::Q4 : Fmt::Q8;
+    a.x = d_x;
+    a.norm_w = d_norm_w;
+    a.norm_eps = eps;
+    a.cols = cols;
+    a.n_jobs = 1;
+    a.jobs[0] = MatvecJobDev{d_W_shard, d_logits_shard, static_cast<uint32_t>(cnt), 0};
+    if (int st = launch_matvec(a, di->d_err, s)) return st;
+  }
+  ArgmaxPair* mine = comm->d_pairs + comm->rank;
+  if (int st = launch_argmax_local(d_logits_shard, cnt, b, mine, s)) return st;
+  if (comm->nranks > 1) {
+    Nccl* n = nullptr;
+    if (int st = load_nccl(&n)) return st;
+    // in place: each rank's pair (8 bytes as two 4-byte words) lands in its slot everywhere
+    if (int st = nccl_check(n, n->all_gather(mine, comm->d_pairs, 2, ncclFloat32, comm->comm, s), "ncclAllGather"))
+      return st;
+  }
+  return launch_argmax_combine(comm->d_pairs, comm->nranks, d_token, s);
 }
 
 }  // extern "C"

@@ -204,6 +204,21 @@ int efg_comm_destroy(efg_comm* comm);
  * collective failure. */
 int efg_matvec_sharded(int qtype, float* d_y, const uint8_t* d_W_shard, const float* d_x, size_t rows, size_t cols,
                        efg_comm* comm, void* stream);
+/* ef::kern::argmax (src/kernels.cpp:105-111) on the device: *d_index = the index of the
+ * first maximum of d_x[0..n) (NaN never wins, except that a NaN at index 0 is kept; 0 for
+ * n = 0). Stream-ordered. */
+int efg_argmax(const float* d_x, size_t n, int32_t* d_index, void* stream);
+/* The lm_head and the greedy argmax of the decode step (src/model.cpp:266-270, 278-304)
+ * with lm_head row-sharded over the GPUs of one node: d_W_shard holds this rank's rows
+ * (efg_shard_rows) of the [rows][cols] packed lm_head, d_x the whole hidden state and
+ * d_norm_w (or NULL) the final RMSNorm weights. Writes this rank's logits (its row count of
+ * floats) to d_logits_shard and, on every rank, the argmax over all rows (the rule of
+ * efg_argmax) to *d_token: each rank reduces its logits to one (value, index) pair and the
+ * pairs travel in one 8-byte-per-rank all-gather. Every rank calls it with the same
+ * rows/cols. No reference counterpart for the sharding itself. */
+int efg_lm_head_argmax_sharded(int qtype, float* d_logits_shard, int32_t* d_token, const uint8_t* d_W_shard,
+                               const float* d_x, const float* d_norm_w, float eps, size_t rows, size_t cols,
+                               efg_comm* comm, void* stream);
 
 /* ================================================================ .efq and the decode step */
 

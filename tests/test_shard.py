@@ -94,7 +94,83 @@ def test_two_gloo_ranks_assemble_full_y(tmp_path, qt, rows, cols):
         np.testing.assert_array_equal(np.load(tmp_path / f"y{r}.npy"), full)
 
 
+def _local_pair(shard, offset):
+    """One shard's candidate under kern::argmax's rule (src/kernels.cpp:105-111): the largest
+    non-NaN value with the lowest index; (None, -2) when the shard starts the vector with a
+    NaN; (None, -1) when it has no non-NaN value. Mirrors argmax_local_kernel."""
+    if offset == 0 and shard.size and np.isnan(shard[0]):
+        return (0.0, -2)
+    ok = ~np.isnan(shard)
+    if not ok.any():
+        return (0.0, -1)
+    best = shard[ok].max()
+    return (float(best), offset + int(np.nonzero(shard == best)[0][0]))
+
+
+def _combine(pairs):
+    """argmax_combine_kernel: shards in index order, strictly greater wins."""
+    idx, best = -1, 0.0
+    for v, i in pairs:
+        if i == -2:
+            return 0
+        if i >= 0 and (idx < 0 or v > best):
+            idx, best = i, v
+    return max(idx, 0)
+
+
+def _argmax_rank(rank, world, port, cases, out_dir):
+    import torch
+    import torch.distributed as dist
+
+    from oracle.oracle import Oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    o = Oracle()
+    got = []
+    for v in cases:
+        b, c = efg.shard_rows(v.size, world, rank)
+        mine = torch.tensor(_local_pair(v[b:b + c], b), dtype=torch.float64)
+        parts = [torch.empty(2, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(parts, mine)
+        got.append((_combine([(float(t[0]), int(t[1])) for t in parts]), o.argmax(v)))
+    np.save(os.path.join(out_dir, f"argmax{rank}.npy"), np.array(got))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_distributed_argmax(tmp_path):
+    """The row-sharded argmax (efg_lm_head_argmax_sharded) decomposes kern::argmax exactly:
+    per-shard pairs combined in rank order equal the reference's argmax of the whole vector
+    on ties across shards, NaN at index 0, NaN elsewhere, an all-NaN shard and maxima at a
+    shard edge."""
+    import torch.multiprocessing as mp
+
+    rng = np.random.default_rng(3)
+    v = rng.standard_normal(1001).astype(np.float32)
+    tie = v.copy()
+    tie[[100, 900]] = 9.0  # the same maximum in both shards
+    nan0 = v.copy()
+    nan0[0] = np.nan
+    nans = v.copy()
+    nans[::7] = np.nan
+    allnan_b = v.copy()
+    allnan_b[500:] = np.nan  # the second shard holds no number
+    edge = v.copy()
+    edge[500] = 7.0  # first element of shard 1
+    edge2 = v.copy()
+    edge2[499] = 7.0  # last element of shard 0
+    neg = np.full(16, -np.inf, np.float32)
+    cases = [v, tie, nan0, nans, allnan_b, edge, edge2, neg]
+    mp.start_processes(_argmax_rank, args=(2, _free_port(), cases, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        got = np.load(tmp_path / f"argmax{r}.npy")
+        np.testing.assert_array_equal(got[:, 0], got[:, 1])
+
+
 def test_comm_symbols_present():
     lib = efg.load()
-    for name in ("efg_comm_unique_id", "efg_comm_init", "efg_comm_destroy", "efg_matvec_sharded", "efg_shard_rows"):
+    for name in ("efg_comm_unique_id", "efg_comm_init", "efg_comm_destroy", "efg_matvec_sharded", "efg_shard_rows",
+                 "efg_argmax", "efg_lm_head_argmax_sharded"):
         assert isinstance(getattr(lib, name), C._CFuncPtr)

@@ -56,6 +56,58 @@ def test_single_rank(cuda, oracle):
     assert efg.device_error() == 0
 
 
+def _rmsnorm_host(x, w, eps):
+    """h = w * (x * inv), inv = float(1 / sqrt(mean(x^2) + eps)) with the sum in double
+    (src/kernels.cpp:69-75)."""
+    xd = x.astype(np.float64)
+    inv = np.float32(1.0 / np.sqrt((xd * xd).sum() / x.size + eps))
+    return (w * (x * inv)).astype(np.float32)
+
+
+def test_argmax_rule(cuda, oracle):
+    """efg_argmax against kern::argmax: ties keep the lower index, NaN never wins except at
+    index 0, all-NaN and -inf vectors, unaligned starts, n = 0."""
+    import torch
+
+    rng = np.random.default_rng(9)
+    v = rng.standard_normal(32000).astype(np.float32)
+    cases = [v]
+    t = v.copy(); t[[5, 31000]] = 50.0; cases.append(t)
+    t = v.copy(); t[0] = np.nan; cases.append(t)
+    t = v.copy(); t[::3] = np.nan; cases.append(t)
+    cases.append(np.full(1000, np.nan, np.float32))
+    cases.append(np.full(37, -np.inf, np.float32))
+    t = v[:1001].copy(); t[1000] = 99.0; cases.append(t)
+    for c in cases:
+        got = efg.argmax(torch.from_numpy(c).cuda())
+        assert int(got.item()) == oracle.argmax(c)
+    buf = torch.from_numpy(v).cuda()
+    assert int(efg.argmax(buf[1:1001]).item()) == oracle.argmax(v[1:1001])  # 4-byte offset: scalar path
+    assert int(efg.argmax(buf[:0]).item()) == 0
+
+
+def test_lm_head_argmax_single_rank(cuda, oracle):
+    """The lm_head shape (Q8_0 32000 x 2048) with the final RMSNorm on one rank: logits
+    within 1e-5 of sum|w h| of the reference dot, and the token is their argmax."""
+    import torch
+
+    rows, cols = 32000, 2048
+    W, x = _make(torch, QType.Q8_0, rows, cols, 21)
+    nw = (1 + 0.1 * torch.randn(cols, generator=torch.Generator(device="cuda").manual_seed(4), device="cuda"))
+    comm = efg.Comm(efg.Comm.unique_id(), 1, 0)
+    try:
+        logits = torch.full((rows,), float("nan"), device="cuda")
+        tok = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+        efg.lm_head_argmax_sharded(QType.Q8_0, logits, tok, W, x, nw, 1e-5, rows, cols, comm)
+        torch.cuda.synchronize()
+    finally:
+        comm.close()
+    h = _rmsnorm_host(x.cpu().numpy(), nw.cpu().numpy(), 1e-5)
+    _check(oracle, QType.Q8_0, W, torch.from_numpy(h), logits, rows)
+    assert int(tok.item()) == oracle.argmax(logits.cpu().numpy())
+    assert efg.device_error() == 0
+
+
 def _free_port() -> int:
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -84,6 +136,18 @@ def _rank_main(rank, world, port, cases, out_dir):
             if rank == 0:
                 np.save(os.path.join(out_dir, f"W{i}.npy"), W.cpu().numpy())
                 np.save(os.path.join(out_dir, f"x{i}.npy"), x.cpu().numpy())
+        # lm_head sharded over the ranks with the distributed argmax
+        rows, cols = 32000, 2048
+        W, x = _make(torch, QType.Q8_0, rows, cols, 23)
+        nw = 1 + 0.1 * torch.randn(cols, generator=torch.Generator(device="cuda").manual_seed(4), device="cuda")
+        b, c = efg.shard_rows(rows, world, rank)
+        shard = W[b:b + c].contiguous()
+        logits = torch.empty(c, device="cuda")
+        tok = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+        efg.lm_head_argmax_sharded(QType.Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"lm_logits_{rank}.npy"), logits.cpu().numpy())
+        np.save(os.path.join(out_dir, f"lm_tok_{rank}.npy"), tok.cpu().numpy())
         assert efg.device_error() == 0
     finally:
         comm.close()
@@ -110,3 +174,7 @@ def test_multi_rank(tmp_path, oracle):
         W, x = np.load(tmp_path / f"W{i}.npy"), np.load(tmp_path / f"x{i}.npy")
         err = rel_dot_errors(oracle, qt, W, x, rows, ys[0])
         assert err.max() <= TOL, (i, err.max())
+    # the distributed argmax: the same token on every rank, the argmax of all shards' logits
+    full = np.concatenate([np.load(tmp_path / f"lm_logits_{r}.npy") for r in range(n)])
+    toks = [int(np.load(tmp_path / f"lm_tok_{r}.npy")[0]) for r in range(n)]
+    assert len(set(toks)) == 1 and toks[0] == oracle.argmax(full)
