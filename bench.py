@@ -299,6 +299,7 @@ def run_ours(args):
 
     dec = decode_extra(hbm_peak, with_cpu=not args.no_cpu_baseline) if world == 1 and not args.no_decode else None
     shard = None if args.no_sharded else sharded_extra(torch, efg, world, rank, hbm_peak)
+    lmh = None if args.no_sharded else lm_head_extra(torch, efg, world, rank)
     gemm = gemm_extra(torch, efg, bf16_peak) if world == 1 and not args.no_gemm else None
     quant = quant_extra(torch, efg, hbm_peak) if world == 1 and not args.no_gemm else None
 
@@ -337,6 +338,7 @@ def run_ours(args):
                 "bytes_per_launch": algo_bytes(Q4_0, q4_rows, q4_cols), "copies": q4_copies},
                 "config2_decode_tinyllama": dec,
                 "config4_sharded_q4_0_131072x8192": shard,
+                "lm_head_sharded_argmax_32000x2048": lmh,
                 "config3_gemm_q4_0": gemm,
                 "config1_quantize_round_trip": quant},
         }
@@ -469,6 +471,47 @@ def sharded_extra(torch, efg, world, rank, hbm_peak, steps=200, warmup=10, rows=
             "local_matvec_us_cuda_cores": round(ms_local_cc * 1e3, 3),
             "local_frac_of_hbm_cuda_cores": round(shard_bytes / (ms_local_cc / 1e3) / 1e9 / hbm_peak, 4),
             "gather_bytes": 4 * rows, "ranks": world, "rows_per_rank": c, "matrix_bytes": rows * rb,
+            "scaling": "strong"}
+
+
+def lm_head_extra(torch, efg, world, rank, steps=200, warmup=10, rows=32000, cols=2048):
+    """The decode step's last operation with lm_head (Q8_0 32000 x 2048) row-sharded over the
+    job's GPUs: this rank's logits with the final RMSNorm fused, then the argmax over all
+    ranks (efg_lm_head_argmax_sharded: one 8-byte-per-rank all-gather). Device time per call,
+    max over ranks; strong scaling."""
+    b, c = efg.shard_rows(rows, world, rank)
+    rb = cols // 32 * 34
+    g = torch.Generator(device="cuda").manual_seed(200)
+    X = torch.randn(rows, cols, generator=g, device="cuda") * 0.02
+    W = torch.empty(rows * rb, dtype=torch.uint8, device="cuda")
+    efg.quantize_rows(Q8_0, X, rows, cols, W, True)
+    del X
+    shard = W[b * rb:(b + c) * rb].clone()
+    del W
+    x = torch.randn(cols, generator=g, device="cuda")
+    nw = torch.ones(cols, device="cuda")
+    logits = torch.empty(max(c, 1), device="cuda")
+    tok = torch.empty(1, dtype=torch.int32, device="cuda")
+    comm = efg.Comm.from_torch() if world > 1 else efg.Comm(efg.Comm.unique_id(), 1, 0)
+    for _ in range(warmup):
+        efg.lm_head_argmax_sharded(Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(steps):
+        efg.lm_head_argmax_sharded(Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
+    s1.record()
+    torch.cuda.synchronize()
+    ms = s0.elapsed_time(s1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    comm.close()
+    assert efg.device_error() == 0
+    return {"us_per_call": round(ms * 1e3, 3), "ranks": world, "rows_per_rank": c, "token": int(tok.item()),
             "scaling": "strong"}
 
 
