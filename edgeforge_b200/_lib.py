@@ -87,6 +87,8 @@ SIGNATURES = {
     "efg_decoder_reset": (_i, [_vp]),
     "efg_decoder_forward": (_i, [_vp, C.c_int32, _sz, _vp]),
     "efg_decoder_prefill": (_i, [_vp, _vp, _sz, _sz, _vp]),
+    "efg_decoder_set_slots": (_i, [_vp, _sz]),
+    "efg_decoder_step_slots": (_i, [_vp, _vp, _vp, _vp, _sz, _vp, _vp]),
     "efg_decoder_set_mode": (_i, [_vp, _i]),
     "efg_decoder_mode": (_i, [_vp]),
     "efg_decoder_generate": (_i, [_vp, _vp, _sz, _sz, C.c_int32, _vp, _vp, C.POINTER(_sz), _vp,

@@ -388,6 +388,27 @@ class Decoder:
                                          C.c_void_p(out.ctypes.data) if out is not None else None))
         return out
 
+    def set_slots(self, n: int) -> None:
+        """efg_decoder_set_slots: n sequence slots (0 = this decoder's own cache)."""
+        check(load().efg_decoder_set_slots(self._h, int(n)))
+
+    def step_slots(self, slots, tokens, positions, compute_logits: bool = True):
+        """efg_decoder_step_slots: one step of several sequences; returns (logits
+        [n][vocab] or None, argmax tokens [n])."""
+        sl = np.ascontiguousarray(slots, np.int32)
+        tk = np.ascontiguousarray(tokens, np.int32)
+        ps = np.ascontiguousarray(positions, np.int32)
+        n = len(sl)
+        if len(tk) != n or len(ps) != n:
+            raise EdgeForgeError(1, "step_slots: slots, tokens and positions differ in length")
+        lg = np.empty((n, self.vocab), np.float32) if compute_logits else None
+        nxt = np.empty(n, np.int32)
+        check(load().efg_decoder_step_slots(self._h, C.c_void_p(sl.ctypes.data), C.c_void_p(tk.ctypes.data),
+                                            C.c_void_p(ps.ctypes.data), n,
+                                            C.c_void_p(lg.ctypes.data) if lg is not None else None,
+                                            C.c_void_p(nxt.ctypes.data)))
+        return lg, nxt
+
     def generate(self, prompt, max_new: int, eos_id: int = -1, forced=None,
                  keep_step_logits: bool = False) -> GreedyResult:
         """ef::generate_greedy (src/model.cpp:278-304). `forced` (max_new ids) teacher-forces

@@ -296,13 +296,50 @@ __global__ void rope_keys_kernel(float* __restrict__ k_layer, const float* __res
   }
 }
 
+// Multi-sequence step: row b's key (rotated at row_pos[b]) and value into its slot's cache
+// at that position (grid.x = rows).
+__global__ void store_kv_rows_kernel(const float* __restrict__ kb, const float* __restrict__ vb,
+                                     const uint64_t* __restrict__ slot_k, const uint64_t* __restrict__ slot_v,
+                                     const int32_t* __restrict__ row_slot, const int32_t* __restrict__ row_pos,
+                                     uint64_t layer_off, const float* __restrict__ rope_cos,
+                                     const float* __restrict__ rope_sin, int KV, int hd) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x, pos = row_pos[b], half = hd / 2, kvd = KV * hd;
+  float* kc = reinterpret_cast<float*>(slot_k[row_slot[b]]) + layer_off + static_cast<size_t>(pos) * kvd;
+  float* vc = reinterpret_cast<float*>(slot_v[row_slot[b]]) + layer_off + static_cast<size_t>(pos) * kvd;
+  const float* kr = kb + static_cast<size_t>(b) * kvd;
+  const float* c = rope_cos + static_cast<size_t>(pos) * half;
+  const float* s = rope_sin + static_cast<size_t>(pos) * half;
+  for (int e = threadIdx.x; e < KV * half; e += blockDim.x) {
+    const int kv = e / half, i = e % half;
+    rope_pair(kr[kv * hd + i], kr[kv * hd + i + half], c[i], s[i], kc[kv * hd + i], kc[kv * hd + i + half]);
+  }
+  for (int e = threadIdx.x; e < kvd; e += blockDim.x) vc[e] = vb[static_cast<size_t>(b) * kvd + e];
+}
+
+// Multi-sequence step: next[b] = argmax of logits row b (kern::argmax's rule), one CTA per row.
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restrict__ logits, uint32_t n,
+                                                           int32_t* __restrict__ next) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const float* x = logits + static_cast<size_t>(blockIdx.x) * n;
+  float best;
+  uint32_t idx;
+  block_argmax(x, n, best, idx);
+  if (threadIdx.x == 0) next[blockIdx.x] = x[0] != x[0] || idx == 0xFFFFFFFFu ? 0 : static_cast<int32_t>(idx);
+}
+
 // Batched prefill: query head blockIdx.x of token blockIdx.y (position p0 + blockIdx.y),
 // RoPE of q, then attend_head over the cache, which holds every rotated key up to its
 // position (causal: later tokens of the batch are not read).
+// Multi-sequence steps pass row_pos / row_slot: row b attends over its own slot's cache
+// (slot_k[row_slot[b]] + layer_off) up to row_pos[b] instead.
 __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(
     const float* __restrict__ qb, const float* __restrict__ k_layer, const float* __restrict__ v_layer,
     float* __restrict__ ctxb, const float* __restrict__ rope_cos, const float* __restrict__ rope_sin, int p0, int H,
-    int KV, int hd, int dim) {
+    int KV, int hd, int dim, const int32_t* __restrict__ row_pos, const int32_t* __restrict__ row_slot,
+    const uint64_t* __restrict__ slot_k, const uint64_t* __restrict__ slot_v, uint64_t layer_off) {
   extern __shared__ float sm[];
   float* qh = sm;                             // [hd]
   float* stage = qh + hd;                     // [attn_stage_floats(hd)]
@@ -311,7 +348,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_rows_kernel(
   __shared__ double red_d[kAttnThreads / 32];
   pdl_wait();
   pdl_launch_dependents();
-  const int b = blockIdx.y, pos = p0 + b;
+  const int b = blockIdx.y, pos = row_pos ? row_pos[b] : p0 + b;
+  if (row_pos) {
+    k_layer = reinterpret_cast<const float*>(slot_k[row_slot[b]]) + layer_off;
+    v_layer = reinterpret_cast<const float*>(slot_v[row_slot[b]]) + layer_off;
+  }
   const int h = blockIdx.x, group = H / KV, kv = h / group, half = hd / 2, kvd = KV * hd;
   const float* q = qb + static_cast<size_t>(b) * dim;
   const float* c = rope_cos + static_cast<size_t>(pos) * half;
@@ -453,8 +494,17 @@ struct Decoder {
   // batched prefill (prefill_tokens): [P][hidden] x5, [P][intermediate] x3, allocated on first use
   float* pb = nullptr;
   float *xb = nullptr, *hb = nullptr, *qb = nullptr, *cb = nullptr, *ob = nullptr, *gb = nullptr, *ub = nullptr,
-        *ab = nullptr;
+        *ab = nullptr, *kt = nullptr, *vt = nullptr;
   size_t pb_rows = 0;
+  // sequence slots for multi-sequence steps (efg_decoder_set_slots); slot 0 is kc / vc and
+  // `cached`, the cache of forward / prefill / generate
+  size_t n_slots = 1;
+  std::vector<float*> slot_kc, slot_vc;  // slots 1.. (index s - 1)
+  std::vector<size_t> slot_cached;        // slots 1..
+  uint64_t *d_slot_k = nullptr, *d_slot_v = nullptr;  // [n_slots] cache base addresses
+  int32_t* d_rows = nullptr;  // [3][pb_rows]: token, slot, position per row of a step
+  float* d_lb = nullptr;      // [pb_rows][vocab] logits of a step
+  int32_t* d_next = nullptr;  // [pb_rows] argmax of each row
   int32_t* pos_p() const { return state; }
   int32_t* nfix_p() const { return state + 1; }
   int32_t* tokens() const { return state + 2; }
@@ -471,7 +521,7 @@ int check_mat(const Mat& m, const char* name) {
 }
 
 // logits = lm_head . rmsnorm(x, final_norm) (src/model.cpp:266-270).
-int enqueue_lm_head(Decoder& D, const float* x, cudaStream_t s) {
+int enqueue_lm_head(Decoder& D, const float* x, cudaStream_t s, float* out = nullptr) {
   cudaLaunchAttribute attr[1];
   const uint32_t Dm = static_cast<uint32_t>(D.c.hidden);
   MatvecArgs a;
@@ -482,7 +532,7 @@ int enqueue_lm_head(Decoder& D, const float* x, cudaStream_t s) {
   a.cols = Dm;
   a.pdl = true;
   a.n_jobs = 1;
-  a.jobs[0] = MatvecJobDev{D.lm_head.w, D.logits, D.lm_head.rows, 0};
+  a.jobs[0] = MatvecJobDev{D.lm_head.w, out ? out : D.logits, D.lm_head.rows, 0};
   if (!matvec_fast_path_ok(a)) {
     cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(256), 0, s, attr);
     EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rmsnorm_kernel, D.h, x, D.final_norm, Dm, static_cast<float>(D.c.rms_eps)),
@@ -826,12 +876,25 @@ int device_status(Decoder& D) {
   return EFG_OK;
 }
 
+void free_slots(Decoder& D) {
+  for (float* p : D.slot_kc) cudaFree(p);
+  for (float* p : D.slot_vc) cudaFree(p);
+  D.slot_kc.clear();
+  D.slot_vc.clear();
+  D.slot_cached.clear();
+  D.n_slots = 1;
+}
+
 void destroy(Decoder* D) {
   if (!D) return;
   if (D->stream) cudaStreamSynchronize(D->stream);
   if (D->g_full) cudaGraphExecDestroy(D->g_full);
   if (D->g_prefill) cudaGraphExecDestroy(D->g_prefill);
   if (D->pb) cudaFree(D->pb);
+  free_slots(*D);
+  for (void* p : {static_cast<void*>(D->d_slot_k), static_cast<void*>(D->d_slot_v), static_cast<void*>(D->d_rows),
+                  static_cast<void*>(D->d_lb), static_cast<void*>(D->d_next)})
+    if (p) cudaFree(p);
   for (void* p : {static_cast<void*>(D->d_data), static_cast<void*>(D->kc), static_cast<void*>(D->vc),
                   static_cast<void*>(D->rcos), static_cast<void*>(D->rsin), static_cast<void*>(D->x),
                   static_cast<void*>(D->state), static_cast<void*>(D->d_phases), static_cast<void*>(D->d_bar),
@@ -993,11 +1056,13 @@ int ensure_prefill_buffers(Decoder& D) {
   const size_t P = std::min(kPrefillRows, D.max_seq), Dm = static_cast<size_t>(D.c.hidden),
                F = static_cast<size_t>(D.c.intermediate);
   auto al = [](size_t n) { return (n * sizeof(float) + 255) / 256 * 256; };
-  EFG_TRY_CUDA(cudaMalloc(&D.pb, al(P * Dm) * 5 + al(P * F) * 3), "prefill buffer allocation");
+  const size_t kvd = static_cast<size_t>(D.c.kv_dim());
+  EFG_TRY_CUDA(cudaMalloc(&D.pb, al(P * Dm) * 5 + al(P * F) * 3 + al(P * kvd) * 2), "prefill buffer allocation");
   uint8_t* a = reinterpret_cast<uint8_t*>(D.pb);
   size_t o = 0;
   for (float** b : {&D.xb, &D.hb, &D.qb, &D.cb, &D.ob}) *b = reinterpret_cast<float*>(a + o), o += al(P * Dm);
   for (float** b : {&D.gb, &D.ub, &D.ab}) *b = reinterpret_cast<float*>(a + o), o += al(P * F);
+  for (float** b : {&D.kt, &D.vt}) *b = reinterpret_cast<float*>(a + o), o += al(P * kvd);
   D.pb_rows = P;
   return EFG_OK;
 }
@@ -1018,9 +1083,11 @@ int batched_proj(Decoder& D, const Mat& M, const float* X, float* Y, size_t n, c
   return EFG_OK;
 }
 
-// Tokens tokens()[p0..p0+n) (already on the device), n <= pb_rows; with `logits`, the last
-// token's logits in D.logits.
-int prefill_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s) {
+// n <= pb_rows rows through every layer. Prefill (multi = false): tokens tokens()[p0..p0+n)
+// of slot 0 at positions p0..; with `logits`, the last token's logits in D.logits.
+// Multi-sequence step (multi = true): row b is d_rows' (token, slot, position); every
+// row's logits into d_lb and its argmax into d_next.
+int batch_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s, bool multi = false) {
   cudaLaunchAttribute attr[1];
   const uint32_t Dm = static_cast<uint32_t>(D.c.hidden), F = static_cast<uint32_t>(D.c.intermediate),
                  V = static_cast<uint32_t>(D.c.vocab);
@@ -1032,9 +1099,11 @@ int prefill_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s) {
   {
     cudaLaunchConfig_t cf = cfg_of(dim3(std::max(1u, std::min(16u, (Dm + 255) / 256)), nb), dim3(256), 0, s, attr);
     EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, embed_rows_kernel, D.embed.w, D.embed.type, V, Dm,
-                                    static_cast<const int32_t*>(D.tokens() + p0), D.xb, D.d_err),
+                                    static_cast<const int32_t*>(multi ? D.d_rows : D.tokens() + p0), D.xb, D.d_err),
                  "embed launch");
   }
+  const int32_t* row_slot = multi ? D.d_rows + D.pb_rows : nullptr;
+  const int32_t* row_pos = multi ? D.d_rows + 2 * D.pb_rows : nullptr;
   for (size_t l = 0; l < D.layers.size(); ++l) {
     const Layer& Ly = D.layers[l];
     float* kl = D.kc + l * D.max_seq * kvd;
@@ -1043,14 +1112,24 @@ int prefill_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s) {
     EFG_TRY_CUDA(cudaLaunchKernelEx(&cn, rmsnorm_rows_kernel, D.hb, static_cast<const float*>(D.xb), Ly.attn_norm, Dm,
                                     eps),
                  "rmsnorm launch");
+    const uint64_t layer_off = static_cast<uint64_t>(l) * D.max_seq * kvd;
     if (int st = batched_proj(D, Ly.q, D.hb, D.qb, n, s)) return st;
-    if (int st = batched_proj(D, Ly.k, D.hb, kl + p0 * kvd, n, s)) return st;  // unrotated keys, rotated below
-    if (int st = batched_proj(D, Ly.v, D.hb, vl + p0 * kvd, n, s)) return st;
-    {
+    if (!multi) {
+      if (int st = batched_proj(D, Ly.k, D.hb, kl + p0 * kvd, n, s)) return st;  // unrotated keys, rotated below
+      if (int st = batched_proj(D, Ly.v, D.hb, vl + p0 * kvd, n, s)) return st;
       cudaLaunchConfig_t cf = cfg_of(dim3(nb), dim3(128), 0, s, attr);
       EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rope_keys_kernel, kl, static_cast<const float*>(D.rcos),
                                       static_cast<const float*>(D.rsin), static_cast<int>(p0), KV, hd),
                    "rope launch");
+    } else {  // each row's key and value into its own slot's cache
+      if (int st = batched_proj(D, Ly.k, D.hb, D.kt, n, s)) return st;
+      if (int st = batched_proj(D, Ly.v, D.hb, D.vt, n, s)) return st;
+      cudaLaunchConfig_t cf = cfg_of(dim3(nb), dim3(128), 0, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, store_kv_rows_kernel, static_cast<const float*>(D.kt),
+                                      static_cast<const float*>(D.vt), static_cast<const uint64_t*>(D.d_slot_k),
+                                      static_cast<const uint64_t*>(D.d_slot_v), row_slot, row_pos, layer_off,
+                                      static_cast<const float*>(D.rcos), static_cast<const float*>(D.rsin), KV, hd),
+                   "kv store launch");
     }
     {
       const size_t smem = (hd + attn_stage_floats(hd) + D.max_seq) * sizeof(float);
@@ -1058,7 +1137,9 @@ int prefill_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s) {
       EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, attention_rows_kernel, static_cast<const float*>(D.qb),
                                       static_cast<const float*>(kl), static_cast<const float*>(vl), D.cb,
                                       static_cast<const float*>(D.rcos), static_cast<const float*>(D.rsin),
-                                      static_cast<int>(p0), H, KV, hd, static_cast<int>(Dm)),
+                                      static_cast<int>(p0), H, KV, hd, static_cast<int>(Dm), row_pos, row_slot,
+                                      static_cast<const uint64_t*>(D.d_slot_k), static_cast<const uint64_t*>(D.d_slot_v),
+                                      layer_off),
                    "attention launch");
     }
     if (int st = batched_proj(D, Ly.o, D.cb, D.ob, n, s)) return st;
@@ -1083,6 +1164,14 @@ int prefill_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s) {
       EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, add_kernel, D.xb, static_cast<const float*>(D.ob), n * Dm), "add launch");
     }
   }
+  if (multi) {
+    for (size_t b = 0; b < n; ++b)
+      if (int st = enqueue_lm_head(D, D.xb + b * Dm, s, D.d_lb + b * V)) return st;
+    cudaLaunchConfig_t cf = cfg_of(dim3(nb), dim3(1024), 0, s, attr);
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, argmax_rows_kernel, static_cast<const float*>(D.d_lb), V, D.d_next),
+                 "argmax launch");
+    return EFG_OK;
+  }
   if (logits) return enqueue_lm_head(D, D.xb + (n - 1) * Dm, s);
   return EFG_OK;
 }
@@ -1092,10 +1181,49 @@ int prefill_tokens(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s)
   if (int st = ensure_prefill_buffers(D)) return st;
   for (size_t c0 = 0; c0 < n; c0 += D.pb_rows) {
     const size_t cn = std::min(D.pb_rows, n - c0);
-    if (int st = prefill_pass(D, p0 + c0, cn, logits && c0 + cn == n, s)) return st;
+    if (int st = batch_pass(D, p0 + c0, cn, logits && c0 + cn == n, s)) return st;
   }
   return EFG_OK;
 }
+
+// Slots 1..n-1 get fresh (zeroed) caches; slot 0 keeps the decoder's own.
+int set_slots(Decoder& D, size_t n) {
+  if (n < 1 || n > 4096) return fail(EFG_EINVAL, "set_slots: %zu slots (1..4096)", n);
+  EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+  free_slots(D);
+  const size_t bytes = static_cast<size_t>(D.c.layers) * D.max_seq * static_cast<size_t>(D.c.kv_dim()) * sizeof(float);
+  for (size_t i = 1; i < n; ++i) {
+    float *k = nullptr, *v = nullptr;
+    if (cudaMalloc(&k, bytes) != cudaSuccess || cudaMalloc(&v, bytes) != cudaSuccess) {
+      if (k) cudaFree(k);
+      free_slots(D);
+      return fail(EFG_ECUDA, "set_slots: KV-cache allocation for %zu slots", n);
+    }
+    D.slot_kc.push_back(k);
+    D.slot_vc.push_back(v);
+    D.slot_cached.push_back(0);
+    EFG_TRY_CUDA(cudaMemset(k, 0, bytes), "KV cache init");
+    EFG_TRY_CUDA(cudaMemset(v, 0, bytes), "KV cache init");
+  }
+  D.n_slots = n;
+  if (D.d_slot_k) cudaFree(D.d_slot_k);
+  if (D.d_slot_v) cudaFree(D.d_slot_v);
+  D.d_slot_k = D.d_slot_v = nullptr;
+  std::vector<uint64_t> hk(n), hv(n);
+  hk[0] = reinterpret_cast<uint64_t>(D.kc);
+  hv[0] = reinterpret_cast<uint64_t>(D.vc);
+  for (size_t i = 1; i < n; ++i) {
+    hk[i] = reinterpret_cast<uint64_t>(D.slot_kc[i - 1]);
+    hv[i] = reinterpret_cast<uint64_t>(D.slot_vc[i - 1]);
+  }
+  EFG_TRY_CUDA(cudaMalloc(&D.d_slot_k, n * sizeof(uint64_t)), "slot table allocation");
+  EFG_TRY_CUDA(cudaMalloc(&D.d_slot_v, n * sizeof(uint64_t)), "slot table allocation");
+  EFG_TRY_CUDA(cudaMemcpy(D.d_slot_k, hk.data(), n * sizeof(uint64_t), cudaMemcpyHostToDevice), "slot table upload");
+  EFG_TRY_CUDA(cudaMemcpy(D.d_slot_v, hv.data(), n * sizeof(uint64_t), cudaMemcpyHostToDevice), "slot table upload");
+  return EFG_OK;
+}
+
+size_t& slot_cached(Decoder& D, size_t s) { return s == 0 ? D.cached : D.slot_cached[s - 1]; }
 
 int set_step(Decoder& D, int32_t token, size_t pos, int32_t n_fixed) {
   const int32_t st[2] = {static_cast<int32_t>(pos), n_fixed};
@@ -1322,6 +1450,64 @@ int efg_decoder_generate(efg_decoder* h, const int32_t* prompt, size_t n_prompt,
   if (decode_seconds) *decode_seconds = ms_dec / 1e3;
   if (n_tokens) *n_tokens = n_out;
   D.cached = n_prompt + (n_out ? n_out - 1 : 0);
+  return EFG_OK;
+}
+
+int efg_decoder_set_slots(efg_decoder* h, size_t n_slots) {
+  if (!h) return fail(EFG_EINVAL, "set_slots: null handle");
+  return efg::set_slots(*reinterpret_cast<Decoder*>(h), n_slots);
+}
+
+int efg_decoder_step_slots(efg_decoder* h, const int32_t* slots, const int32_t* tokens, const int32_t* positions,
+                           size_t n, float* logits, int32_t* next_tokens) {
+  if (!h || !slots || !tokens || !positions) return fail(EFG_EINVAL, "step_slots: null argument");
+  Decoder& D = *reinterpret_cast<Decoder*>(h);
+  if (n == 0) return fail(EFG_EINVAL, "step_slots: no rows");
+  std::vector<char> seen(D.n_slots, 0);
+  for (size_t b = 0; b < n; ++b) {
+    if (slots[b] < 0 || static_cast<size_t>(slots[b]) >= D.n_slots)
+      return fail(EFG_EINVAL, "step_slots: slot %d is outside [0, %zu)", slots[b], D.n_slots);
+    if (seen[slots[b]]++) return fail(EFG_EINVAL, "step_slots: slot %d appears twice in one step", slots[b]);
+    if (tokens[b] < 0 || tokens[b] >= D.c.vocab)
+      return fail(EFG_EINVAL, "step_slots: token id %d is outside [0, %lld)", tokens[b],
+                  static_cast<long long>(D.c.vocab));
+    const size_t pos = static_cast<size_t>(positions[b]);
+    if (positions[b] < 0 || pos >= D.max_seq)
+      return fail(EFG_ESTATE, "step_slots: position %d exceeds the KV-cache capacity %zu", positions[b], D.max_seq);
+    if (pos > efg::slot_cached(D, slots[b]))
+      return fail(EFG_ESTATE, "step_slots: position %zu skips ahead of the %zu cached tokens of slot %d", pos,
+                  efg::slot_cached(D, slots[b]), slots[b]);
+  }
+  if (int st = efg::ensure_prefill_buffers(D)) return st;
+  if (!D.d_rows) {
+    EFG_TRY_CUDA(cudaMalloc(&D.d_rows, 3 * D.pb_rows * sizeof(int32_t)), "step buffer allocation");
+    EFG_TRY_CUDA(cudaMalloc(&D.d_lb, D.pb_rows * D.c.vocab * sizeof(float)), "step buffer allocation");
+    EFG_TRY_CUDA(cudaMalloc(&D.d_next, D.pb_rows * sizeof(int32_t)), "step buffer allocation");
+  }
+  if (D.n_slots == 1 && !D.d_slot_k)
+    if (int st = efg::set_slots(D, 1)) return st;
+  for (size_t c0 = 0; c0 < n; c0 += D.pb_rows) {
+    const size_t cn = std::min(D.pb_rows, n - c0);
+    std::vector<int32_t> rows(3 * D.pb_rows, 0);
+    for (size_t b = 0; b < cn; ++b) {
+      rows[b] = tokens[c0 + b];
+      rows[D.pb_rows + b] = slots[c0 + b];
+      rows[2 * D.pb_rows + b] = positions[c0 + b];
+    }
+    EFG_TRY_CUDA(cudaMemcpyAsync(D.d_rows, rows.data(), rows.size() * sizeof(int32_t), cudaMemcpyHostToDevice, D.stream),
+                 "row upload");
+    if (int st = efg::batch_pass(D, 0, cn, true, D.stream, true)) return st;
+    if (logits)
+      EFG_TRY_CUDA(cudaMemcpyAsync(logits + c0 * D.c.vocab, D.d_lb, cn * D.c.vocab * sizeof(float),
+                                   cudaMemcpyDeviceToHost, D.stream),
+                   "logits download");
+    if (next_tokens)
+      EFG_TRY_CUDA(cudaMemcpyAsync(next_tokens + c0, D.d_next, cn * sizeof(int32_t), cudaMemcpyDeviceToHost, D.stream),
+                   "token download");
+    EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+  }
+  if (int st = efg::device_status(D)) return st;
+  for (size_t b = 0; b < n; ++b) efg::slot_cached(D, slots[b]) = static_cast<size_t>(positions[b]) + 1;
   return EFG_OK;
 }
 

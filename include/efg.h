@@ -283,6 +283,18 @@ int efg_decoder_prefill(efg_decoder* d, const int32_t* tokens, size_t n, size_t 
 int efg_decoder_generate(efg_decoder* d, const int32_t* prompt, size_t n_prompt, size_t max_new, int32_t eos_id,
                          const int32_t* forced, int32_t* tokens_out, size_t* n_tokens, float* step_logits,
                          double* prefill_seconds, double* decode_seconds);
+/* Sequence slots for decoding several sequences together: slot 0 is the decoder's own KV
+ * cache (forward, prefill, generate); slots 1..n_slots-1 get caches of their own, zeroed
+ * (a second call resets them). */
+int efg_decoder_set_slots(efg_decoder* d, size_t n_slots);
+/* One decode step of n independent sequences at once (src/model.cpp:184-270 for each):
+ * row b feeds tokens[b] at positions[b] (<= slot slots[b]'s cached count, which it rewinds
+ * like forward) of slot slots[b] (distinct within a call). All rows share the weight
+ * reads: Q4_0 projections as one tensor-core GEMM per matrix, Q8_0 ones one matvec per
+ * row. Writes each row's logits (n * vocab floats) and its argmax (n ints) unless NULL.
+ * No reference counterpart: the reference decodes one sequence at a time. */
+int efg_decoder_step_slots(efg_decoder* d, const int32_t* slots, const int32_t* tokens, const int32_t* positions,
+                           size_t n, float* logits, int32_t* next_tokens);
 /* How the decode step runs: 0 = a CUDA graph of one kernel per operation (the default),
  * 1 = one persistent kernel per launch (one CTA per SM, the weights streamed through shared
  * memory across grid barriers). Both follow the reference's arithmetic. EFG_EINVAL when 1 is

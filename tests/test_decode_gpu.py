@@ -192,6 +192,53 @@ def test_medium_batched_prefill(medium):
         assert efg.device_error() == 0
 
 
+def test_medium_multi_sequence_step(medium):
+    """Three sequences of different lengths in three slots, stepped together (their rows
+    share each GEMM): each one's logits after its last token match the reference decoder
+    run on that sequence alone."""
+    from oracle.oracle import Oracle, OracleDecoder
+
+    efq = medium[0]
+    rng = np.random.default_rng(21)
+    seqs = [rng.integers(0, 300, n).astype(np.int32) for n in (9, 4, 13)]
+    o = Oracle()
+    want = [OracleDecoder(o, efq, 64).run(s, np.array([1], np.int32), threads=4)[0] for s in seqs]
+    with efg.Decoder(efq, 64) as dec:
+        dec.set_slots(3)
+        last = [None] * 3
+        for t in range(max(len(s) for s in seqs)):
+            live = [i for i, s in enumerate(seqs) if t < len(s)]
+            lg, nxt = dec.step_slots(live, [seqs[i][t] for i in live], [t] * len(live))
+            np.testing.assert_array_equal(nxt, np.argmax(lg, axis=1))
+            for r, i in enumerate(live):
+                last[i] = lg[r]
+        for i in range(3):
+            assert np.abs(last[i] - want[i]).max() <= TOL, i
+        assert efg.device_error() == 0
+
+
+def test_multi_sequence_matches_forward(z):
+    """Slot 0 is the decoder's own cache: a step of slot 0 continues a forward() run, and a
+    sequence replayed in slot 1 gives forward()'s logits."""
+    prompt = z["prompt"]
+    with efg.Decoder(GOLD / "decode_tiny_mixed.efq", MAX_SEQ) as dec:
+        ref = [dec.forward(int(t), i) for i, t in enumerate(prompt)]
+        dec.set_slots(2)
+        for i, t in enumerate(prompt):
+            lg, _ = dec.step_slots([1], [t], [i])
+            assert np.abs(lg[0] - ref[i]).max() <= TOL
+        lg, _ = dec.step_slots([0, 1], [5, 5], [len(prompt), len(prompt)])
+        assert np.abs(lg[0] - lg[1]).max() <= TOL  # same history in both slots
+        want = dec.forward(5, len(prompt))  # rewinds slot 0 to the same position
+        assert np.abs(lg[0] - want).max() <= TOL
+        with pytest.raises(efg.EdgeForgeError, match="twice"):
+            dec.step_slots([1, 1], [1, 2], [0, 0])
+        with pytest.raises(efg.EdgeForgeError, match="outside"):
+            dec.step_slots([2], [1], [0])
+        with pytest.raises(efg.EdgeForgeError, match="skips ahead"):
+            dec.step_slots([1], [1], [40])
+
+
 @pytest.mark.parametrize("persistent", [True, False])
 def test_medium_forward_and_generate(medium, persistent):
     efq, prompt, forced, ref = medium
