@@ -384,12 +384,29 @@ def decode_extra(hbm_peak, with_cpu, prompt_len=23, steps=32, reps=5):
             runs.append((r.decode_seconds, r.prefill_seconds, time.perf_counter() - t0))
         bpt = dec.bytes_per_token
         tokens = r.tokens
+        # several sequences at once (efg_decoder_step_slots): S slots, each fed its own
+        # 23-token prompt through the batch step, then `steps` greedy steps of all S rows
+        batch = {}
+        rng = np.random.default_rng(3)
+        for S in (8, 32, 64):
+            dec.set_slots(S)
+            prompts = rng.integers(0, 32000, (S, prompt_len)).astype(np.int32)
+            slots = np.arange(S, dtype=np.int32)
+            for t in range(prompt_len):
+                _, nxt = dec.step_slots(slots, prompts[:, t], np.full(S, t, np.int32), compute_logits=False)
+            t0 = time.perf_counter()
+            for k in range(steps - 1):
+                _, nxt = dec.step_slots(slots, nxt, np.full(S, prompt_len + k, np.int32), compute_logits=False)
+            el = time.perf_counter() - t0
+            batch[f"S{S}"] = {"tok_s": round(S * (steps - 1) / el, 1), "ms_per_step": round(el / (steps - 1) * 1e3, 3)}
+        dec.set_slots(1)
     dsec, psec, wall = min(runs)
     tok_s = (steps - 1) / dsec
     out = {"decode_tok_s": round(tok_s, 1), "prefill_tok_s": round(prompt_len / psec, 1),
            "weight_gbs": round(bpt * tok_s / 1e9, 1), "frac_of_hbm": round(bpt * tok_s / 1e9 / hbm_peak, 4),
            "ms_per_token": round(dsec / (steps - 1) * 1e3, 4), "bytes_per_token": bpt,
            "e2e_generate_s": round(wall, 5), "prompt": prompt_len, "steps": steps,
+           "batch_decode": dict(batch, note="efg_decoder_step_slots, S sequences per step, host wall time per step"),
            "model": "random TinyLlama-1.1B shape, .efq from efg_quantize_model (policy auto)"}
     if with_cpu and (ROOT / "oracle" / "_ref" / "libefref.so").exists():
         from oracle.oracle import Reference

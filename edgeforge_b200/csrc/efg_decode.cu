@@ -21,6 +21,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -496,6 +497,8 @@ struct Decoder {
   float *xb = nullptr, *hb = nullptr, *qb = nullptr, *cb = nullptr, *ob = nullptr, *gb = nullptr, *ub = nullptr,
         *ab = nullptr, *kt = nullptr, *vt = nullptr;
   size_t pb_rows = 0;
+  void* gemm_ws = nullptr;  // the GEMM's split-X workspace for pb_rows rows (stable for graphs)
+  size_t gemm_ws_cap = 0;
   // sequence slots for multi-sequence steps (efg_decoder_set_slots); slot 0 is kc / vc and
   // `cached`, the cache of forward / prefill / generate
   size_t n_slots = 1;
@@ -505,6 +508,7 @@ struct Decoder {
   int32_t* d_rows = nullptr;  // [3][pb_rows]: token, slot, position per row of a step
   float* d_lb = nullptr;      // [pb_rows][vocab] logits of a step
   int32_t* d_next = nullptr;  // [pb_rows] argmax of each row
+  std::map<size_t, cudaGraphExec_t> step_graphs;  // a multi-sequence step per row count
   int32_t* pos_p() const { return state; }
   int32_t* nfix_p() const { return state + 1; }
   int32_t* tokens() const { return state + 2; }
@@ -876,6 +880,11 @@ int device_status(Decoder& D) {
   return EFG_OK;
 }
 
+void drop_step_graphs(Decoder& D) {
+  for (auto& kv : D.step_graphs) cudaGraphExecDestroy(kv.second);
+  D.step_graphs.clear();
+}
+
 void free_slots(Decoder& D) {
   for (float* p : D.slot_kc) cudaFree(p);
   for (float* p : D.slot_vc) cudaFree(p);
@@ -891,6 +900,8 @@ void destroy(Decoder* D) {
   if (D->g_full) cudaGraphExecDestroy(D->g_full);
   if (D->g_prefill) cudaGraphExecDestroy(D->g_prefill);
   if (D->pb) cudaFree(D->pb);
+  if (D->gemm_ws) cudaFree(D->gemm_ws);
+  drop_step_graphs(*D);
   free_slots(*D);
   for (void* p : {static_cast<void*>(D->d_slot_k), static_cast<void*>(D->d_slot_v), static_cast<void*>(D->d_rows),
                   static_cast<void*>(D->d_lb), static_cast<void*>(D->d_next)})
@@ -1063,13 +1074,15 @@ int ensure_prefill_buffers(Decoder& D) {
   for (float** b : {&D.xb, &D.hb, &D.qb, &D.cb, &D.ob}) *b = reinterpret_cast<float*>(a + o), o += al(P * Dm);
   for (float** b : {&D.gb, &D.ub, &D.ab}) *b = reinterpret_cast<float*>(a + o), o += al(P * F);
   for (float** b : {&D.kt, &D.vt}) *b = reinterpret_cast<float*>(a + o), o += al(P * kvd);
+  D.gemm_ws_cap = gemm_ws_bytes(static_cast<size_t>(std::max(D.c.hidden, D.c.intermediate)), P);
+  if (D.gemm_ws_cap) EFG_TRY_CUDA(cudaMalloc(&D.gemm_ws, D.gemm_ws_cap), "gemm workspace allocation");
   D.pb_rows = P;
   return EFG_OK;
 }
 
 // Y[b] = M . X[b] for b < n (X [n][M.cols], Y [n][M.rows]).
 int batched_proj(Decoder& D, const Mat& M, const float* X, float* Y, size_t n, cudaStream_t s) {
-  if (M.type == 4) return launch_gemm_q4_0(Y, M.w, X, M.rows, M.cols, n, D.d_err, s);
+  if (M.type == 4) return launch_gemm_q4_0(Y, M.w, X, M.rows, M.cols, n, D.d_err, s, D.gemm_ws, D.gemm_ws_cap);
   for (size_t b = 0; b < n; ++b) {
     MatvecArgs a;
     a.fmt = Fmt::Q8;
@@ -1190,6 +1203,7 @@ int prefill_tokens(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s)
 int set_slots(Decoder& D, size_t n) {
   if (n < 1 || n > 4096) return fail(EFG_EINVAL, "set_slots: %zu slots (1..4096)", n);
   EFG_TRY_CUDA(cudaStreamSynchronize(D.stream), "stream synchronize");
+  drop_step_graphs(D);  // they hold the old slot table
   free_slots(D);
   const size_t bytes = static_cast<size_t>(D.c.layers) * D.max_seq * static_cast<size_t>(D.c.kv_dim()) * sizeof(float);
   for (size_t i = 1; i < n; ++i) {
@@ -1224,6 +1238,36 @@ int set_slots(Decoder& D, size_t n) {
 }
 
 size_t& slot_cached(Decoder& D, size_t s) { return s == 0 ? D.cached : D.slot_cached[s - 1]; }
+
+// One multi-sequence pass of cn rows (d_rows already uploaded). The first pass of a row count
+// runs directly (it also allocates lazily created workspaces), then is recorded as a CUDA
+// graph that later steps of the same row count replay: a step is ~20 launches per layer
+// plus per-row launches, too many to issue from the host at the GPU's pace.
+int step_pass(Decoder& D, size_t cn) {
+  auto it = D.step_graphs.find(cn);
+  if (it != D.step_graphs.end()) {
+    EFG_TRY_CUDA(cudaGraphLaunch(it->second, D.stream), "graph launch");
+    return EFG_OK;
+  }
+  if (int st = batch_pass(D, 0, cn, true, D.stream, true)) return st;
+  cudaGraph_t g = nullptr;
+  if (cudaStreamBeginCapture(D.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    cudaGetLastError();
+    return EFG_OK;  // run uncaptured next time as well
+  }
+  const int st = batch_pass(D, 0, cn, true, D.stream, true);
+  const cudaError_t e = cudaStreamEndCapture(D.stream, &g);
+  if (st != EFG_OK || e != cudaSuccess || !g) {
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    return EFG_OK;
+  }
+  cudaGraphExec_t ge = nullptr;
+  if (cudaGraphInstantiate(&ge, g, 0) == cudaSuccess) D.step_graphs[cn] = ge;
+  cudaGraphDestroy(g);
+  cudaGetLastError();
+  return EFG_OK;
+}
 
 int set_step(Decoder& D, int32_t token, size_t pos, int32_t n_fixed) {
   const int32_t st[2] = {static_cast<int32_t>(pos), n_fixed};
@@ -1496,7 +1540,7 @@ int efg_decoder_step_slots(efg_decoder* h, const int32_t* slots, const int32_t* 
     }
     EFG_TRY_CUDA(cudaMemcpyAsync(D.d_rows, rows.data(), rows.size() * sizeof(int32_t), cudaMemcpyHostToDevice, D.stream),
                  "row upload");
-    if (int st = efg::batch_pass(D, 0, cn, true, D.stream, true)) return st;
+    if (int st = efg::step_pass(D, cn)) return st;
     if (logits)
       EFG_TRY_CUDA(cudaMemcpyAsync(logits + c0 * D.c.vocab, D.d_lb, cn * D.c.vocab * sizeof(float),
                                    cudaMemcpyDeviceToHost, D.stream),

@@ -569,28 +569,40 @@ GemmScratch g_gemm_scratch[64];
 
 // The warp-specialised path (K % 256 == 0): split X, then the GEMM with split-K over a
 // cluster of S CTAs sized so that ~one wave covers the SMs.
+size_t gemm_ws_bytes(size_t K, size_t B) {
+  if (K % kRawK != 0 || B == 0) return 0;
+  const size_t n_tile = std::min<size_t>(kMaxTileN2, (B + 15) / 16 * 16);
+  return (B + n_tile - 1) / n_tile * (K / kChunkK) * 2 * n_tile * 128;
+}
+
 int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
-                   cudaStream_t s) {
+                   cudaStream_t s, void* ws, size_t ws_cap) {
   DeviceInfo* dev = current_device();
   if (!dev) return EFG_ECUDA;
   const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN2, (B + 15) / 16 * 16));
   const uint32_t n_tiles = static_cast<uint32_t>((B + n_tile - 1) / n_tile);
   const uint32_t m_tiles = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
-  const size_t ws_bytes = static_cast<size_t>(n_tiles) * (K / kChunkK) * 2 * n_tile * 128;
+  const size_t ws_bytes = gemm_ws_bytes(K, B);
   GemmScratch& gs = g_gemm_scratch[dev->device];
-  std::lock_guard<std::mutex> lk(gs.mu);
-  if (ws_bytes > gs.cap) {
-    if (gs.p) cudaFree(gs.p);
-    gs.p = nullptr;
-    gs.cap = 0;
-    EFG_TRY_CUDA(cudaMalloc(&gs.p, ws_bytes), "gemm workspace");
-    gs.cap = ws_bytes;
+  std::unique_lock<std::mutex> lk(gs.mu, std::defer_lock);
+  if (ws) {  // the caller's workspace (stable for CUDA graphs, not shared with other callers)
+    if (ws_cap < ws_bytes) return fail(EFG_EINVAL, "gemm: workspace of %zu bytes, %zu needed", ws_cap, ws_bytes);
+  } else {
+    lk.lock();
+    if (ws_bytes > gs.cap) {
+      if (gs.p) cudaFree(gs.p);
+      gs.p = nullptr;
+      gs.cap = 0;
+      EFG_TRY_CUDA(cudaMalloc(&gs.p, ws_bytes), "gemm workspace");
+      gs.cap = ws_bytes;
+    }
+    ws = gs.p;
   }
   {
     const uint64_t items = static_cast<uint64_t>(n_tiles) * (K / kChunkK) * n_tile * 8;
     const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((items + 255) / 256, 8ull * dev->sm_count));
     split_x_kernel<<<grid, 256, 0, s>>>(X, static_cast<uint32_t>(B), static_cast<uint32_t>(K), n_tile,
-                                        static_cast<uint8_t*>(gs.p), n_tiles);
+                                        static_cast<uint8_t*>(ws), n_tiles);
     EFG_TRY_CUDA(cudaGetLastError(), "gemm split launch");
   }
   const size_t smem = 1024 + kOpStages * (kOpABytes + 2 * static_cast<size_t>(n_tile) * 128) + kRawStages * kRawBytes;
@@ -598,7 +610,7 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
   const uint32_t raw_total = static_cast<uint32_t>(K / kRawK);
   uint32_t S = std::max<uint32_t>(1, static_cast<uint32_t>(dev->sm_count) / (m_tiles * n_tiles));
   S = std::min<uint32_t>({S, 8u, std::max<uint32_t>(1, raw_total / 2)});
-  GemmWsParams p{W, static_cast<const uint8_t*>(gs.p), Y, static_cast<uint32_t>(M), static_cast<uint32_t>(K),
+  GemmWsParams p{W, static_cast<const uint8_t*>(ws), Y, static_cast<uint32_t>(M), static_cast<uint32_t>(K),
                  static_cast<uint32_t>(B), static_cast<uint32_t>(K / 32 * 18), n_tile, 1, d_err};
   for (;; S /= 2) {  // the largest cluster the device can place
     p.S = std::max(S, 1u);
@@ -629,7 +641,7 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
 }
 
 int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
-                     cudaStream_t s) {
+                     cudaStream_t s, void* ws, size_t ws_cap) {
   if (K % 32 != 0) return fail(EFG_EINVAL, "Q4_0 needs a row length divisible by 32, got %zu", K);
   if (M == 0 || B == 0) return EFG_OK;
   if (!Y || (K && (!W || !X))) return fail(EFG_EINVAL, "gemm: null pointer");
@@ -641,7 +653,8 @@ int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
   if (reinterpret_cast<uintptr_t>(X) % 16 != 0 || reinterpret_cast<uintptr_t>(W) % 2 != 0 ||
       reinterpret_cast<uintptr_t>(Y) % 4 != 0)
     return fail(EFG_EINVAL, "gemm: X must be 16-byte aligned, W 2-byte aligned and Y 4-byte aligned");
-  if (K % kRawK == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0) return launch_gemm_ws(Y, W, X, M, K, B, d_err, s);
+  if (K % kRawK == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0)
+    return launch_gemm_ws(Y, W, X, M, K, B, d_err, s, ws, ws_cap);
   const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN, (B + 15) / 16 * 16));
   GemmParams p{W, X, Y, static_cast<uint32_t>(M), static_cast<uint32_t>(K), static_cast<uint32_t>(B),
                static_cast<uint32_t>(K / 32 * 18), n_tile, d_err};
