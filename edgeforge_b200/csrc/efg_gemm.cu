@@ -299,6 +299,7 @@ constexpr uint32_t kRawStages = 3, kOpStages = 2, kMaxTileN2 = 128;
 constexpr uint32_t kOpABytes = 2 * kATileBytes;  // W_hi + W_lo
 
 struct GemmWsParams {
+  CUtensorMap wmap;  // W as [M][rb / 8] u64, box {18, 128}: one raw chunk (256 columns) of a row tile
   const uint8_t* W;
   const uint8_t* Xs;  // split X: [n_tiles][K/64][2][n_tile][128 B]
   float* Y;
@@ -391,7 +392,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  pdl_wait();  // X (split by the previous kernel) and W are ready
+  // W is constant: the raw W producer streams it while the previous kernel finishes; every
+  // other role waits for that kernel (it split X, and Y may be read by earlier kernels)
+  if (warp != 0) pdl_wait();
   const uint32_t tmem = tmem_slot;
   bool ok = true;
 
@@ -406,11 +409,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
         ok = false;
         break;
       }
-      if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], valid_rows * kRawRow);
+      // one 2-D tensor copy per raw chunk: 128 rows x 144 bytes, rows past M zero-filled
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
+        tma_load_2d(raw + rs * kRawBytes, &p.wmap, static_cast<int32_t>((rc0 + rc) * (kRawRow / 8)),
+                    static_cast<int32_t>(m0), &raw_full[rs], pol);
+      }
       __syncwarp();
-      for (uint32_t r = lane; r < valid_rows; r += 32)
-        bulk_g2s(raw + rs * kRawBytes + r * kRawRow, p.W + static_cast<uint64_t>(m0 + r) * p.rb + (rc0 + rc) * kRawRow,
-                 kRawRow, &raw_full[rs], pol);
       issued_raw = rc + 1;
     }
     // copies issued into the ring land before the CTA may exit (bounded; immediate when done)
@@ -610,8 +615,19 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
   const uint32_t raw_total = static_cast<uint32_t>(K / kRawK);
   uint32_t S = std::max<uint32_t>(1, static_cast<uint32_t>(dev->sm_count) / (m_tiles * n_tiles));
   S = std::min<uint32_t>({S, 8u, std::max<uint32_t>(1, raw_total / 2)});
-  GemmWsParams p{W, static_cast<const uint8_t*>(ws), Y, static_cast<uint32_t>(M), static_cast<uint32_t>(K),
-                 static_cast<uint32_t>(B), static_cast<uint32_t>(K / 32 * 18), n_tile, 1, d_err};
+  GemmWsParams p{};
+  if (!encode_u64_rows_map(&p.wmap, W, M, K / 32 * 18, kRawRow / 8, kTileM))
+    return fail(EFG_ECUDA, "gemm: tensor map for a %zu x %zu Q4_0 matrix", M, K);
+  p.W = W;
+  p.Xs = static_cast<const uint8_t*>(ws);
+  p.Y = Y;
+  p.M = static_cast<uint32_t>(M);
+  p.K = static_cast<uint32_t>(K);
+  p.B = static_cast<uint32_t>(B);
+  p.rb = static_cast<uint32_t>(K / 32 * 18);
+  p.n_tile = n_tile;
+  p.S = 1;
+  p.err = d_err;
   for (;; S /= 2) {  // the largest cluster the device can place
     p.S = std::max(S, 1u);
     cudaLaunchConfig_t cfg{};

@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <string>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "efg_status.h"
@@ -36,6 +37,13 @@ bool& q4_mma_flag();
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel, size);
 // later calls are free, so launches can be captured into CUDA graphs.
 int ensure_smem_attr(const void* fn, size_t bytes);
+
+// A 2-D TMA tensor map over `rows` rows of `row_bytes` bytes (16-byte aligned base and row
+// stride) seen as 8-byte elements, with a box of box_elems x box_rows; the box may reach past
+// a row's end or past the last row (zero fill). cuTensorMapEncodeTiled from the driver, looked
+// up once. False when the driver rejects the map.
+bool encode_u64_rows_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_elems,
+                         uint32_t box_rows);
 
 // State of the current device, created on first use (allocates the error word).
 // Returns nullptr and records an error if the device cannot be queried.

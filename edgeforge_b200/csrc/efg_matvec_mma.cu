@@ -118,15 +118,6 @@ __device__ __forceinline__ void locate_rt(const MmaParams& p, uint32_t rt, uint3
   nrows = min(kTileRows, p.jobs[j].rows - r0);
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, uint64_t* bar,
-                                            uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(pol)
-      : "memory");
-}
-
 template <Epi E, bool NORM>
 __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __grid_constant__ MmaParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -458,35 +449,10 @@ bool plan_mma(uint32_t nblk, const DeviceInfo& dev, MmaPlan& pl) {
   return true;
 }
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// cuTensorMapEncodeTiled from the driver, looked up once.
-EncodeTiledFn encode_tiled() {
-  static const EncodeTiledFn fn = [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      f = nullptr;
-    return reinterpret_cast<EncodeTiledFn>(f);
-  }();
-  return fn;
-}
-
 // W (rows x rb bytes, 16-byte aligned) as [rows][rb / 8] u64 with the box {146, 16}; the
 // box may reach past the row (zero fill) and past the last row (zero fill).
 bool encode_w_map(CUtensorMap* m, const uint8_t* W, uint32_t rows, uint32_t rb) {
-  const EncodeTiledFn fn = encode_tiled();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {rb / 8, rows};
-  const cuuint64_t strides[1] = {rb};
-  const cuuint32_t box[2] = {kBoxElems, kTileRows};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(W), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return encode_u64_rows_map(m, W, rows, rb, kBoxElems, kTileRows);
 }
 
 }  // namespace
