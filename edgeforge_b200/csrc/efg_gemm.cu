@@ -113,6 +113,26 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 __device__ __forceinline__ float bf16_lo_f(uint32_t p) { return __uint_as_float(p << 16); }
 __device__ __forceinline__ float bf16_hi_f(uint32_t p) { return __uint_as_float(p & 0xFFFF0000u); }
 
+// Float 2^(23-p) + field for the 4-bit field at bit p of w (p <= 12): the field lands in
+// the mantissa under a fixed exponent, so one LOP3 converts it exactly.
+template <int P>
+__device__ __forceinline__ float q4f(uint32_t w) {
+  return __uint_as_float((w & (0xFu << P)) | (uint32_t(150 - P) << 23));
+}
+// 2^(23-p) + 8: subtracting it leaves the signed code c - 8 exactly.
+template <int P>
+__device__ __forceinline__ constexpr float q4b() {
+  return float((1u << (23 - P)) + 8u);
+}
+
+// Writes element e (compile-time after unrolling) of a uint4.
+__device__ __forceinline__ void set_u4(uint4& v, uint32_t e, uint32_t x) {
+  if (e == 0) v.x = x;
+  else if (e == 1) v.y = x;
+  else if (e == 2) v.z = x;
+  else v.w = x;
+}
+
 // Splits 2 floats into packed (hi, lo) bf16 pairs with v = hi + lo (+ residual).
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
   hi = pack_bf16(a, b);
@@ -482,25 +502,39 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
       uint8_t* st = ops + os * op_stage;
       uint4 hi4[4], lo4[4];
       if (r < valid_rows) {
-        const uint16_t* q = reinterpret_cast<const uint16_t*>(raw + rs * kRawBytes + r * kRawRow + (sub * 2 + blk) * 18);
-        const float d = fp16_to_f32(q[0]);
-        uint32_t qs[4];
+        // The block starts 2 bytes into a 32-bit word when blk is odd (18-byte blocks in a
+        // 144-byte row): read the five aligned words that cover it and funnel-shift out
+        // the four code words.
+        const uint32_t sh = blk * 16;
+        const uint32_t* q =
+            reinterpret_cast<const uint32_t*>(raw + rs * kRawBytes + r * kRawRow + (sub * 2 + blk) * 18 - blk * 2);
+        uint32_t wv[5];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) qs[i] = q[1 + 2 * i] | (static_cast<uint32_t>(q[2 + 2 * i]) << 16);
-        float w[32];
+        for (int i = 0; i < 5; ++i) wv[i] = q[i];
+        const float d = fp16_to_f32(wv[0] >> sh);
+        const float2 dd = make_float2(d, d);
+        const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const uint32_t byte = (qs[j >> 2] >> (8 * (j & 3))) & 0xFFu;
-          w[j] = __fmul_rn(static_cast<float>(static_cast<int>(byte & 15u) - 8), d);
-          w[j + 16] = __fmul_rn(static_cast<float>(static_cast<int>(byte >> 4) - 8), d);
-        }
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t qs = __funnelshift_rc(wv[i], wv[i + 1], sh + 16);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t h[4], l[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) split2(w[8 * c + 2 * e], w[8 * c + 2 * e + 1], h[e], l[e]);
-          hi4[c] = make_uint4(h[0], h[1], h[2], h[3]);
-          lo4[c] = make_uint4(l[0], l[1], l[2], l[3]);
+          for (int h = 0; h < 2; ++h) {
+            // byte 2h / 2h+1 of the code word: low nibbles are columns 4i+2h, 4i+2h+1,
+            // high nibbles the same columns + 16. Each field becomes the exact float
+            // c - 8 through its exponent; (c - 8) * d is exact in binary32.
+            const uint32_t v = h ? (qs >> 16) : qs;
+            const float2 lo_c = __fadd2_rn(make_float2(q4f<0>(v), q4f<8>(v)), make_float2(-q4b<0>(), -q4b<8>()));
+            const float2 hi_c = __fadd2_rn(make_float2(q4f<4>(v), q4f<12>(v)), make_float2(-q4b<4>(), -q4b<12>()));
+            const float2 wl = __fmul2_rn(lo_c, dd), wh = __fmul2_rn(hi_c, dd);
+            const uint32_t e = 2 * (i & 1) + h;
+            uint32_t hl = pack_bf16(wl.x, wl.y), hh = pack_bf16(wh.x, wh.y);
+            const float2 rl = __ffma2_rn(make_float2(bf16_lo_f(hl), bf16_hi_f(hl)), neg1, wl);
+            const float2 rh = __ffma2_rn(make_float2(bf16_lo_f(hh), bf16_hi_f(hh)), neg1, wh);
+            set_u4(hi4[i >> 1], e, hl);
+            set_u4(lo4[i >> 1], e, pack_bf16(rl.x, rl.y));
+            set_u4(hi4[2 + (i >> 1)], e, hh);
+            set_u4(lo4[2 + (i >> 1)], e, pack_bf16(rh.x, rh.y));
+          }
         }
       } else {
 #pragma unroll
