@@ -125,14 +125,6 @@ __device__ __forceinline__ constexpr float q4b() {
   return float((1u << (23 - P)) + 8u);
 }
 
-// Writes element e (compile-time after unrolling) of a uint4.
-__device__ __forceinline__ void set_u4(uint4& v, uint32_t e, uint32_t x) {
-  if (e == 0) v.x = x;
-  else if (e == 1) v.y = x;
-  else if (e == 2) v.z = x;
-  else v.w = x;
-}
-
 // Splits 2 floats into packed (hi, lo) bf16 pairs with v = hi + lo (+ residual).
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
   hi = pack_bf16(a, b);
@@ -298,32 +290,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4_0_kernel(const __grid
 
 // ================================================================ warp-specialised kernel
 //
-// For K a multiple of 256 (every config-3 shape). Roles per CTA (11 warps):
-//   warp 0      streams the CTA's raw W rows, 256 columns (144 bytes) per row and chunk,
-//               into a 3-stage ring with 1-D bulk copies;
+// For K a multiple of 256 (every config-3 shape). The dequantised W operand lives in TMEM,
+// not shared memory: the MMAs read A from tensor memory ("A in TMEM" form of tcgen05.mma),
+// so the dequantising threads write their rows with tcgen05.st (one lane per row, no
+// swizzle, no generic->async proxy fence) and the tensor core reads no A bytes from shared
+// memory. Roles per CTA (11 warps):
+//   warp 0      streams the CTA's raw W rows, 256 columns (144 bytes) per row and chunk, into
+//               a 4-stage ring with one 2-D tensor copy per chunk;
 //   warp 10     streams the B operand tiles: X is split once per call into BF16 hi / lo
-//               parts laid out tile by tile in the swizzled UMMA layout (split_x_kernel),
-//               so each 64-column tile is one contiguous bulk copy;
-//   warps 2..9  dequantize each 64-column sub-chunk of the raw ring into the W_hi / W_lo
-//               operand tiles, then run the epilogue;
-//   warp 1      allocates TMEM and issues the MMAs (one thread), committing each sub-chunk
-//               to the operand stage's "empty" barrier and the last one to "acc_full".
-// Split-K: a cluster of S CTAs along z shares an output tile; each accumulates its share of
-// K, writes the partial tile into its own shared memory, and after a cluster barrier CTA z
-// sums columns z of all S partials through distributed shared memory in rank order (fixed
-// order: the result does not depend on timing).
+//               parts laid out tile by tile in the swizzled UMMA layout (split_x_kernel), hi
+//               rows then lo rows, so one 64-column tile is one contiguous bulk copy and one
+//               MMA operand of 2 N rows;
+//   warps 2..9  dequantize each 64-column sub-chunk: warp w owns TMEM lanes 32 (w % 4) .. +31
+//               (one row each) and half of the sub-chunk's columns (one Q4_0 block), writing
+//               W_hi and W_lo as packed BF16 pairs; then they run the epilogue;
+//   warp 1      allocates TMEM and issues the MMAs (one thread): per 16-wide K step
+//               D[:, 0:2N] += W_hi [X_hi | X_lo] and D[:, 0:2N] += W_lo [X_hi | X_lo], so
+//               D[:, n] collects the X_hi products and D[:, N + n] the X_lo products
+//               (their sum is the FP32 result; W_lo X_lo is below 2^-16 of |w x| and adds
+//               nothing harmful). Each sub-chunk is committed to its stage's "empty"
+//               barrier, the last one to "acc_full".
+// TMEM: the accumulator at columns [0, 2N), the A stages (64 columns: 32 of W_hi pairs, 32
+// of W_lo pairs) from column 128 (N <= 64, six stages) or 256 (N <= 128, four stages).
+// Split-K: a cluster of S CTAs along z shares an output tile and splits its 64-column
+// sub-chunks evenly (a raw chunk at a split boundary is streamed by both CTAs, each using its
+// own sub-chunks); each CTA writes its partial tile into shared memory, and after a cluster
+// barrier CTA z sums its share of the valid columns over all S partials through distributed
+// shared memory in rank order (fixed order: the result does not depend on timing).
 constexpr int kWsWarps = 11;
 constexpr int kWsThreads = kWsWarps * 32;
 constexpr uint32_t kRawK = 256, kRawRow = 144, kRawBytes = kTileM * kRawRow;
-constexpr uint32_t kRawStages = 3, kOpStages = 2, kMaxTileN2 = 128;
-constexpr uint32_t kOpABytes = 2 * kATileBytes;  // W_hi + W_lo
+constexpr uint32_t kRawStages = 4, kMaxAStages = 6, kMaxTileN2 = 128, kMaxSplit = 8;
+constexpr uint32_t kTmemCols = 512;
+constexpr size_t kWsMinSmem = 120 * 1024;  // keeps one CTA per SM (it holds all 512 TMEM columns)
 
 struct GemmWsParams {
   CUtensorMap wmap;  // W as [M][rb / 8] u64, box {18, 128}: one raw chunk (256 columns) of a row tile
-  const uint8_t* W;
   const uint8_t* Xs;  // split X: [n_tiles][K/64][2][n_tile][128 B]
   float* Y;
-  uint32_t M, K, B, rb, n_tile, S;
+  uint32_t M, K, B, n_tile, S, a_stages;
   int* err;
 };
 
@@ -335,13 +340,38 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ float ld_dsmem(uint32_t local_addr, uint32_t rank) {
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t local_addr, uint32_t rank) {
   uint32_t remote;
-  float v;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return remote;
+}
+__device__ __forceinline__ float ld_dsmem(uint32_t remote_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote_addr) : "memory");
   return v;
 }
+
+// D (TMEM) [+]= A (TMEM, one row per lane, K pairs packed per 32-bit column) * B (smem)^T.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane <- 16 registers.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // X [B][K] FP32 -> the B operand tiles: for every n-tile and 64-column chunk, n_tile rows of
 // 128 bytes (8 chunks of 8 BF16), swizzled as the MMA reads them; hi part then lo part.
@@ -372,35 +402,68 @@ __global__ void split_x_kernel(const float* __restrict__ X, uint32_t B, uint32_t
   }
 }
 
+// One Q4_0 block (18 bytes at `blk_ptr - 2 * odd`, `odd` = the block starts 2 bytes into a
+// 32-bit word) -> 16 packed BF16 pairs of W_hi and of W_lo, pair j = columns 2j, 2j + 1.
+// Each code becomes the exact float c - 8 through its exponent field, (c - 8) * d is exact in
+// binary32, w_hi = bf16(w) and w_lo = bf16(w - w_hi) (exact: w has at most 14 significant bits).
+__device__ __forceinline__ void dequant_block_bf16x2(const uint32_t* q, uint32_t odd, uint32_t (&hi)[16],
+                                                     uint32_t (&lo)[16]) {
+  uint32_t wv[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) wv[i] = q[i];
+  const uint32_t sh = odd * 16;
+  const float d = fp16_to_f32(wv[0] >> sh);
+  const float2 dd = make_float2(d, d);
+  const float2 neg1 = make_float2(-1.f, -1.f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t qs = __funnelshift_rc(wv[i], wv[i + 1], sh + 16);  // code bytes 4i .. 4i+3
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      // bytes 2h, 2h+1: low nibbles are columns 4i+2h, 4i+2h+1, high nibbles those + 16
+      const uint32_t v = h ? (qs >> 16) : qs;
+      const float2 lo_c = __fadd2_rn(make_float2(q4f<0>(v), q4f<8>(v)), make_float2(-q4b<0>(), -q4b<8>()));
+      const float2 hi_c = __fadd2_rn(make_float2(q4f<4>(v), q4f<12>(v)), make_float2(-q4b<4>(), -q4b<12>()));
+      const float2 wl = __fmul2_rn(lo_c, dd), wh = __fmul2_rn(hi_c, dd);
+      const uint32_t hl = pack_bf16(wl.x, wl.y), hh = pack_bf16(wh.x, wh.y);
+      const float2 rl = __ffma2_rn(make_float2(bf16_lo_f(hl), bf16_hi_f(hl)), neg1, wl);
+      const float2 rh = __ffma2_rn(make_float2(bf16_lo_f(hh), bf16_hi_f(hh)), neg1, wh);
+      hi[2 * i + h] = hl;
+      lo[2 * i + h] = pack_bf16(rl.x, rl.y);
+      hi[8 + 2 * i + h] = hh;
+      lo[8 + 2 * i + h] = pack_bf16(rh.x, rh.y);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __grid_constant__ GemmWsParams p) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t raw_full[kRawStages], raw_empty[kRawStages], a_full[kOpStages], b_full[kOpStages],
-      op_empty[kOpStages], acc_full;
+  __shared__ uint64_t raw_full[kRawStages], raw_empty[kRawStages], a_full[kMaxAStages], b_full[kMaxAStages],
+      op_empty[kMaxAStages], acc_full;
   __shared__ uint32_t tmem_slot;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t N = p.n_tile, m0 = blockIdx.x * kTileM, n0 = blockIdx.y * N;
   const uint32_t z = p.S > 1 ? cluster_rank() : 0;
-  const uint32_t raw_total = p.K / kRawK;
-  const uint32_t rc0 = static_cast<uint32_t>(static_cast<uint64_t>(raw_total) * z / p.S);
-  const uint32_t rc1 = static_cast<uint32_t>(static_cast<uint64_t>(raw_total) * (z + 1) / p.S);
-  const uint32_t n_raw = rc1 - rc0, n_sub = n_raw * (kRawK / kChunkK);
-  const uint32_t valid_rows = min(static_cast<uint32_t>(kTileM), p.M - m0);
-  const uint32_t b_bytes = N * 128;
-  // 1024-byte aligned: operand stages (A_hi, A_lo, B1, B2) x 2, then the raw ring
+  const uint32_t n_stage = p.a_stages;
+  // this CTA's 64-column sub-chunks [g0, g1) and the raw chunks that hold them
+  const uint32_t sub_total = p.K / kChunkK;
+  const uint32_t g0 = static_cast<uint32_t>(static_cast<uint64_t>(sub_total) * z / p.S);
+  const uint32_t g1 = static_cast<uint32_t>(static_cast<uint64_t>(sub_total) * (z + 1) / p.S);
+  const uint32_t n_sub = g1 - g0;
+  const uint32_t rc_first = g0 / (kRawK / kChunkK);
+  const uint32_t n_raw = n_sub ? (g1 - 1) / (kRawK / kChunkK) - rc_first + 1 : 0;
+  const uint32_t b_bytes = 2 * N * 128;  // X_hi rows then X_lo rows
+  // 1024-byte aligned: the B stages, then the raw ring
   const uint32_t raw_base_addr = smem_addr(smem_raw);
-  uint8_t* base = smem_raw + (((raw_base_addr + 1023u) & ~1023u) - raw_base_addr);
-  uint8_t* ops = base;
-  const uint32_t op_stage = kOpABytes + 2 * b_bytes;
-  uint8_t* raw = ops + kOpStages * op_stage;
-  uint32_t ncols = 32;
-  while (ncols < N) ncols <<= 1;
+  uint8_t* bst = smem_raw + (((raw_base_addr + 1023u) & ~1023u) - raw_base_addr);
+  uint8_t* raw = bst + n_stage * b_bytes;
 
   if (tid == 0) {
     for (uint32_t i = 0; i < kRawStages; ++i) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], 8);
     }
-    for (uint32_t i = 0; i < kOpStages; ++i) {
+    for (uint32_t i = 0; i < n_stage; ++i) {
       mbar_init(&a_full[i], 8);
       mbar_init(&b_full[i], 1);
       mbar_init(&op_empty[i], 1);
@@ -408,7 +471,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
     mbar_init(&acc_full, 1);
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(&tmem_slot, ncols);
+  if (warp == 1) tmem_alloc(&tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -416,6 +479,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
   // other role waits for that kernel (it split X, and Y may be read by earlier kernels)
   if (warp != 0) pdl_wait();
   const uint32_t tmem = tmem_slot;
+  const uint32_t a_col0 = 2 * N <= 128 ? 128u : 256u;
   bool ok = true;
 
   if (warp == 0) {
@@ -432,7 +496,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
       // one 2-D tensor copy per raw chunk: 128 rows x 144 bytes, rows past M zero-filled
       if (lane == 0) {
         mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
-        tma_load_2d(raw + rs * kRawBytes, &p.wmap, static_cast<int32_t>((rc0 + rc) * (kRawRow / 8)),
+        tma_load_2d(raw + rs * kRawBytes, &p.wmap, static_cast<int32_t>((rc_first + rc) * (kRawRow / 8)),
                     static_cast<int32_t>(m0), &raw_full[rs], pol);
       }
       __syncwarp();
@@ -446,42 +510,36 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
   } else if (warp == 10) {
     // ---------------------------------------------------------- B tile producer
     if (lane == 0) {
-      const uint32_t kc_n = p.K / kChunkK;
       const uint64_t keep = l2_evict_last_policy();  // X tiles are read by every M-tile
       uint32_t issued_b = 0;
       for (uint32_t s = 0; s < n_sub && ok; ++s) {
-        const uint32_t os = s % kOpStages;
-        if (s >= kOpStages) ok = mbar_wait(&op_empty[os], ((s / kOpStages) - 1) & 1u, p.err);
+        const uint32_t os = s % n_stage;
+        if (s >= n_stage) ok = mbar_wait(&op_empty[os], ((s / n_stage) - 1) & 1u, p.err);
         if (!ok) break;
-        const uint32_t kc = rc0 * (kRawK / kChunkK) + s;
-        const uint8_t* src = p.Xs + (static_cast<uint64_t>(blockIdx.y) * kc_n + kc) * 2 * b_bytes;
-        mbar_arrive_expect_tx(&b_full[os], 2 * b_bytes);
-        bulk_g2s(ops + os * op_stage + kOpABytes, src, 2 * b_bytes, &b_full[os], keep);
+        const uint8_t* src = p.Xs + (static_cast<uint64_t>(blockIdx.y) * sub_total + g0 + s) * b_bytes;
+        mbar_arrive_expect_tx(&b_full[os], b_bytes);
+        bulk_g2s(bst + os * b_bytes, src, b_bytes, &b_full[os], keep);
         issued_b = s + 1;
       }
-      for (uint32_t q = issued_b > kOpStages ? issued_b - kOpStages : 0; q < issued_b; ++q)
-        mbar_drain(&b_full[q % kOpStages], (q / kOpStages) & 1u, p.err);
+      for (uint32_t q = issued_b > n_stage ? issued_b - n_stage : 0; q < issued_b; ++q)
+        mbar_drain(&b_full[q % n_stage], (q / n_stage) & 1u, p.err);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(kTileM, N);
+      const uint32_t idesc = idesc_bf16(kTileM, 2 * N);
       for (uint32_t s = 0; s < n_sub && ok; ++s) {
-        const uint32_t os = s % kOpStages, par = (s / kOpStages) & 1u;
+        const uint32_t os = s % n_stage, par = (s / n_stage) & 1u;
         ok = mbar_wait(&a_full[os], par, p.err) && mbar_wait(&b_full[os], par, p.err);
         if (!ok) break;
         tc_fence_after();
-        uint8_t* st = ops + os * op_stage;
-        const uint64_t dah = smem_desc_sw128(smem_addr(st)), dal = smem_desc_sw128(smem_addr(st + kATileBytes));
-        const uint64_t db1 = smem_desc_sw128(smem_addr(st + kOpABytes)),
-                       db2 = smem_desc_sw128(smem_addr(st + kOpABytes + b_bytes));
+        const uint32_t a_hi = tmem + a_col0 + os * 64, a_lo = a_hi + 32;
+        const uint64_t db = smem_desc_sw128(smem_addr(bst + os * b_bytes));
 #pragma unroll
         for (uint32_t ks = 0; ks < kChunkK / 16; ++ks) {
-          const uint64_t adv = 2ull * ks;
-          mma_bf16(tmem, dah + adv, db1 + adv, idesc, (s | ks) != 0);
-          mma_bf16(tmem, dah + adv, db2 + adv, idesc, 1);
-          mma_bf16(tmem, dal + adv, db1 + adv, idesc, 1);
+          mma_bf16_ts(tmem, a_hi + 8 * ks, db + 2ull * ks, idesc, (s | ks) != 0);
+          mma_bf16_ts(tmem, a_lo + 8 * ks, db + 2ull * ks, idesc, 1);
         }
         mma_commit(&op_empty[os]);
       }
@@ -490,67 +548,30 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
     __syncwarp();
   } else {
     // ---------------------------------------------------------- dequant (warps 2..9)
-    const uint32_t t = tid - 64, r = t >> 1, blk = t & 1;
+    const uint32_t q = warp & 3u, blk = (warp - 2) >> 2, r = 32 * q + lane;
+    const uint32_t lane_addr = tmem + ((32 * q) << 16) + a_col0 + blk * 16;
     for (uint32_t s = 0; s < n_sub && ok; ++s) {
-      const uint32_t rc = s / 4, sub = s % 4, rs = rc % kRawStages, os = s % kOpStages;
-      if (sub == 0) ok = mbar_wait(&raw_full[rs], (rc / kRawStages) & 1u, p.err);
-      if (ok && s >= kOpStages) ok = mbar_wait(&op_empty[os], ((s / kOpStages) - 1) & 1u, p.err);
+      const uint32_t g = g0 + s, rc = g / (kRawK / kChunkK) - rc_first, sub = g % (kRawK / kChunkK);
+      const uint32_t rs = rc % kRawStages, os = s % n_stage;
+      if (s == 0 || sub == 0) ok = mbar_wait(&raw_full[rs], (rc / kRawStages) & 1u, p.err);
+      if (ok && s >= n_stage) ok = mbar_wait(&op_empty[os], ((s / n_stage) - 1) & 1u, p.err);
       if (!__all_sync(0xFFFFFFFFu, ok)) {
         ok = false;
         break;
       }
-      uint8_t* st = ops + os * op_stage;
-      uint4 hi4[4], lo4[4];
-      if (r < valid_rows) {
-        // The block starts 2 bytes into a 32-bit word when blk is odd (18-byte blocks in a
-        // 144-byte row): read the five aligned words that cover it and funnel-shift out
-        // the four code words.
-        const uint32_t sh = blk * 16;
-        const uint32_t* q =
-            reinterpret_cast<const uint32_t*>(raw + rs * kRawBytes + r * kRawRow + (sub * 2 + blk) * 18 - blk * 2);
-        uint32_t wv[5];
-#pragma unroll
-        for (int i = 0; i < 5; ++i) wv[i] = q[i];
-        const float d = fp16_to_f32(wv[0] >> sh);
-        const float2 dd = make_float2(d, d);
-        const float2 neg1 = make_float2(-1.f, -1.f);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t qs = __funnelshift_rc(wv[i], wv[i + 1], sh + 16);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            // byte 2h / 2h+1 of the code word: low nibbles are columns 4i+2h, 4i+2h+1,
-            // high nibbles the same columns + 16. Each field becomes the exact float
-            // c - 8 through its exponent; (c - 8) * d is exact in binary32.
-            const uint32_t v = h ? (qs >> 16) : qs;
-            const float2 lo_c = __fadd2_rn(make_float2(q4f<0>(v), q4f<8>(v)), make_float2(-q4b<0>(), -q4b<8>()));
-            const float2 hi_c = __fadd2_rn(make_float2(q4f<4>(v), q4f<12>(v)), make_float2(-q4b<4>(), -q4b<12>()));
-            const float2 wl = __fmul2_rn(lo_c, dd), wh = __fmul2_rn(hi_c, dd);
-            const uint32_t e = 2 * (i & 1) + h;
-            uint32_t hl = pack_bf16(wl.x, wl.y), hh = pack_bf16(wh.x, wh.y);
-            const float2 rl = __ffma2_rn(make_float2(bf16_lo_f(hl), bf16_hi_f(hl)), neg1, wl);
-            const float2 rh = __ffma2_rn(make_float2(bf16_lo_f(hh), bf16_hi_f(hh)), neg1, wh);
-            set_u4(hi4[i >> 1], e, hl);
-            set_u4(lo4[i >> 1], e, pack_bf16(rl.x, rl.y));
-            set_u4(hi4[2 + (i >> 1)], e, hh);
-            set_u4(lo4[2 + (i >> 1)], e, pack_bf16(rh.x, rh.y));
-          }
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) hi4[c] = lo4[c] = make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint32_t off = sw128(r, blk * 4 + c);
-        *reinterpret_cast<uint4*>(st + off) = hi4[c];
-        *reinterpret_cast<uint4*>(st + kATileBytes + off) = lo4[c];
-      }
-      fence_proxy_async();
+      tc_fence_after();
+      uint32_t hi[16], lo[16];
+      dequant_block_bf16x2(
+          reinterpret_cast<const uint32_t*>(raw + rs * kRawBytes + r * kRawRow + (sub * 2 + blk) * 18 - blk * 2), blk,
+          hi, lo);
+      tmem_st16(lane_addr + os * 64, hi);
+      tmem_st16(lane_addr + os * 64 + 32, lo);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&a_full[os]);
-        if (sub == 3) mbar_arrive(&raw_empty[rs]);  // every read of this raw chunk is done
+        if (sub == 3 || s + 1 == n_sub) mbar_arrive(&raw_empty[rs]);  // this CTA's reads of the chunk are done
       }
     }
   }
@@ -560,17 +581,21 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
   if (warp >= 2 && warp < 10) ok = mbar_drain(&acc_full, 0, p.err) && ok;
   const int all_ok = __syncthreads_and(ok);
   tc_fence_after();
-  float* part = reinterpret_cast<float*>(ops);  // [N][128] partial tile, reusing the operand stages
+  const uint32_t n_valid = min(N, p.B - n0);
+  float* part = reinterpret_cast<float*>(bst);  // [N][128] partial tile, reusing the B stages
   if (warp >= 2 && warp < 10) {
     const uint32_t q = warp & 3u, half = (warp - 2) >> 2, row = 32 * q + lane;
-    for (uint32_t c0 = half * (N / 2); c0 < (half + 1) * (N / 2); c0 += 8) {
-      float v[8];
+    for (uint32_t c0 = half * (N / 2); c0 < (half + 1) * (N / 2) && c0 < n_valid; c0 += 8) {
+      float v[8], u[8];
       tmem_ld8(tmem + ((32 * q) << 16) + c0, v);
+      tmem_ld8(tmem + ((32 * q) << 16) + N + c0, u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] += u[e];
       if (p.S == 1) {
         if (all_ok && m0 + row < p.M)
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            if (n0 + c0 + e < p.B) p.Y[static_cast<uint64_t>(n0 + c0 + e) * p.M + m0 + row] = v[e];
+            if (c0 + e < n_valid) p.Y[static_cast<uint64_t>(n0 + c0 + e) * p.M + m0 + row] = v[e];
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) part[(c0 + e) * kTileM + row] = v[e];
@@ -579,21 +604,28 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
   }
   if (p.S > 1) {
     cluster_sync();  // every partial tile of the cluster is in shared memory
-    const uint32_t c_lo = static_cast<uint32_t>(static_cast<uint64_t>(N) * z / p.S);
-    const uint32_t c_hi = static_cast<uint32_t>(static_cast<uint64_t>(N) * (z + 1) / p.S);
+    const uint32_t c_lo = static_cast<uint32_t>(static_cast<uint64_t>(n_valid) * z / p.S);
+    const uint32_t c_hi = static_cast<uint32_t>(static_cast<uint64_t>(n_valid) * (z + 1) / p.S);
+    const uint32_t base_addr = smem_addr(part);
     for (uint32_t i = tid; i < (c_hi - c_lo) * kTileM; i += kWsThreads) {
       const uint32_t c = c_lo + i / kTileM, row = i % kTileM;
-      const uint32_t a = smem_addr(part + c * kTileM + row);
-      float acc = 0.f;
-      for (uint32_t q = 0; q < p.S; ++q) acc += ld_dsmem(a, q);
-      if (all_ok && m0 + row < p.M && n0 + c < p.B) p.Y[static_cast<uint64_t>(n0 + c) * p.M + m0 + row] = acc;
+      const uint32_t a = base_addr + (c * kTileM + row) * 4u;
+      float v[kMaxSplit];
+#pragma unroll
+      for (uint32_t rk = 0; rk < kMaxSplit; ++rk)
+        if (rk < p.S) v[rk] = ld_dsmem(dsmem_map(a, rk));  // all loads in flight, then a fixed-order sum
+      float acc = v[0];
+#pragma unroll
+      for (uint32_t rk = 1; rk < kMaxSplit; ++rk)
+        if (rk < p.S) acc += v[rk];
+      if (all_ok && m0 + row < p.M) p.Y[static_cast<uint64_t>(n0 + c) * p.M + m0 + row] = acc;
     }
     cluster_sync();  // peers keep their shared memory until every read is done
   }
   pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, ncols);
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
 // Per-device grow-only workspace for the split X (the only scratch the GEMM needs).
@@ -604,10 +636,19 @@ struct GemmScratch {
 };
 GemmScratch g_gemm_scratch[64];
 
+// Largest number of S-CTA clusters the device keeps resident at once, per (device, S, smem):
+// the split is chosen so that every cluster of a call is resident in one wave.
+struct ClusterFit {
+  std::mutex mu;
+  size_t smem[kMaxSplit + 1] = {};
+  int clusters[kMaxSplit + 1] = {};
+};
+ClusterFit g_cluster_fit[64];
+
 }  // namespace
 
 // The warp-specialised path (K % 256 == 0): split X, then the GEMM with split-K over a
-// cluster of S CTAs sized so that ~one wave covers the SMs.
+// cluster of S CTAs sized so that one wave covers the SMs.
 size_t gemm_ws_bytes(size_t K, size_t B) {
   if (K % kRawK != 0 || B == 0) return 0;
   const size_t n_tile = std::min<size_t>(kMaxTileN2, (B + 15) / 16 * 16);
@@ -644,25 +685,26 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
                                         static_cast<uint8_t*>(ws), n_tiles);
     EFG_TRY_CUDA(cudaGetLastError(), "gemm split launch");
   }
-  const size_t smem = 1024 + kOpStages * (kOpABytes + 2 * static_cast<size_t>(n_tile) * 128) + kRawStages * kRawBytes;
+  const uint32_t a_stages = 2 * n_tile <= 128 ? kMaxAStages : 4u;
+  const size_t smem = std::max(kWsMinSmem, 1024 + a_stages * 2 * static_cast<size_t>(n_tile) * 128 +
+                                               static_cast<size_t>(kRawStages) * kRawBytes);
   if (int st = ensure_smem_attr(reinterpret_cast<const void*>(gemm_q4_0_ws_kernel), smem)) return st;
-  const uint32_t raw_total = static_cast<uint32_t>(K / kRawK);
+  const uint32_t sub_total = static_cast<uint32_t>(K / kChunkK);
   uint32_t S = std::max<uint32_t>(1, static_cast<uint32_t>(dev->sm_count) / (m_tiles * n_tiles));
-  S = std::min<uint32_t>({S, 8u, std::max<uint32_t>(1, raw_total / 2)});
+  S = std::min<uint32_t>({S, kMaxSplit, std::max<uint32_t>(1, sub_total / 4)});
   GemmWsParams p{};
   if (!encode_u64_rows_map(&p.wmap, W, M, K / 32 * 18, kRawRow / 8, kTileM))
     return fail(EFG_ECUDA, "gemm: tensor map for a %zu x %zu Q4_0 matrix", M, K);
-  p.W = W;
   p.Xs = static_cast<const uint8_t*>(ws);
   p.Y = Y;
   p.M = static_cast<uint32_t>(M);
   p.K = static_cast<uint32_t>(K);
   p.B = static_cast<uint32_t>(B);
-  p.rb = static_cast<uint32_t>(K / 32 * 18);
   p.n_tile = n_tile;
-  p.S = 1;
+  p.a_stages = a_stages;
   p.err = d_err;
-  for (;; S /= 2) {  // the largest cluster the device can place
+  ClusterFit& fit = g_cluster_fit[dev->device];
+  for (;; --S) {  // the largest split whose clusters are all resident at once
     p.S = std::max(S, 1u);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(m_tiles, n_tiles, p.S);
@@ -680,10 +722,20 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
     cfg.numAttrs = 2;
     if (p.S > 1) {
       int clusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&clusters, gemm_q4_0_ws_kernel, &cfg) != cudaSuccess || clusters < 1) {
-        cudaGetLastError();
-        continue;
+      {
+        std::lock_guard<std::mutex> g(fit.mu);
+        if (fit.smem[p.S] == smem) {
+          clusters = fit.clusters[p.S];
+        } else {
+          if (cudaOccupancyMaxActiveClusters(&clusters, gemm_q4_0_ws_kernel, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            clusters = 0;
+          }
+          fit.smem[p.S] = smem;
+          fit.clusters[p.S] = clusters;
+        }
       }
+      if (clusters < static_cast<int>(m_tiles * n_tiles)) continue;
     }
     EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, gemm_q4_0_ws_kernel, p), "gemm launch");
     return EFG_OK;
