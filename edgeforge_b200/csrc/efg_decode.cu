@@ -497,8 +497,6 @@ struct Decoder {
   float *xb = nullptr, *hb = nullptr, *qb = nullptr, *cb = nullptr, *ob = nullptr, *gb = nullptr, *ub = nullptr,
         *ab = nullptr, *kt = nullptr, *vt = nullptr;
   size_t pb_rows = 0;
-  void* gemm_ws = nullptr;  // the GEMM's split-X workspace for pb_rows rows (stable for graphs)
-  size_t gemm_ws_cap = 0;
   // sequence slots for multi-sequence steps (efg_decoder_set_slots); slot 0 is kc / vc and
   // `cached`, the cache of forward / prefill / generate
   size_t n_slots = 1;
@@ -900,7 +898,6 @@ void destroy(Decoder* D) {
   if (D->g_full) cudaGraphExecDestroy(D->g_full);
   if (D->g_prefill) cudaGraphExecDestroy(D->g_prefill);
   if (D->pb) cudaFree(D->pb);
-  if (D->gemm_ws) cudaFree(D->gemm_ws);
   drop_step_graphs(*D);
   free_slots(*D);
   for (void* p : {static_cast<void*>(D->d_slot_k), static_cast<void*>(D->d_slot_v), static_cast<void*>(D->d_rows),
@@ -1074,15 +1071,13 @@ int ensure_prefill_buffers(Decoder& D) {
   for (float** b : {&D.xb, &D.hb, &D.qb, &D.cb, &D.ob}) *b = reinterpret_cast<float*>(a + o), o += al(P * Dm);
   for (float** b : {&D.gb, &D.ub, &D.ab}) *b = reinterpret_cast<float*>(a + o), o += al(P * F);
   for (float** b : {&D.kt, &D.vt}) *b = reinterpret_cast<float*>(a + o), o += al(P * kvd);
-  D.gemm_ws_cap = gemm_ws_bytes(static_cast<size_t>(std::max(D.c.hidden, D.c.intermediate)), P);
-  if (D.gemm_ws_cap) EFG_TRY_CUDA(cudaMalloc(&D.gemm_ws, D.gemm_ws_cap), "gemm workspace allocation");
   D.pb_rows = P;
   return EFG_OK;
 }
 
 // Y[b] = M . X[b] for b < n (X [n][M.cols], Y [n][M.rows]).
 int batched_proj(Decoder& D, const Mat& M, const float* X, float* Y, size_t n, cudaStream_t s) {
-  if (M.type == 4) return launch_gemm_q4_0(Y, M.w, X, M.rows, M.cols, n, D.d_err, s, D.gemm_ws, D.gemm_ws_cap);
+  if (M.type == 4) return launch_gemm_q4_0(Y, M.w, X, M.rows, M.cols, n, D.d_err, s);
   for (size_t b = 0; b < n; ++b) {
     MatvecArgs a;
     a.fmt = Fmt::Q8;

@@ -133,6 +133,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps until it
+// completes (or `ns` pass) instead of returning at once, so waiting warps leave the issue
+// slots and pipes to the warps that work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for warp-specialised kernels with many waiting warps: same bound and error
+// behaviour, each poll sleeps up to 2 us on the barrier.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
+    if ((i & 7u) == 7u) {
+      if (error_raised(err)) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        record_error(err, EFG_ETIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- 1-D bulk copy (TMA)
 // L2 policy for data read exactly once (weights streamed by a matvec).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {

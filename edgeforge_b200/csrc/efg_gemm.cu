@@ -294,16 +294,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4_0_kernel(const __grid
 // not shared memory: the MMAs read A from tensor memory ("A in TMEM" form of tcgen05.mma),
 // so the dequantising threads write their rows with tcgen05.st (one lane per row, no
 // swizzle, no generic->async proxy fence) and the tensor core reads no A bytes from shared
-// memory. Roles per CTA (11 warps):
+// memory. Roles per CTA (22 warps):
 //   warp 0      streams the CTA's raw W rows, 256 columns (144 bytes) per row and chunk, into
 //               a 4-stage ring with one 2-D tensor copy per chunk;
-//   warp 10     streams the B operand tiles: X is split once per call into BF16 hi / lo
-//               parts laid out tile by tile in the swizzled UMMA layout (split_x_kernel), hi
-//               rows then lo rows, so one 64-column tile is one contiguous bulk copy and one
-//               MMA operand of 2 N rows;
-//   warps 2..9  dequantize each 64-column sub-chunk: warp w owns TMEM lanes 32 (w % 4) .. +31
-//               (one row each) and half of the sub-chunk's columns (one Q4_0 block), writing
-//               W_hi and W_lo as packed BF16 pairs; then they run the epilogue;
+//   warps 18..21 fill the B operand stages, hi rows then lo rows of the swizzled UMMA layout,
+//               so one stage is one MMA operand of 2 N rows. For N <= 64 they build the tiles
+//               from X (read the tile's N rows of FP32, split every value into BF16 hi / lo
+//               parts): no separate kernel and no workspace. For wider tiles that work would be
+//               repeated by every row tile, so X is split once per call by split_x_kernel into
+//               a per-device scratch laid out tile by tile, and each warp bulk-copies a quarter
+//               of the stage;
+//   warps 2..17 dequantize the 64-column sub-chunks in two groups of 8 (warps 2..9 the even
+//               sub-chunks, 10..17 the odd ones, so one group's waits overlap the other's
+//               arithmetic): warp w owns TMEM lanes 32 (w % 4) .. +31 (one row each) and half
+//               of the sub-chunk's columns (one Q4_0 block), writing W_hi and W_lo as packed
+//               BF16 pairs; warps 2..9 then run the epilogue;
 //   warp 1      allocates TMEM and issues the MMAs (one thread): per 16-wide K step
 //               D[:, 0:2N] += W_hi [X_hi | X_lo] and D[:, 0:2N] += W_lo [X_hi | X_lo], so
 //               D[:, n] collects the X_hi products and D[:, N + n] the X_lo products
@@ -317,7 +322,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4_0_kernel(const __grid
 // own sub-chunks); each CTA writes its partial tile into shared memory, and after a cluster
 // barrier CTA z sums its share of the valid columns over all S partials through distributed
 // shared memory in rank order (fixed order: the result does not depend on timing).
-constexpr int kWsWarps = 11;
+constexpr int kWsWarps = 22;
+constexpr uint32_t kDequantWarps = 16, kBWarp0 = 18, kBWarps = 4;
 constexpr int kWsThreads = kWsWarps * 32;
 constexpr uint32_t kRawK = 256, kRawRow = 144, kRawBytes = kTileM * kRawRow;
 constexpr uint32_t kRawStages = 4, kMaxAStages = 6, kMaxTileN2 = 128, kMaxSplit = 8;
@@ -326,7 +332,8 @@ constexpr size_t kWsMinSmem = 120 * 1024;  // keeps one CTA per SM (it holds all
 
 struct GemmWsParams {
   CUtensorMap wmap;  // W as [M][rb / 8] u64, box {18, 128}: one raw chunk (256 columns) of a row tile
-  const uint8_t* Xs;  // split X: [n_tiles][K/64][2][n_tile][128 B]
+  const float* X;    // [B][K], 16-byte aligned
+  const uint8_t* Xs;  // null, or X split by split_x_kernel: [n_tiles][K/64][2][n_tile][128 B]
   float* Y;
   uint32_t M, K, B, n_tile, S, a_stages;
   int* err;
@@ -461,11 +468,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
   if (tid == 0) {
     for (uint32_t i = 0; i < kRawStages; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 8);
+      mbar_init(&raw_empty[i], kDequantWarps);
     }
     for (uint32_t i = 0; i < n_stage; ++i) {
       mbar_init(&a_full[i], 8);
-      mbar_init(&b_full[i], 1);
+      mbar_init(&b_full[i], kBWarps);
       mbar_init(&op_empty[i], 1);
     }
     mbar_init(&acc_full, 1);
@@ -475,9 +482,12 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // W is constant: the raw W producer streams it while the previous kernel finishes; every
-  // other role waits for that kernel (it split X, and Y may be read by earlier kernels)
-  if (warp != 0) pdl_wait();
+  // W is constant: the raw W producer, the dequantising warps and the MMA issuer start while
+  // the previous kernel (the X split) finishes. Only the B producer reads that kernel's
+  // output, so only it waits for the grid dependency; every MMA waits for its B tile and the
+  // epilogue for every MMA, so Y is written after all earlier kernels (which may read Y)
+  // have completed.
+  if (warp >= kBWarp0) pdl_wait();
   const uint32_t tmem = tmem_slot;
   const uint32_t a_col0 = 2 * N <= 128 ? 128u : 256u;
   bool ok = true;
@@ -488,7 +498,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
     uint32_t issued_raw = 0;
     for (uint32_t rc = 0; rc < n_raw && ok; ++rc) {
       const uint32_t rs = rc % kRawStages;
-      if (rc >= kRawStages) ok = mbar_wait(&raw_empty[rs], ((rc / kRawStages) - 1) & 1u, p.err);
+      if (rc >= kRawStages) ok = mbar_wait_idle(&raw_empty[rs], ((rc / kRawStages) - 1) & 1u, p.err);
       if (!__all_sync(0xFFFFFFFFu, ok)) {
         ok = false;
         break;
@@ -507,23 +517,57 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
       for (uint32_t q = issued_raw > kRawStages ? issued_raw - kRawStages : 0; q < issued_raw; ++q)
         mbar_drain(&raw_full[q % kRawStages], (q / kRawStages) & 1u, p.err);
     __syncwarp();
-  } else if (warp == 10) {
-    // ---------------------------------------------------------- B tile producer
-    if (lane == 0) {
-      const uint64_t keep = l2_evict_last_policy();  // X tiles are read by every M-tile
-      uint32_t issued_b = 0;
-      for (uint32_t s = 0; s < n_sub && ok; ++s) {
-        const uint32_t os = s % n_stage;
-        if (s >= n_stage) ok = mbar_wait(&op_empty[os], ((s / n_stage) - 1) & 1u, p.err);
-        if (!ok) break;
-        const uint8_t* src = p.Xs + (static_cast<uint64_t>(blockIdx.y) * sub_total + g0 + s) * b_bytes;
-        mbar_arrive_expect_tx(&b_full[os], b_bytes);
-        bulk_g2s(bst + os * b_bytes, src, b_bytes, &b_full[os], keep);
-        issued_b = s + 1;
+  } else if (warp >= kBWarp0) {
+    // ---------------------------------------------------------- B tile builders (X split)
+    // item i of a sub-chunk: row n = i / 8 of the n-tile, 8 columns starting at 8 (i % 8);
+    // eight consecutive threads cover one row (32-byte loads, conflict-free 16-byte stores)
+    const uint32_t bt = tid - kBWarp0 * 32, n_items = N * 8, quarter = b_bytes / kBWarps;
+    const uint64_t keep = l2_evict_last_policy();  // the split X is read by every row tile
+    uint32_t issued = 0;
+    for (uint32_t s = 0; s < n_sub && ok; ++s) {
+      const uint32_t os = s % n_stage;
+      if (s >= n_stage) ok = mbar_wait_idle(&op_empty[os], ((s / n_stage) - 1) & 1u, p.err);
+      if (!__all_sync(0xFFFFFFFFu, ok)) {
+        ok = false;
+        break;
       }
-      for (uint32_t q = issued_b > n_stage ? issued_b - n_stage : 0; q < issued_b; ++q)
-        mbar_drain(&b_full[q % n_stage], (q / n_stage) & 1u, p.err);
+      uint8_t* st = bst + os * b_bytes;
+      if (p.Xs) {
+        if (lane == 0) {
+          const uint32_t part = warp - kBWarp0;
+          const uint8_t* src = p.Xs + (static_cast<uint64_t>(blockIdx.y) * sub_total + g0 + s) * b_bytes;
+          mbar_arrive_expect_tx(&b_full[os], quarter);
+          bulk_g2s(st + part * quarter, src + part * quarter, quarter, &b_full[os], keep);
+        }
+        __syncwarp();
+        issued = s + 1;
+        continue;
+      }
+      const uint32_t k0 = (g0 + s) * kChunkK;
+      for (uint32_t i = bt; i < n_items; i += kBWarps * 32) {
+        const uint32_t n = i >> 3, c = i & 7u;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+        if (n0 + n < p.B) {
+          const float4* src = reinterpret_cast<const float4*>(p.X + static_cast<uint64_t>(n0 + n) * p.K + k0 + 8 * c);
+          a = __ldg(src);
+          b = __ldg(src + 1);
+        }
+        uint32_t h[4], l[4];
+        split2(a.x, a.y, h[0], l[0]);
+        split2(a.z, a.w, h[1], l[1]);
+        split2(b.x, b.y, h[2], l[2]);
+        split2(b.z, b.w, h[3], l[3]);
+        *reinterpret_cast<uint4*>(st + sw128(n, c)) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(st + sw128(N + n, c)) = make_uint4(l[0], l[1], l[2], l[3]);
+      }
+      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b_full[os]);
     }
+    // bulk copies issued into the stages land before the CTA may exit (bounded)
+    if (p.Xs && lane == 0)
+      for (uint32_t q = issued > n_stage ? issued - n_stage : 0; q < issued; ++q)
+        mbar_drain(&b_full[q % n_stage], (q / n_stage) & 1u, p.err);
     __syncwarp();
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
@@ -531,7 +575,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
       const uint32_t idesc = idesc_bf16(kTileM, 2 * N);
       for (uint32_t s = 0; s < n_sub && ok; ++s) {
         const uint32_t os = s % n_stage, par = (s / n_stage) & 1u;
-        ok = mbar_wait(&a_full[os], par, p.err) && mbar_wait(&b_full[os], par, p.err);
+        ok = mbar_wait_idle(&a_full[os], par, p.err) && mbar_wait_idle(&b_full[os], par, p.err);
         if (!ok) break;
         tc_fence_after();
         const uint32_t a_hi = tmem + a_col0 + os * 64, a_lo = a_hi + 32;
@@ -547,31 +591,36 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
     }
     __syncwarp();
   } else {
-    // ---------------------------------------------------------- dequant (warps 2..9)
-    const uint32_t q = warp & 3u, blk = (warp - 2) >> 2, r = 32 * q + lane;
+    // ---------------------------------------------------------- dequant (warps 2..17)
+    // Every warp walks every sub-chunk so that each raw chunk is waited for and released by
+    // all 16 warps in order; a warp dequantizes only its group's sub-chunks.
+    const uint32_t grp = (warp - 2) >> 3, q = warp & 3u, blk = ((warp - 2) >> 2) & 1u, r = 32 * q + lane;
     const uint32_t lane_addr = tmem + ((32 * q) << 16) + a_col0 + blk * 16;
     for (uint32_t s = 0; s < n_sub && ok; ++s) {
       const uint32_t g = g0 + s, rc = g / (kRawK / kChunkK) - rc_first, sub = g % (kRawK / kChunkK);
       const uint32_t rs = rc % kRawStages, os = s % n_stage;
-      if (s == 0 || sub == 0) ok = mbar_wait(&raw_full[rs], (rc / kRawStages) & 1u, p.err);
-      if (ok && s >= n_stage) ok = mbar_wait(&op_empty[os], ((s / n_stage) - 1) & 1u, p.err);
+      const bool mine = (s & 1u) == grp;
+      if (s == 0 || sub == 0) ok = mbar_wait_idle(&raw_full[rs], (rc / kRawStages) & 1u, p.err);
+      if (mine && ok && s >= n_stage) ok = mbar_wait_idle(&op_empty[os], ((s / n_stage) - 1) & 1u, p.err);
       if (!__all_sync(0xFFFFFFFFu, ok)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      uint32_t hi[16], lo[16];
-      dequant_block_bf16x2(
-          reinterpret_cast<const uint32_t*>(raw + rs * kRawBytes + r * kRawRow + (sub * 2 + blk) * 18 - blk * 2), blk,
-          hi, lo);
-      tmem_st16(lane_addr + os * 64, hi);
-      tmem_st16(lane_addr + os * 64 + 32, lo);
-      tmem_wait_st();
-      tc_fence_before();
+      if (mine) {
+        tc_fence_after();
+        uint32_t hi[16], lo[16];
+        dequant_block_bf16x2(
+            reinterpret_cast<const uint32_t*>(raw + rs * kRawBytes + r * kRawRow + (sub * 2 + blk) * 18 - blk * 2),
+            blk, hi, lo);
+        tmem_st16(lane_addr + os * 64, hi);
+        tmem_st16(lane_addr + os * 64 + 32, lo);
+        tmem_wait_st();
+        tc_fence_before();
+      }
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&a_full[os]);
-        if (sub == 3 || s + 1 == n_sub) mbar_arrive(&raw_empty[rs]);  // this CTA's reads of the chunk are done
+        if (mine) mbar_arrive(&a_full[os]);
+        if (sub == 3 || s + 1 == n_sub) mbar_arrive(&raw_empty[rs]);  // this warp is done with the chunk
       }
     }
   }
@@ -628,7 +677,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-// Per-device grow-only workspace for the split X (the only scratch the GEMM needs).
+// Per-device grow-only scratch for the split X of wide tiles (N > 64).
 struct GemmScratch {
   std::mutex mu;
   void* p = nullptr;
@@ -647,28 +696,21 @@ ClusterFit g_cluster_fit[64];
 
 }  // namespace
 
-// The warp-specialised path (K % 256 == 0): split X, then the GEMM with split-K over a
-// cluster of S CTAs sized so that one wave covers the SMs.
-size_t gemm_ws_bytes(size_t K, size_t B) {
-  if (K % kRawK != 0 || B == 0) return 0;
-  const size_t n_tile = std::min<size_t>(kMaxTileN2, (B + 15) / 16 * 16);
-  return (B + n_tile - 1) / n_tile * (K / kChunkK) * 2 * n_tile * 128;
-}
-
+// The warp-specialised path (K % 256 == 0): one kernel, split-K over a cluster of S CTAs
+// sized so that one wave covers the SMs.
 int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
-                   cudaStream_t s, void* ws, size_t ws_cap) {
+                   cudaStream_t s) {
   DeviceInfo* dev = current_device();
   if (!dev) return EFG_ECUDA;
   const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN2, (B + 15) / 16 * 16));
   const uint32_t n_tiles = static_cast<uint32_t>((B + n_tile - 1) / n_tile);
   const uint32_t m_tiles = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
-  const size_t ws_bytes = gemm_ws_bytes(K, B);
-  GemmScratch& gs = g_gemm_scratch[dev->device];
-  std::unique_lock<std::mutex> lk(gs.mu, std::defer_lock);
-  if (ws) {  // the caller's workspace (stable for CUDA graphs, not shared with other callers)
-    if (ws_cap < ws_bytes) return fail(EFG_EINVAL, "gemm: workspace of %zu bytes, %zu needed", ws_cap, ws_bytes);
-  } else {
-    lk.lock();
+  const uint8_t* Xs = nullptr;
+  std::unique_lock<std::mutex> lk;
+  if (n_tile > 64) {  // split X once per call (see the kernel's role notes)
+    GemmScratch& gs = g_gemm_scratch[dev->device];
+    lk = std::unique_lock<std::mutex>(gs.mu);
+    const size_t ws_bytes = static_cast<size_t>(n_tiles) * (K / kChunkK) * 2 * n_tile * 128;
     if (ws_bytes > gs.cap) {
       if (gs.p) cudaFree(gs.p);
       gs.p = nullptr;
@@ -676,14 +718,12 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
       EFG_TRY_CUDA(cudaMalloc(&gs.p, ws_bytes), "gemm workspace");
       gs.cap = ws_bytes;
     }
-    ws = gs.p;
-  }
-  {
     const uint64_t items = static_cast<uint64_t>(n_tiles) * (K / kChunkK) * n_tile * 8;
     const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((items + 255) / 256, 8ull * dev->sm_count));
     split_x_kernel<<<grid, 256, 0, s>>>(X, static_cast<uint32_t>(B), static_cast<uint32_t>(K), n_tile,
-                                        static_cast<uint8_t*>(ws), n_tiles);
+                                        static_cast<uint8_t*>(gs.p), n_tiles);
     EFG_TRY_CUDA(cudaGetLastError(), "gemm split launch");
+    Xs = static_cast<const uint8_t*>(gs.p);
   }
   const uint32_t a_stages = 2 * n_tile <= 128 ? kMaxAStages : 4u;
   const size_t smem = std::max(kWsMinSmem, 1024 + a_stages * 2 * static_cast<size_t>(n_tile) * 128 +
@@ -695,7 +735,8 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
   GemmWsParams p{};
   if (!encode_u64_rows_map(&p.wmap, W, M, K / 32 * 18, kRawRow / 8, kTileM))
     return fail(EFG_ECUDA, "gemm: tensor map for a %zu x %zu Q4_0 matrix", M, K);
-  p.Xs = static_cast<const uint8_t*>(ws);
+  p.X = X;
+  p.Xs = Xs;
   p.Y = Y;
   p.M = static_cast<uint32_t>(M);
   p.K = static_cast<uint32_t>(K);
@@ -743,7 +784,7 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
 }
 
 int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
-                     cudaStream_t s, void* ws, size_t ws_cap) {
+                     cudaStream_t s) {
   if (K % 32 != 0) return fail(EFG_EINVAL, "Q4_0 needs a row length divisible by 32, got %zu", K);
   if (M == 0 || B == 0) return EFG_OK;
   if (!Y || (K && (!W || !X))) return fail(EFG_EINVAL, "gemm: null pointer");
@@ -756,7 +797,7 @@ int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
       reinterpret_cast<uintptr_t>(Y) % 4 != 0)
     return fail(EFG_EINVAL, "gemm: X must be 16-byte aligned, W 2-byte aligned and Y 4-byte aligned");
   if (K % kRawK == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0)
-    return launch_gemm_ws(Y, W, X, M, K, B, d_err, s, ws, ws_cap);
+    return launch_gemm_ws(Y, W, X, M, K, B, d_err, s);
   const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN, (B + 15) / 16 * 16));
   GemmParams p{W, X, Y, static_cast<uint32_t>(M), static_cast<uint32_t>(K), static_cast<uint32_t>(B),
                static_cast<uint32_t>(K / 32 * 18), n_tile, d_err};
