@@ -18,6 +18,7 @@ from .api import (  # noqa: F401
     dot_q8_0,
     efq_check,
     gemm_q4_0,
+    gemm_q8_0,
     host_dequantize_row,
     host_matvec,
     host_matvec_static,

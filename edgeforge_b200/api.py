@@ -214,6 +214,12 @@ def gemm_q4_0(Y, W, X, M: int, K: int, B: int) -> None:
     check(load().efg_gemm_q4_0(_ptr(Y), _ptr(W), _ptr(X), M, K, B, _stream()))
 
 
+def gemm_q8_0(Y, W, X, M: int, K: int, B: int) -> None:
+    """gemm_q4_0 for Q8_0 weights (K a multiple of 256): each column equals
+    ef::kern::matvec_q8_0 of that column within 1e-5 of sum|w x|."""
+    check(load().efg_gemm_q8_0(_ptr(Y), _ptr(W), _ptr(X), M, K, B, _stream()))
+
+
 # ---------------------------------------------------------------- row-sharded matvec
 
 

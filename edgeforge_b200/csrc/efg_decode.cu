@@ -1075,9 +1075,17 @@ int ensure_prefill_buffers(Decoder& D) {
   return EFG_OK;
 }
 
+// Whether the tensor-core GEMM takes a Q8_0 matrix (rows of a multiple of 256 columns,
+// 16-byte aligned operands); otherwise the rows go through the matvec one by one.
+bool gemm_q8_ok(const Mat& M, const float* X) {
+  return M.type == 3 && M.cols % 256 == 0 && reinterpret_cast<uintptr_t>(M.w) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(X) % 16 == 0;
+}
+
 // Y[b] = M . X[b] for b < n (X [n][M.cols], Y [n][M.rows]).
 int batched_proj(Decoder& D, const Mat& M, const float* X, float* Y, size_t n, cudaStream_t s) {
   if (M.type == 4) return launch_gemm_q4_0(Y, M.w, X, M.rows, M.cols, n, D.d_err, s);
+  if (gemm_q8_ok(M, X)) return launch_gemm_q8_0(Y, M.w, X, M.rows, M.cols, n, D.d_err, s);
   for (size_t b = 0; b < n; ++b) {
     MatvecArgs a;
     a.fmt = Fmt::Q8;
@@ -1173,8 +1181,16 @@ int batch_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s, boo
     }
   }
   if (multi) {
-    for (size_t b = 0; b < n; ++b)
-      if (int st = enqueue_lm_head(D, D.xb + b * Dm, s, D.d_lb + b * V)) return st;
+    if (D.lm_head.type == 4 || gemm_q8_ok(D.lm_head, D.hb)) {  // final norm of every row, one GEMM
+      cudaLaunchConfig_t cn = cfg_of(dim3(nb), dim3(256), 0, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cn, rmsnorm_rows_kernel, D.hb, static_cast<const float*>(D.xb), D.final_norm,
+                                      Dm, eps),
+                   "rmsnorm launch");
+      if (int st = batched_proj(D, D.lm_head, D.hb, D.d_lb, n, s)) return st;
+    } else {
+      for (size_t b = 0; b < n; ++b)
+        if (int st = enqueue_lm_head(D, D.xb + b * Dm, s, D.d_lb + b * V)) return st;
+    }
     cudaLaunchConfig_t cf = cfg_of(dim3(nb), dim3(1024), 0, s, attr);
     EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, argmax_rows_kernel, static_cast<const float*>(D.d_lb), V, D.d_next),
                  "argmax launch");

@@ -30,6 +30,7 @@
 
 #include "../../include/efg.h"
 #include "efg_device.cuh"
+#include "efg_dot.cuh"
 #include "efg_gemm.cuh"
 #include "efg_host.h"
 
@@ -112,18 +113,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 
 __device__ __forceinline__ float bf16_lo_f(uint32_t p) { return __uint_as_float(p << 16); }
 __device__ __forceinline__ float bf16_hi_f(uint32_t p) { return __uint_as_float(p & 0xFFFF0000u); }
-
-// Float 2^(23-p) + field for the 4-bit field at bit p of w (p <= 12): the field lands in
-// the mantissa under a fixed exponent, so one LOP3 converts it exactly.
-template <int P>
-__device__ __forceinline__ float q4f(uint32_t w) {
-  return __uint_as_float((w & (0xFu << P)) | (uint32_t(150 - P) << 23));
-}
-// 2^(23-p) + 8: subtracting it leaves the signed code c - 8 exactly.
-template <int P>
-__device__ __forceinline__ constexpr float q4b() {
-  return float((1u << (23 - P)) + 8u);
-}
 
 // Splits 2 floats into packed (hi, lo) bf16 pairs with v = hi + lo (+ residual).
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
@@ -325,13 +314,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4_0_kernel(const __grid
 constexpr int kWsWarps = 22;
 constexpr uint32_t kDequantWarps = 16, kBWarp0 = 18, kBWarps = 4;
 constexpr int kWsThreads = kWsWarps * 32;
-constexpr uint32_t kRawK = 256, kRawRow = 144, kRawBytes = kTileM * kRawRow;
-constexpr uint32_t kRawStages = 4, kMaxAStages = 6, kMaxTileN2 = 128, kMaxSplit = 8;
+constexpr uint32_t kRawK = 256, kMaxRawStages = 4, kMaxAStages = 6, kMaxTileN2 = 128, kMaxSplit = 8;
+
+// Per weight format: bytes of one 32-column block, of one raw chunk row (256 columns), the
+// raw ring depth, and how many exact BF16 terms a dequantised weight needs (Q4_0: (c - 8) d
+// has at most 14 significant bits, two terms; Q8_0: q d has at most 18, three terms).
+template <int kQ>
+struct WsFormat;
+template <>
+struct WsFormat<4> {
+  static constexpr uint32_t kBlock = 18, kRawRow = 144, kRawStages = 4, kTerms = 2;
+};
+template <>
+struct WsFormat<8> {
+  static constexpr uint32_t kBlock = 34, kRawRow = 272, kRawStages = 3, kTerms = 3;
+};
 constexpr uint32_t kTmemCols = 512;
 constexpr size_t kWsMinSmem = 120 * 1024;  // keeps one CTA per SM (it holds all 512 TMEM columns)
 
 struct GemmWsParams {
-  CUtensorMap wmap;  // W as [M][rb / 8] u64, box {18, 128}: one raw chunk (256 columns) of a row tile
+  CUtensorMap wmap;  // W as [M][row bytes / 8] u64, box {raw chunk row / 8, 128}: one raw chunk of a row tile
   const float* X;    // [B][K], 16-byte aligned
   const uint8_t* Xs;  // null, or X split by split_x_kernel: [n_tiles][K/64][2][n_tile][128 B]
   float* Y;
@@ -429,8 +431,8 @@ __device__ __forceinline__ void dequant_block_bf16x2(const uint32_t* q, uint32_t
     for (int h = 0; h < 2; ++h) {
       // bytes 2h, 2h+1: low nibbles are columns 4i+2h, 4i+2h+1, high nibbles those + 16
       const uint32_t v = h ? (qs >> 16) : qs;
-      const float2 lo_c = __fadd2_rn(make_float2(q4f<0>(v), q4f<8>(v)), make_float2(-q4b<0>(), -q4b<8>()));
-      const float2 hi_c = __fadd2_rn(make_float2(q4f<4>(v), q4f<12>(v)), make_float2(-q4b<4>(), -q4b<12>()));
+      const float2 lo_c = __fadd2_rn(make_float2(q4_field<0>(v), q4_field<8>(v)), make_float2(-q4_bias<0>(), -q4_bias<8>()));
+      const float2 hi_c = __fadd2_rn(make_float2(q4_field<4>(v), q4_field<12>(v)), make_float2(-q4_bias<4>(), -q4_bias<12>()));
       const float2 wl = __fmul2_rn(lo_c, dd), wh = __fmul2_rn(hi_c, dd);
       const uint32_t hl = pack_bf16(wl.x, wl.y), hh = pack_bf16(wh.x, wh.y);
       const float2 rl = __ffma2_rn(make_float2(bf16_lo_f(hl), bf16_hi_f(hl)), neg1, wl);
@@ -443,9 +445,45 @@ __device__ __forceinline__ void dequant_block_bf16x2(const uint32_t* q, uint32_t
   }
 }
 
-__global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __grid_constant__ GemmWsParams p) {
+// One Q8_0 block (34 bytes, same addressing as dequant_block_bf16x2) -> 16 packed BF16 pairs
+// of each of three terms t0 + t1 + t2 = w exactly: q becomes the exact float through its
+// exponent field, w = q d is exact in binary32 (at most 18 significant bits), t0 = bf16(w),
+// t1 = bf16(w - t0) and t2 = w - t0 - t1 (at most 3 significant bits left, exact in BF16).
+__device__ __forceinline__ void dequant_q8_block_bf16x3(const uint32_t* q, uint32_t odd, uint32_t (&t0)[16],
+                                                        uint32_t (&t1)[16], uint32_t (&t2)[16]) {
+  uint32_t wv[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) wv[i] = q[i];
+  const uint32_t sh = odd * 16;
+  const float d = fp16_to_f32(wv[0] >> sh);
+  const float2 dd = make_float2(d, d);
+  const float2 neg1 = make_float2(-1.f, -1.f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t qs = __funnelshift_rc(wv[i], wv[i + 1], sh + 16);  // code bytes 4i .. 4i+3
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t v = h ? (qs >> 16) : qs;  // columns 4i+2h, 4i+2h+1
+      const float2 c = __fadd2_rn(make_float2(q8_field<0>(v), q8_field<8>(v)), make_float2(-q8_bias<0>(), -q8_bias<8>()));
+      const float2 w = __fmul2_rn(c, dd);
+      const uint32_t a = pack_bf16(w.x, w.y);
+      const float2 r1 = __ffma2_rn(make_float2(bf16_lo_f(a), bf16_hi_f(a)), neg1, w);
+      const uint32_t b = pack_bf16(r1.x, r1.y);
+      const float2 r2 = __ffma2_rn(make_float2(bf16_lo_f(b), bf16_hi_f(b)), neg1, r1);
+      t0[2 * i + h] = a;
+      t1[2 * i + h] = b;
+      t2[2 * i + h] = pack_bf16(r2.x, r2.y);
+    }
+  }
+}
+
+template <int kQ>
+__global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_constant__ GemmWsParams p) {
+  using F = WsFormat<kQ>;
+  constexpr uint32_t kRawRow = F::kRawRow, kRawBytes = kTileM * F::kRawRow, kRawStages = F::kRawStages;
+  constexpr uint32_t kStageCols = 32 * F::kTerms;  // TMEM columns of one A stage
   extern __shared__ uint8_t smem_raw[];
-  __shared__ uint64_t raw_full[kRawStages], raw_empty[kRawStages], a_full[kMaxAStages], b_full[kMaxAStages],
+  __shared__ uint64_t raw_full[kMaxRawStages], raw_empty[kMaxRawStages], a_full[kMaxAStages], b_full[kMaxAStages],
       op_empty[kMaxAStages], acc_full;
   __shared__ uint32_t tmem_slot;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -578,13 +616,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
         ok = mbar_wait_idle(&a_full[os], par, p.err) && mbar_wait_idle(&b_full[os], par, p.err);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t a_hi = tmem + a_col0 + os * 64, a_lo = a_hi + 32;
+        const uint32_t a0 = tmem + a_col0 + os * kStageCols;
         const uint64_t db = smem_desc_sw128(smem_addr(bst + os * b_bytes));
 #pragma unroll
-        for (uint32_t ks = 0; ks < kChunkK / 16; ++ks) {
-          mma_bf16_ts(tmem, a_hi + 8 * ks, db + 2ull * ks, idesc, (s | ks) != 0);
-          mma_bf16_ts(tmem, a_lo + 8 * ks, db + 2ull * ks, idesc, 1);
-        }
+        for (uint32_t ks = 0; ks < kChunkK / 16; ++ks)
+#pragma unroll
+          for (uint32_t t = 0; t < F::kTerms; ++t)
+            mma_bf16_ts(tmem, a0 + 32 * t + 8 * ks, db + 2ull * ks, idesc, (s | ks | t) != 0);
         mma_commit(&op_empty[os]);
       }
       mma_commit(&acc_full);  // after every MMA issued (or none)
@@ -608,12 +646,23 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_q4_0_ws_kernel(const __gri
       }
       if (mine) {
         tc_fence_after();
-        uint32_t hi[16], lo[16];
-        dequant_block_bf16x2(
-            reinterpret_cast<const uint32_t*>(raw + rs * kRawBytes + r * kRawRow + (sub * 2 + blk) * 18 - blk * 2),
-            blk, hi, lo);
-        tmem_st16(lane_addr + os * 64, hi);
-        tmem_st16(lane_addr + os * 64 + 32, lo);
+        // the block starts 2 bytes into a 32-bit word when blk is odd (18- and 34-byte
+        // blocks in rows of a multiple of 4 bytes): read from the aligned word below it
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(raw + rs * kRawBytes + r * kRawRow +
+                                                                (sub * 2 + blk) * F::kBlock - blk * 2);
+        const uint32_t ta = lane_addr + os * kStageCols;
+        if constexpr (kQ == 4) {
+          uint32_t hi[16], lo[16];
+          dequant_block_bf16x2(src, blk, hi, lo);
+          tmem_st16(ta, hi);
+          tmem_st16(ta + 32, lo);
+        } else {
+          uint32_t t0[16], t1[16], t2[16];
+          dequant_q8_block_bf16x3(src, blk, t0, t1, t2);
+          tmem_st16(ta, t0);
+          tmem_st16(ta + 32, t1);
+          tmem_st16(ta + 64, t2);
+        }
         tmem_wait_st();
         tc_fence_before();
       }
@@ -692,14 +741,16 @@ struct ClusterFit {
   size_t smem[kMaxSplit + 1] = {};
   int clusters[kMaxSplit + 1] = {};
 };
-ClusterFit g_cluster_fit[64];
+ClusterFit g_cluster_fit[64][2];  // [device][Q4_0, Q8_0]
 
 }  // namespace
 
 // The warp-specialised path (K % 256 == 0): one kernel, split-K over a cluster of S CTAs
 // sized so that one wave covers the SMs.
+template <int kQ>
 int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
                    cudaStream_t s) {
+  using F = WsFormat<kQ>;
   DeviceInfo* dev = current_device();
   if (!dev) return EFG_ECUDA;
   const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN2, (B + 15) / 16 * 16));
@@ -725,16 +776,19 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
     EFG_TRY_CUDA(cudaGetLastError(), "gemm split launch");
     Xs = static_cast<const uint8_t*>(gs.p);
   }
-  const uint32_t a_stages = 2 * n_tile <= 128 ? kMaxAStages : 4u;
+  // TMEM: the accumulator below column 128 or 256, then as many A stages as fit
+  const uint32_t a_col0 = 2 * n_tile <= 128 ? 128u : 256u;
+  const uint32_t a_stages = std::min<uint32_t>(kMaxAStages, (kTmemCols - a_col0) / (32 * F::kTerms));
   const size_t smem = std::max(kWsMinSmem, 1024 + a_stages * 2 * static_cast<size_t>(n_tile) * 128 +
-                                               static_cast<size_t>(kRawStages) * kRawBytes);
-  if (int st = ensure_smem_attr(reinterpret_cast<const void*>(gemm_q4_0_ws_kernel), smem)) return st;
+                                               static_cast<size_t>(F::kRawStages) * kTileM * F::kRawRow);
+  auto* kernel = gemm_ws_kernel<kQ>;
+  if (int st = ensure_smem_attr(reinterpret_cast<const void*>(kernel), smem)) return st;
   const uint32_t sub_total = static_cast<uint32_t>(K / kChunkK);
   uint32_t S = std::max<uint32_t>(1, static_cast<uint32_t>(dev->sm_count) / (m_tiles * n_tiles));
   S = std::min<uint32_t>({S, kMaxSplit, std::max<uint32_t>(1, sub_total / 4)});
   GemmWsParams p{};
-  if (!encode_u64_rows_map(&p.wmap, W, M, K / 32 * 18, kRawRow / 8, kTileM))
-    return fail(EFG_ECUDA, "gemm: tensor map for a %zu x %zu Q4_0 matrix", M, K);
+  if (!encode_u64_rows_map(&p.wmap, W, M, K / 32 * F::kBlock, F::kRawRow / 8, kTileM))
+    return fail(EFG_ECUDA, "gemm: tensor map for a %zu x %zu Q%d_0 matrix", M, K, kQ);
   p.X = X;
   p.Xs = Xs;
   p.Y = Y;
@@ -744,7 +798,7 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
   p.n_tile = n_tile;
   p.a_stages = a_stages;
   p.err = d_err;
-  ClusterFit& fit = g_cluster_fit[dev->device];
+  ClusterFit& fit = g_cluster_fit[dev->device][kQ == 8];
   for (;; --S) {  // the largest split whose clusters are all resident at once
     p.S = std::max(S, 1u);
     cudaLaunchConfig_t cfg{};
@@ -768,7 +822,7 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
         if (fit.smem[p.S] == smem) {
           clusters = fit.clusters[p.S];
         } else {
-          if (cudaOccupancyMaxActiveClusters(&clusters, gemm_q4_0_ws_kernel, &cfg) != cudaSuccess) {
+          if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
             cudaGetLastError();
             clusters = 0;
           }
@@ -778,7 +832,7 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
       }
       if (clusters < static_cast<int>(m_tiles * n_tiles)) continue;
     }
-    EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, gemm_q4_0_ws_kernel, p), "gemm launch");
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, kernel, p), "gemm launch");
     return EFG_OK;
   }
 }
@@ -797,7 +851,7 @@ int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
       reinterpret_cast<uintptr_t>(Y) % 4 != 0)
     return fail(EFG_EINVAL, "gemm: X must be 16-byte aligned, W 2-byte aligned and Y 4-byte aligned");
   if (K % kRawK == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0)
-    return launch_gemm_ws(Y, W, X, M, K, B, d_err, s);
+    return launch_gemm_ws<4>(Y, W, X, M, K, B, d_err, s);
   const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN, (B + 15) / 16 * 16));
   GemmParams p{W, X, Y, static_cast<uint32_t>(M), static_cast<uint32_t>(K), static_cast<uint32_t>(B),
                static_cast<uint32_t>(K / 32 * 18), n_tile, d_err};
@@ -817,6 +871,23 @@ int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
   return EFG_OK;
 }
 
+int launch_gemm_q8_0(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
+                     cudaStream_t s) {
+  if (K % kRawK != 0)
+    return fail(EFG_EINVAL, "the Q8_0 GEMM needs a row length divisible by %u, got %zu", kRawK, K);
+  if (M == 0 || B == 0) return EFG_OK;
+  if (!Y || (K && (!W || !X))) return fail(EFG_EINVAL, "gemm: null pointer");
+  if (M >= (1u << 31) || K >= (1u << 30) || B >= (1u << 20)) return fail(EFG_EINVAL, "gemm: shape too large");
+  if (K == 0) {
+    EFG_TRY_CUDA(cudaMemsetAsync(Y, 0, M * B * sizeof(float), s), "gemm zero fill");
+    return EFG_OK;
+  }
+  if (reinterpret_cast<uintptr_t>(X) % 16 != 0 || reinterpret_cast<uintptr_t>(W) % 16 != 0 ||
+      reinterpret_cast<uintptr_t>(Y) % 4 != 0)
+    return fail(EFG_EINVAL, "gemm: X and W must be 16-byte aligned and Y 4-byte aligned");
+  return launch_gemm_ws<8>(Y, W, X, M, K, B, d_err, s);
+}
+
 }  // namespace efg
 
 extern "C" int efg_gemm_q4_0(float* d_Y, const uint8_t* d_W, const float* d_X, size_t M, size_t K, size_t B,
@@ -824,4 +895,11 @@ extern "C" int efg_gemm_q4_0(float* d_Y, const uint8_t* d_W, const float* d_X, s
   efg::DeviceInfo* dev = efg::current_device();
   if (!dev) return EFG_ECUDA;
   return efg::launch_gemm_q4_0(d_Y, d_W, d_X, M, K, B, dev->d_err, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int efg_gemm_q8_0(float* d_Y, const uint8_t* d_W, const float* d_X, size_t M, size_t K, size_t B,
+                             void* stream) {
+  efg::DeviceInfo* dev = efg::current_device();
+  if (!dev) return EFG_ECUDA;
+  return efg::launch_gemm_q8_0(d_Y, d_W, d_X, M, K, B, dev->d_err, static_cast<cudaStream_t>(stream));
 }

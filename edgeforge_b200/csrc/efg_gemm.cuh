@@ -14,5 +14,8 @@ namespace efg {
 // may outlive a larger call). Returns an EFG_* status.
 int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
                      cudaStream_t s);
+// The same product for Q8_0 weights (K a multiple of 256, W and X 16-byte aligned).
+int launch_gemm_q8_0(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
+                     cudaStream_t s);
 
 }  // namespace efg

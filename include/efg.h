@@ -182,6 +182,11 @@ int efg_host_matvec_static(int qtype, float* y, const uint8_t* W, const float* x
  * within 1e-5 of sum|w x|. */
 int efg_gemm_q4_0(float* d_Y, const uint8_t* d_W, const float* d_X, size_t M, size_t K, size_t B, void* stream);
 
+/* The same product for Q8_0 weights: W dequantized to an exact sum of three BF16 terms (a
+ * Q8_0 weight q d has up to 18 significant bits), K a multiple of 256, W and X 16-byte
+ * aligned. Replaces B calls of ef::kern::matvec_q8_0 (qkernels.h:63-64) with one launch. */
+int efg_gemm_q8_0(float* d_Y, const uint8_t* d_W, const float* d_X, size_t M, size_t K, size_t B, void* stream);
+
 /* ================================================================ row-sharded matvec (several GPUs) */
 
 /* A communicator between the GPUs of one node, one rank per GPU and process (or thread).

@@ -14,18 +14,18 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-5
 
 
-def _weights(torch, M, K, seed):
+def _weights(torch, M, K, seed, qt=QType.Q4_0):
     g = torch.Generator(device="cuda").manual_seed(seed)
-    W = torch.empty(M * (K // 32) * 18, dtype=torch.uint8, device="cuda")
+    W = torch.empty(M * (K // 32) * (18 if qt == QType.Q4_0 else 34), dtype=torch.uint8, device="cuda")
     if M * K:
         X = torch.randn(M, K, generator=g, device="cuda") * 0.02
-        efg.quantize_rows(QType.Q4_0, X, M, K, W, True)
+        efg.quantize_rows(qt, X, M, K, W, True)
     return W
 
 
-def _exact(oracle, W, X, K):
+def _exact(oracle, W, X, K, qt=QType.Q4_0):
     """(exact, sum|w x|) for every (column, row), in float64."""
-    Wd = oracle.dequantize_rows(QType.Q4_0, W.cpu().numpy(), K).astype(np.float64)
+    Wd = oracle.dequantize_rows(qt, W.cpu().numpy(), K).astype(np.float64)
     Xd = X.cpu().numpy().astype(np.float64)
     return Xd @ Wd.T, np.abs(Xd) @ np.abs(Wd).T
 
@@ -91,4 +91,47 @@ def test_edges_and_errors(cuda):
     Xbig = torch.randn(4 * 64 + 1, device="cuda")
     with pytest.raises(efg.EdgeForgeError, match="aligned"):
         efg.gemm_q4_0(Y, W, Xbig[1:], 64, 64, 4)
+    assert efg.device_error() == 0
+
+
+@pytest.mark.parametrize("M,K", [(5632, 2048), (2048, 5632), (32000, 2048), (1000, 768)])
+@pytest.mark.parametrize("B", [1, 23, 64, 200])
+def test_q8_0_shapes(cuda, oracle, M, K, B):
+    """efg_gemm_q8_0: three exact BF16 terms per weight; every column within 1e-5 of the
+    exact dot and of the per-column Q8_0 matvec (the lm_head and the Q8_0 projections)."""
+    import torch
+
+    W = _weights(torch, M, K, 6, QType.Q8_0)
+    X = torch.randn(B, K, generator=torch.Generator(device="cuda").manual_seed(7), device="cuda") * 2
+    Y = torch.full((B, M), float("nan"), device="cuda")
+    efg.gemm_q8_0(Y, W, X, M, K, B)
+    torch.cuda.synchronize()
+    exact, mag = _exact(oracle, W, X, K, QType.Q8_0)
+    err = np.abs(Y.cpu().numpy().astype(np.float64) - exact) / mag
+    assert err.max() <= TOL, err.max()
+    y = torch.empty(M, device="cuda")
+    for b in {0, B - 1}:
+        efg.matvec_q8_0(y, W, X[b].contiguous(), M, K)
+        torch.cuda.synchronize()
+        diff = np.abs(y.cpu().numpy().astype(np.float64) - Y[b].cpu().numpy())
+        assert (diff / mag[b]).max() <= 2 * TOL
+    Y2 = torch.empty_like(Y)
+    efg.gemm_q8_0(Y2, W, X, M, K, B)
+    torch.cuda.synchronize()
+    assert torch.equal(Y, Y2)
+    assert efg.device_error() == 0
+
+
+def test_q8_0_errors(cuda):
+    import torch
+
+    W = _weights(torch, 64, 512, 8, QType.Q8_0)
+    X = torch.randn(4, 512, device="cuda")
+    Y = torch.empty(4, 64, device="cuda")
+    with pytest.raises(efg.EdgeForgeError, match="divisible by 256"):
+        efg.gemm_q8_0(Y, W, X, 64, 480, 4)
+    Xbig = torch.randn(4 * 512 + 1, device="cuda")
+    with pytest.raises(efg.EdgeForgeError, match="aligned"):
+        efg.gemm_q8_0(Y, W, Xbig[1:], 64, 512, 4)
+    efg.gemm_q8_0(Y, W, X, 0, 512, 4)  # nothing to do
     assert efg.device_error() == 0
