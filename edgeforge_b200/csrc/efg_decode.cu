@@ -371,8 +371,7 @@ __global__ void swiglu_kernel(float* __restrict__ out, const float* __restrict__
   pdl_wait();
   pdl_launch_dependents();
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const float gv = g[i];
-    out[i] = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), u[i]);
+    out[i] = swiglu_value(g[i], u[i]);
   }
 }
 
@@ -1099,6 +1098,37 @@ int batched_proj(Decoder& D, const Mat& M, const float* X, float* Y, size_t n, c
   return EFG_OK;
 }
 
+// Whether a matrix goes through launch_gemm (fused launches): Q4_0 or Q8_0, rows of a
+// multiple of 256 columns, 16-byte aligned (the batch buffers are).
+bool gemm_fusable(const Mat& M) {
+  return (M.type == 4 || M.type == 3) && M.cols % 256 == 0 && reinterpret_cast<uintptr_t>(M.w) % 16 == 0;
+}
+
+// Y_i = M_i . X for up to three matrices sharing X: those of one weight type that the GEMM
+// takes go out as one launch per type, the others through batched_proj.
+int project_group(Decoder& D, const Mat* const* mats, float* const* outs, int count, const float* X, size_t n,
+                  cudaStream_t s) {
+  bool done[3] = {false, false, false};
+  for (int qt : {4, 3}) {
+    GemmCall c;
+    c.qtype = qt == 4 ? 4 : 8;
+    c.X = X;
+    c.K = mats[0]->cols;
+    c.B = n;
+    for (int i = 0; i < count; ++i)
+      if (mats[i]->type == qt && mats[i]->cols == c.K && gemm_fusable(*mats[i])) {
+        c.jobs[c.n_jobs++] = GemmJob{mats[i]->w, outs[i], mats[i]->rows};
+        done[i] = true;
+      }
+    if (c.n_jobs)
+      if (int st = launch_gemm(c, D.d_err, s)) return st;
+  }
+  for (int i = 0; i < count; ++i)
+    if (!done[i])
+      if (int st = batched_proj(D, *mats[i], X, outs[i], n, s)) return st;
+  return EFG_OK;
+}
+
 // n <= pb_rows rows through every layer. Prefill (multi = false): tokens tokens()[p0..p0+n)
 // of slot 0 at positions p0..; with `logits`, the last token's logits in D.logits.
 // Multi-sequence step (multi = true): row b is d_rows' (token, slot, position); every
@@ -1129,17 +1159,17 @@ int batch_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s, boo
                                     eps),
                  "rmsnorm launch");
     const uint64_t layer_off = static_cast<uint64_t>(l) * D.max_seq * kvd;
-    if (int st = batched_proj(D, Ly.q, D.hb, D.qb, n, s)) return st;
-    if (!multi) {
-      if (int st = batched_proj(D, Ly.k, D.hb, kl + p0 * kvd, n, s)) return st;  // unrotated keys, rotated below
-      if (int st = batched_proj(D, Ly.v, D.hb, vl + p0 * kvd, n, s)) return st;
+    {  // q, k and v in as few launches as the weight types allow
+      const Mat* mats[3] = {&Ly.q, &Ly.k, &Ly.v};
+      float* outs[3] = {D.qb, multi ? D.kt : kl + p0 * kvd, multi ? D.vt : vl + p0 * kvd};
+      if (int st = project_group(D, mats, outs, 3, D.hb, n, s)) return st;
+    }
+    if (!multi) {  // the k projection wrote unrotated keys into the cache rows: rotate them
       cudaLaunchConfig_t cf = cfg_of(dim3(nb), dim3(128), 0, s, attr);
       EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rope_keys_kernel, kl, static_cast<const float*>(D.rcos),
                                       static_cast<const float*>(D.rsin), static_cast<int>(p0), KV, hd),
                    "rope launch");
     } else {  // each row's key and value into its own slot's cache
-      if (int st = batched_proj(D, Ly.k, D.hb, D.kt, n, s)) return st;
-      if (int st = batched_proj(D, Ly.v, D.hb, D.vt, n, s)) return st;
       cudaLaunchConfig_t cf = cfg_of(dim3(nb), dim3(128), 0, s, attr);
       EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, store_kv_rows_kernel, static_cast<const float*>(D.kt),
                                       static_cast<const float*>(D.vt), static_cast<const uint64_t*>(D.d_slot_k),
@@ -1158,8 +1188,18 @@ int batch_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s, boo
                                       layer_off),
                    "attention launch");
     }
-    if (int st = batched_proj(D, Ly.o, D.cb, D.ob, n, s)) return st;
-    {
+    if (gemm_fusable(Ly.o)) {  // o projection with the residual add in its epilogue
+      GemmCall c;
+      c.qtype = Ly.o.type == 4 ? 4 : 8;
+      c.jobs[0] = GemmJob{Ly.o.w, D.xb, Ly.o.rows};
+      c.n_jobs = 1;
+      c.X = D.cb;
+      c.K = Ly.o.cols;
+      c.B = n;
+      c.accumulate = true;
+      if (int st = launch_gemm(c, D.d_err, s)) return st;
+    } else {
+      if (int st = batched_proj(D, Ly.o, D.cb, D.ob, n, s)) return st;
       cudaLaunchConfig_t cf = cfg_of(grid_for(n * Dm), dim3(256), 0, s, attr);
       EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, add_kernel, D.xb, static_cast<const float*>(D.ob), n * Dm), "add launch");
     }
@@ -1174,10 +1214,20 @@ int batch_pass(Decoder& D, size_t p0, size_t n, bool logits, cudaStream_t s, boo
                                       static_cast<const float*>(D.ub), static_cast<uint32_t>(n * F)),
                    "swiglu launch");
     }
-    if (int st = batched_proj(D, Ly.down, D.ab, D.ob, n, s)) return st;
-    {
-      cudaLaunchConfig_t cf = cfg_of(grid_for(n * Dm), dim3(256), 0, s, attr);
-      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, add_kernel, D.xb, static_cast<const float*>(D.ob), n * Dm), "add launch");
+    if (gemm_fusable(Ly.down)) {  // down projection with the residual add in its epilogue
+      GemmCall c;
+      c.qtype = Ly.down.type == 4 ? 4 : 8;
+      c.jobs[0] = GemmJob{Ly.down.w, D.xb, Ly.down.rows};
+      c.n_jobs = 1;
+      c.X = D.ab;
+      c.K = Ly.down.cols;
+      c.B = n;
+      c.accumulate = true;
+      if (int st = launch_gemm(c, D.d_err, s)) return st;
+    } else {
+      if (int st = batched_proj(D, Ly.down, D.ab, D.ob, n, s)) return st;
+      cudaLaunchConfig_t ca = cfg_of(grid_for(n * Dm), dim3(256), 0, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&ca, add_kernel, D.xb, static_cast<const float*>(D.ob), n * Dm), "add launch");
     }
   }
   if (multi) {

@@ -485,10 +485,10 @@ __device__ __noinline__ uint32_t mv_job(const Params& p, const Job& J, const MvS
 // division are not repeated in the phase's code.
 __device__ __noinline__ float4 swiglu4(float4 g, float4 u) {
   float4 r;
-  r.x = __fmul_rn(__fdiv_rn(g.x, __fadd_rn(1.0f, expf(-g.x))), u.x);
-  r.y = __fmul_rn(__fdiv_rn(g.y, __fadd_rn(1.0f, expf(-g.y))), u.y);
-  r.z = __fmul_rn(__fdiv_rn(g.z, __fadd_rn(1.0f, expf(-g.z))), u.z);
-  r.w = __fmul_rn(__fdiv_rn(g.w, __fadd_rn(1.0f, expf(-g.w))), u.w);
+  r.x = swiglu_value(g.x, u.x);
+  r.y = swiglu_value(g.y, u.y);
+  r.z = swiglu_value(g.z, u.z);
+  r.w = swiglu_value(g.w, u.w);
   return r;
 }
 

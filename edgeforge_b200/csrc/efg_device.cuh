@@ -166,6 +166,12 @@ __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, i
   }
 }
 
+// SwiGLU element silu(g) * u of the reference (src/kernels.cpp:94-99), every rounding explicit
+// so that the per-token, persistent and batched kernels that apply it give the same bits.
+__device__ __forceinline__ float swiglu_value(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
 // ---------------------------------------------------------------- 1-D bulk copy (TMA)
 // L2 policy for data read exactly once (weights streamed by a matvec).
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {

@@ -314,6 +314,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4_0_kernel(const __grid
 constexpr int kWsWarps = 22;
 constexpr uint32_t kDequantWarps = 16, kBWarp0 = 18, kBWarps = 4;
 constexpr int kWsThreads = kWsWarps * 32;
+constexpr uint32_t kMaxGemmJobs = 3;
 constexpr uint32_t kRawK = 256, kMaxRawStages = 4, kMaxAStages = 6, kMaxTileN2 = 128, kMaxSplit = 8;
 
 // Per weight format: bytes of one 32-column block, of one raw chunk row (256 columns), the
@@ -332,12 +333,19 @@ struct WsFormat<8> {
 constexpr uint32_t kTmemCols = 512;
 constexpr size_t kWsMinSmem = 120 * 1024;  // keeps one CTA per SM (it holds all 512 TMEM columns)
 
-struct GemmWsParams {
+// One matrix of a launch: the CTAs with blockIdx.x in [tile0, next job's tile0) compute its
+// 128-row tiles; every job shares K and the B operand.
+struct alignas(64) GemmJobDev {
   CUtensorMap wmap;  // W as [M][row bytes / 8] u64, box {raw chunk row / 8, 128}: one raw chunk of a row tile
-  const float* X;    // [B][K], 16-byte aligned
-  const uint8_t* Xs;  // null, or X split by split_x_kernel: [n_tiles][K/64][2][n_tile][128 B]
-  float* Y;
-  uint32_t M, K, B, n_tile, S, a_stages;
+  float* Y;          // [B][M]
+  uint32_t M, tile0;
+};
+
+struct GemmWsParams {
+  GemmJobDev jobs[kMaxGemmJobs];
+  const float* X;     // [B][K], 16-byte aligned
+  const uint8_t* Xs;  // null, or the B operand split by split_x_kernel: [n_tiles][K/64][2][n_tile][128 B]
+  uint32_t n_jobs, K, B, n_tile, S, a_stages, accumulate;  // accumulate: Y += product
   int* err;
 };
 
@@ -487,7 +495,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
       op_empty[kMaxAStages], acc_full;
   __shared__ uint32_t tmem_slot;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t N = p.n_tile, m0 = blockIdx.x * kTileM, n0 = blockIdx.y * N;
+  uint32_t j = 0;
+  while (j + 1 < p.n_jobs && blockIdx.x >= p.jobs[j + 1].tile0) ++j;
+  const GemmJobDev& job = p.jobs[j];
+  const uint32_t N = p.n_tile, m0 = (blockIdx.x - job.tile0) * kTileM, n0 = blockIdx.y * N, M = job.M;
+  float* const Y = job.Y;
   const uint32_t z = p.S > 1 ? cluster_rank() : 0;
   const uint32_t n_stage = p.a_stages;
   // this CTA's 64-column sub-chunks [g0, g1) and the raw chunks that hold them
@@ -544,7 +556,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
       // one 2-D tensor copy per raw chunk: 128 rows x 144 bytes, rows past M zero-filled
       if (lane == 0) {
         mbar_arrive_expect_tx(&raw_full[rs], kRawBytes);
-        tma_load_2d(raw + rs * kRawBytes, &p.wmap, static_cast<int32_t>((rc_first + rc) * (kRawRow / 8)),
+        tma_load_2d(raw + rs * kRawBytes, &job.wmap, static_cast<int32_t>((rc_first + rc) * (kRawRow / 8)),
                     static_cast<int32_t>(m0), &raw_full[rs], pol);
       }
       __syncwarp();
@@ -586,9 +598,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
         const uint32_t n = i >> 3, c = i & 7u;
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
         if (n0 + n < p.B) {
-          const float4* src = reinterpret_cast<const float4*>(p.X + static_cast<uint64_t>(n0 + n) * p.K + k0 + 8 * c);
-          a = __ldg(src);
-          b = __ldg(src + 1);
+          const uint64_t o = static_cast<uint64_t>(n0 + n) * p.K + k0 + 8 * c;
+          a = __ldg(reinterpret_cast<const float4*>(p.X + o));
+          b = __ldg(reinterpret_cast<const float4*>(p.X + o) + 1);
         }
         uint32_t h[4], l[4];
         split2(a.x, a.y, h[0], l[0]);
@@ -690,10 +702,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[e] += u[e];
       if (p.S == 1) {
-        if (all_ok && m0 + row < p.M)
+        if (all_ok && m0 + row < M)
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            if (c0 + e < n_valid) p.Y[static_cast<uint64_t>(n0 + c0 + e) * p.M + m0 + row] = v[e];
+            if (c0 + e < n_valid) {
+              float* y = Y + static_cast<uint64_t>(n0 + c0 + e) * M + m0 + row;
+              *y = p.accumulate ? __fadd_rn(*y, v[e]) : v[e];
+            }
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) part[(c0 + e) * kTileM + row] = v[e];
@@ -716,7 +731,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
 #pragma unroll
       for (uint32_t rk = 1; rk < kMaxSplit; ++rk)
         if (rk < p.S) acc += v[rk];
-      if (all_ok && m0 + row < p.M) p.Y[static_cast<uint64_t>(n0 + c) * p.M + m0 + row] = acc;
+      if (all_ok && m0 + row < M) {
+        float* y = Y + static_cast<uint64_t>(n0 + c) * M + m0 + row;
+        *y = p.accumulate ? __fadd_rn(*y, acc) : acc;
+      }
     }
     cluster_sync();  // peers keep their shared memory until every read is done
   }
@@ -748,14 +766,25 @@ ClusterFit g_cluster_fit[64][2];  // [device][Q4_0, Q8_0]
 // The warp-specialised path (K % 256 == 0): one kernel, split-K over a cluster of S CTAs
 // sized so that one wave covers the SMs.
 template <int kQ>
-int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
-                   cudaStream_t s) {
+int launch_gemm_ws(const GemmCall& c, int* d_err, cudaStream_t s) {
   using F = WsFormat<kQ>;
   DeviceInfo* dev = current_device();
   if (!dev) return EFG_ECUDA;
+  const size_t K = c.K, B = c.B;
   const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN2, (B + 15) / 16 * 16));
   const uint32_t n_tiles = static_cast<uint32_t>((B + n_tile - 1) / n_tile);
-  const uint32_t m_tiles = static_cast<uint32_t>((M + kTileM - 1) / kTileM);
+  GemmWsParams p{};
+  uint32_t m_tiles = 0;
+  for (int j = 0; j < c.n_jobs; ++j) {
+    const GemmJob& jb = c.jobs[j];
+    GemmJobDev& jd = p.jobs[j];
+    if (!encode_u64_rows_map(&jd.wmap, jb.W, jb.M, K / 32 * F::kBlock, F::kRawRow / 8, kTileM))
+      return fail(EFG_ECUDA, "gemm: tensor map for a %zu x %zu Q%d_0 matrix", jb.M, K, kQ);
+    jd.Y = jb.Y;
+    jd.M = static_cast<uint32_t>(jb.M);
+    jd.tile0 = m_tiles;
+    m_tiles += static_cast<uint32_t>((jb.M + kTileM - 1) / kTileM);
+  }
   const uint8_t* Xs = nullptr;
   std::unique_lock<std::mutex> lk;
   if (n_tile > 64) {  // split X once per call (see the kernel's role notes)
@@ -771,7 +800,7 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
     }
     const uint64_t items = static_cast<uint64_t>(n_tiles) * (K / kChunkK) * n_tile * 8;
     const unsigned grid = static_cast<unsigned>(std::min<uint64_t>((items + 255) / 256, 8ull * dev->sm_count));
-    split_x_kernel<<<grid, 256, 0, s>>>(X, static_cast<uint32_t>(B), static_cast<uint32_t>(K), n_tile,
+    split_x_kernel<<<grid, 256, 0, s>>>(c.X, static_cast<uint32_t>(B), static_cast<uint32_t>(K), n_tile,
                                         static_cast<uint8_t*>(gs.p), n_tiles);
     EFG_TRY_CUDA(cudaGetLastError(), "gemm split launch");
     Xs = static_cast<const uint8_t*>(gs.p);
@@ -786,13 +815,10 @@ int launch_gemm_ws(float* Y, const uint8_t* W, const float* X, size_t M, size_t 
   const uint32_t sub_total = static_cast<uint32_t>(K / kChunkK);
   uint32_t S = std::max<uint32_t>(1, static_cast<uint32_t>(dev->sm_count) / (m_tiles * n_tiles));
   S = std::min<uint32_t>({S, kMaxSplit, std::max<uint32_t>(1, sub_total / 4)});
-  GemmWsParams p{};
-  if (!encode_u64_rows_map(&p.wmap, W, M, K / 32 * F::kBlock, F::kRawRow / 8, kTileM))
-    return fail(EFG_ECUDA, "gemm: tensor map for a %zu x %zu Q%d_0 matrix", M, K, kQ);
-  p.X = X;
+  p.n_jobs = static_cast<uint32_t>(c.n_jobs);
+  p.X = c.X;
   p.Xs = Xs;
-  p.Y = Y;
-  p.M = static_cast<uint32_t>(M);
+  p.accumulate = c.accumulate ? 1u : 0u;
   p.K = static_cast<uint32_t>(K);
   p.B = static_cast<uint32_t>(B);
   p.n_tile = n_tile;
@@ -850,8 +876,16 @@ int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
   if (reinterpret_cast<uintptr_t>(X) % 16 != 0 || reinterpret_cast<uintptr_t>(W) % 2 != 0 ||
       reinterpret_cast<uintptr_t>(Y) % 4 != 0)
     return fail(EFG_EINVAL, "gemm: X must be 16-byte aligned, W 2-byte aligned and Y 4-byte aligned");
-  if (K % kRawK == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0)
-    return launch_gemm_ws<4>(Y, W, X, M, K, B, d_err, s);
+  if (K % kRawK == 0 && reinterpret_cast<uintptr_t>(W) % 16 == 0) {
+    GemmCall c;
+    c.qtype = 4;
+    c.jobs[0] = GemmJob{W, Y, M};
+    c.n_jobs = 1;
+    c.X = X;
+    c.K = K;
+    c.B = B;
+    return launch_gemm_ws<4>(c, d_err, s);
+  }
   const uint32_t n_tile = static_cast<uint32_t>(std::min<size_t>(kMaxTileN, (B + 15) / 16 * 16));
   GemmParams p{W, X, Y, static_cast<uint32_t>(M), static_cast<uint32_t>(K), static_cast<uint32_t>(B),
                static_cast<uint32_t>(K / 32 * 18), n_tile, d_err};
@@ -885,7 +919,33 @@ int launch_gemm_q8_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
   if (reinterpret_cast<uintptr_t>(X) % 16 != 0 || reinterpret_cast<uintptr_t>(W) % 16 != 0 ||
       reinterpret_cast<uintptr_t>(Y) % 4 != 0)
     return fail(EFG_EINVAL, "gemm: X and W must be 16-byte aligned and Y 4-byte aligned");
-  return launch_gemm_ws<8>(Y, W, X, M, K, B, d_err, s);
+  GemmCall c;
+  c.qtype = 8;
+  c.jobs[0] = GemmJob{W, Y, M};
+  c.n_jobs = 1;
+  c.X = X;
+  c.K = K;
+  c.B = B;
+  return launch_gemm_ws<8>(c, d_err, s);
+}
+
+int launch_gemm(const GemmCall& c, int* d_err, cudaStream_t s) {
+  if ((c.qtype != 4 && c.qtype != 8) || c.n_jobs < 1 || c.n_jobs > static_cast<int>(kMaxGemmJobs))
+    return fail(EFG_EINVAL, "gemm: %d jobs of type %d", c.n_jobs, c.qtype);
+  if (c.K == 0 || c.K % kRawK != 0 || c.K >= (1u << 30) || c.B == 0 || c.B >= (1u << 20) || !c.X)
+    return fail(EFG_EINVAL, "gemm: K = %zu, B = %zu", c.K, c.B);
+  if (reinterpret_cast<uintptr_t>(c.X) % 16 != 0)
+    return fail(EFG_EINVAL, "gemm: the B operand must be 16-byte aligned");
+  size_t tiles = 0;
+  for (int j = 0; j < c.n_jobs; ++j) {
+    const GemmJob& jb = c.jobs[j];
+    if (!jb.W || !jb.Y || jb.M == 0 || jb.M >= (1u << 31) || reinterpret_cast<uintptr_t>(jb.W) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(jb.Y) % 4 != 0)
+      return fail(EFG_EINVAL, "gemm: job %d (M = %zu) needs 16-byte aligned weights and an output", j, jb.M);
+    tiles += (jb.M + kTileM - 1) / kTileM;
+  }
+  if (tiles >= (1u << 31)) return fail(EFG_EINVAL, "gemm: too many row tiles");
+  return c.qtype == 4 ? launch_gemm_ws<4>(c, d_err, s) : launch_gemm_ws<8>(c, d_err, s);
 }
 
 }  // namespace efg

@@ -18,4 +18,23 @@ int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
 int launch_gemm_q8_0(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
                      cudaStream_t s);
 
+// Several matrices of one weight format that share K and the B operand X, in one launch;
+// the product may be added into Y (the decoder's residual add, Y = fl(Y + product) as an
+// elementwise add after the product would give). K a multiple of 256, weights and X 16-byte
+// aligned.
+struct GemmJob {
+  const uint8_t* W = nullptr;
+  float* Y = nullptr;  // [B][M]
+  size_t M = 0;
+};
+struct GemmCall {
+  int qtype = 4;  // 4: Q4_0, 8: Q8_0
+  GemmJob jobs[3];
+  int n_jobs = 0;
+  const float* X = nullptr;  // [B][K]
+  size_t K = 0, B = 0;
+  bool accumulate = false;  // Y += product (the residual add)
+};
+int launch_gemm(const GemmCall& c, int* d_err, cudaStream_t s);
+
 }  // namespace efg
