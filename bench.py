@@ -594,13 +594,41 @@ def run_profile(args):
     """A few plain launches for ncu (no CPU legs): --profile q8 -> config 1 (Q8_0 32000x2048),
     q4 -> config 0 (Q4_0 5632x2048), q4big -> Q4_0 65536x8192 (302 MB, half of config 4's
     rows, on the tensor-core kernel), gemm -> config 3 (5632x2048, B=64), decode / decode_persistent -> config 2, four
-    single-token forwards in each decode mode."""
+    single-token forwards in each decode mode, prefill / batch -> config 2's batched paths (the 23-token prompt, one
+    32-sequence step), the second run only between cudaProfilerStart and Stop."""
     import torch
 
     import edgeforge_b200 as efg
 
     torch.cuda.set_device(0)
-    if args.profile == "gemm":  # config 3, M=5632 K=2048 B=64: X split + GEMM, 3 calls
+    if args.profile in ("prefill", "batch"):
+        # config 2's batched paths: the 23-token prompt through efg_decoder_prefill, or one
+        # step of 32 sequences through efg_decoder_step_slots; the second run is bracketed by
+        # cudaProfilerStart/Stop (ncu --profile-from-start off captures only that run)
+        prompt = np.random.default_rng(2).integers(0, 32000, 23).astype(np.int32)
+        with efg.Decoder(decode_model(), 64) as dec:
+            if args.profile == "batch":
+                S = 32
+                dec.set_slots(S)
+                slots = np.arange(S, dtype=np.int32)
+                toks = prompt[:S] if S <= len(prompt) else np.resize(prompt, S)
+                for t in range(2):
+                    if t == 1:
+                        torch.cuda.synchronize()
+                        torch.cuda.profiler.start()
+                    _, toks = dec.step_slots(slots, toks, np.full(S, t, np.int32), compute_logits=False)
+            else:
+                for t in range(2):
+                    if t == 1:
+                        torch.cuda.synchronize()
+                        torch.cuda.profiler.start()
+                    dec.prefill(prompt, 0)
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+        assert efg.device_error() == 0
+        print(json.dumps({"profile": args.profile, "rows": 32 if args.profile == "batch" else len(prompt)}))
+        return 0
+    if args.profile == "gemm":  # config 3, M=5632 K=2048 B=64: 3 calls
         M, K, B = 5632, 2048, 64
         W = make_weights(efg, torch, Q4_0, M, K, 1, seed=7)[0]
         X = torch.randn(B, K, device="cuda")
@@ -656,7 +684,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode measurement")
     ap.add_argument("--no-sharded", action="store_true", help="skip the config-4 sharded matvec measurement")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 GEMM measurement")
-    ap.add_argument("--profile", choices=["q8", "q4", "q4big", "gemm", "decode", "decode_persistent"],
+    ap.add_argument("--profile", choices=["q8", "q4", "q4big", "gemm", "decode", "decode_persistent", "prefill", "batch"],
                     help="a few plain launches for ncu")
     args = ap.parse_args()
     global _RESULT_FD

@@ -19,6 +19,7 @@ from .api import (  # noqa: F401
     efq_check,
     gemm_q4_0,
     gemm_q8_0,
+    gemm_jobs,
     host_dequantize_row,
     host_matvec,
     host_matvec_static,

@@ -73,6 +73,7 @@ SIGNATURES = {
     "efg_host_matvec_static": (_i, [_i, _vp, _vp, _vp, _sz, _sz]),
     "efg_gemm_q4_0": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
     "efg_gemm_q8_0": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _vp]),
+    "efg_gemm_jobs": (_i, [_i, _i, _vp, _vp, _vp, _vp, _sz, _sz, _i, _vp]),
     "efg_shard_rows": (_i, [_sz, _i, _i, C.POINTER(_sz), C.POINTER(_sz)]),
     "efg_comm_unique_id": (_i, [_vp]),
     "efg_comm_init": (_i, [_vp, _i, _i, C.POINTER(_vp)]),

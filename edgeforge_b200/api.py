@@ -220,6 +220,16 @@ def gemm_q8_0(Y, W, X, M: int, K: int, B: int) -> None:
     check(load().efg_gemm_q8_0(_ptr(Y), _ptr(W), _ptr(X), M, K, B, _stream()))
 
 
+def gemm_jobs(qtype: int, jobs, X, K: int, B: int, accumulate: bool = False) -> None:
+    """efg_gemm_jobs: one launch for 1-3 (W, Y, M) matrices of one type sharing X; with
+    `accumulate`, Y += W X."""
+    n = len(jobs)
+    Ws = (C.c_void_p * n)(*[_ptr(w).value for w, _, _ in jobs])
+    Ys = (C.c_void_p * n)(*[_ptr(y).value for _, y, _ in jobs])
+    Ms = (C.c_size_t * n)(*[m for _, _, m in jobs])
+    check(load().efg_gemm_jobs(int(qtype), n, Ws, Ys, Ms, _ptr(X), K, B, int(accumulate), _stream()))
+
+
 # ---------------------------------------------------------------- row-sharded matvec
 
 

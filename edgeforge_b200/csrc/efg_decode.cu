@@ -379,15 +379,41 @@ __global__ void swiglu_kernel(float* __restrict__ out, const float* __restrict__
 // one CTA.
 __device__ __forceinline__ void rmsnorm_row(float* __restrict__ h, const float* __restrict__ x,
                                             const float* __restrict__ w, uint32_t n, float eps, double* red) {
+  // Rows of up to 8 elements per thread are read into registers first (all loads in flight
+  // at once instead of one load latency per element); the arithmetic and its order are the
+  // same on both paths.
+  constexpr uint32_t kPer = 8;
+  const bool regs = n <= kPer * blockDim.x;
+  float xv[kPer], wv[kPer];
   double ss = 0.0;
-  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss += static_cast<double>(x[i]) * static_cast<double>(x[i]);
+  if (regs) {
+#pragma unroll
+    for (uint32_t k = 0; k < kPer; ++k) {
+      const uint32_t i = threadIdx.x + k * blockDim.x;
+      xv[k] = i < n ? x[i] : 0.f;
+      wv[k] = i < n ? w[i] : 0.f;
+    }
+#pragma unroll
+    for (uint32_t k = 0; k < kPer; ++k)
+      if (threadIdx.x + k * blockDim.x < n) ss += static_cast<double>(xv[k]) * static_cast<double>(xv[k]);
+  } else {
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss += static_cast<double>(x[i]) * static_cast<double>(x[i]);
+  }
   ss = warp_sum_d(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   double tot = 0.0;
   for (uint32_t k = 0; k < blockDim.x / 32; ++k) tot += red[k];
   const float inv = static_cast<float>(1.0 / sqrt((n ? tot / n : 0.0) + static_cast<double>(eps)));
-  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) h[i] = __fmul_rn(w[i], __fmul_rn(x[i], inv));
+  if (regs) {
+#pragma unroll
+    for (uint32_t k = 0; k < kPer; ++k) {
+      const uint32_t i = threadIdx.x + k * blockDim.x;
+      if (i < n) h[i] = __fmul_rn(wv[k], __fmul_rn(xv[k], inv));
+    }
+  } else {
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) h[i] = __fmul_rn(w[i], __fmul_rn(x[i], inv));
+  }
 }
 
 // RMSNorm for the unfused path; one CTA.

@@ -963,3 +963,20 @@ extern "C" int efg_gemm_q8_0(float* d_Y, const uint8_t* d_W, const float* d_X, s
   if (!dev) return EFG_ECUDA;
   return efg::launch_gemm_q8_0(d_Y, d_W, d_X, M, K, B, dev->d_err, static_cast<cudaStream_t>(stream));
 }
+
+extern "C" int efg_gemm_jobs(int qtype, int n_jobs, const uint8_t* const* d_W, float* const* d_Y, const size_t* M,
+                             const float* d_X, size_t K, size_t B, int accumulate, void* stream) {
+  efg::DeviceInfo* dev = efg::current_device();
+  if (!dev) return EFG_ECUDA;
+  if ((qtype != EFG_Q4_0 && qtype != EFG_Q8_0) || n_jobs < 1 || n_jobs > 3 || !d_W || !d_Y || !M)
+    return efg::fail(EFG_EINVAL, "gemm jobs: type %d with %d jobs (1 to 3 of Q4_0 or Q8_0)", qtype, n_jobs);
+  efg::GemmCall c;
+  c.qtype = qtype == EFG_Q4_0 ? 4 : 8;
+  for (int j = 0; j < n_jobs; ++j) c.jobs[j] = efg::GemmJob{d_W[j], d_Y[j], M[j]};
+  c.n_jobs = n_jobs;
+  c.X = d_X;
+  c.K = K;
+  c.B = B;
+  c.accumulate = accumulate != 0;
+  return efg::launch_gemm(c, dev->d_err, static_cast<cudaStream_t>(stream));
+}

@@ -187,6 +187,14 @@ int efg_gemm_q4_0(float* d_Y, const uint8_t* d_W, const float* d_X, size_t M, si
  * aligned. Replaces B calls of ef::kern::matvec_q8_0 (qkernels.h:63-64) with one launch. */
 int efg_gemm_q8_0(float* d_Y, const uint8_t* d_W, const float* d_X, size_t M, size_t K, size_t B, void* stream);
 
+/* One launch for 1-3 matrices of one type (EFG_Q4_0 or EFG_Q8_0) that share X: Y_j = W_j X
+ * for W_j of M[j] rows, or Y_j += W_j X when `accumulate` (fl(Y + product), bit-identical to
+ * adding the product afterwards). K a multiple of 256, weights and X 16-byte aligned. The
+ * decoder's fused q/k/v projection (kern::matvec_jobs, src/model.cpp:230) and the o / down
+ * projections with their residual adds (src/model.cpp:247-249, 260-262), for a batch. */
+int efg_gemm_jobs(int qtype, int n_jobs, const uint8_t* const* d_W, float* const* d_Y, const size_t* M,
+                  const float* d_X, size_t K, size_t B, int accumulate, void* stream);
+
 /* ================================================================ row-sharded matvec (several GPUs) */
 
 /* A communicator between the GPUs of one node, one rank per GPU and process (or thread).

@@ -135,3 +135,45 @@ def test_q8_0_errors(cuda):
         efg.gemm_q8_0(Y, W, Xbig[1:], 64, 512, 4)
     efg.gemm_q8_0(Y, W, X, 0, 512, 4)  # nothing to do
     assert efg.device_error() == 0
+
+
+@pytest.mark.parametrize("qt", [QType.Q4_0, QType.Q8_0])
+def test_jobs_and_accumulate(cuda, oracle, qt):
+    """efg_gemm_jobs: q, k and v of TinyLlama's shape in one launch (each within 1e-5 of its
+    exact product), and the residual-add epilogue bit-identical to adding the product after."""
+    import torch
+
+    K, B = 2048, 23
+    Ms = [2048, 256, 256]
+    Ws = [_weights(torch, M, K, 10 + i, qt) for i, M in enumerate(Ms)]
+    X = torch.randn(B, K, generator=torch.Generator(device="cuda").manual_seed(11), device="cuda")
+    Ys = [torch.full((B, M), float("nan"), device="cuda") for M in Ms]
+    efg.gemm_jobs(qt, list(zip(Ws, Ys, Ms)), X, K, B)
+    torch.cuda.synchronize()
+    for W, Y, M in zip(Ws, Ys, Ms):
+        exact, mag = _exact(oracle, W, X, K, qt)
+        assert (np.abs(Y.cpu().numpy().astype(np.float64) - exact) / mag).max() <= TOL
+    # accumulate: Y0 + product, the same launch shape (same split) without accumulate
+    base = torch.randn(B, Ms[0], generator=torch.Generator(device="cuda").manual_seed(12), device="cuda")
+    P = torch.empty_like(base)
+    efg.gemm_jobs(qt, [(Ws[0], P, Ms[0])], X, K, B)
+    Yacc = base.clone()
+    efg.gemm_jobs(qt, [(Ws[0], Yacc, Ms[0])], X, K, B, accumulate=True)
+    torch.cuda.synchronize()
+    assert torch.equal(Yacc, base + P)
+    assert efg.device_error() == 0
+
+
+def test_jobs_errors(cuda):
+    import torch
+
+    W = _weights(torch, 256, 512, 13)
+    X = torch.randn(4, 512, device="cuda")
+    Y = torch.empty(4, 256, device="cuda")
+    with pytest.raises(efg.EdgeForgeError, match="jobs"):
+        efg.gemm_jobs(QType.Q4_0, [(W, Y, 256)] * 4, X, 512, 4)
+    with pytest.raises(efg.EdgeForgeError, match="K = 480"):
+        efg.gemm_jobs(QType.Q4_0, [(W, Y, 256)], X, 480, 4)
+    with pytest.raises(efg.EdgeForgeError, match="jobs"):
+        efg.gemm_jobs(2, [(W, Y, 256)], X, 512, 4)
+    assert efg.device_error() == 0
