@@ -107,6 +107,17 @@ int host_stream(HostCtx* h) {
   return EFG_OK;
 }
 
+// Device address of page-locked host memory (null for pageable memory): kernels can store
+// into it directly over the bus.
+void* mapped_host(void* p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
 }  // namespace
 
 extern "C" {
@@ -261,10 +272,14 @@ int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_
   if ((st = ensure(h->in, h->in_cap, cols * sizeof(float) + 16))) return st;
   if ((st = ensure(h->out, h->out_cap, rows * sizeof(float) + 16))) return st;
   if (cols) EFG_TRY_CUDA(cudaMemcpyAsync(h->in, x, cols * sizeof(float), cudaMemcpyHostToDevice, h->stream), "x upload");
-  if ((st = matvec_one(qtype, static_cast<float*>(h->out), static_cast<const uint8_t*>(dW),
+  // A page-locked y is written by the matvec's own stores, as rows finish, instead of by a
+  // copy after the kernel (which adds a copy-engine round trip to every call).
+  float* y_dev = static_cast<float*>(mapped_host(y));
+  if ((st = matvec_one(qtype, y_dev ? y_dev : static_cast<float*>(h->out), static_cast<const uint8_t*>(dW),
                        static_cast<const float*>(h->in), rows, cols, h->stream)))
     return st;
-  EFG_TRY_CUDA(cudaMemcpyAsync(y, h->out, rows * sizeof(float), cudaMemcpyDeviceToHost, h->stream), "y download");
+  if (!y_dev)
+    EFG_TRY_CUDA(cudaMemcpyAsync(y, h->out, rows * sizeof(float), cudaMemcpyDeviceToHost, h->stream), "y download");
   EFG_TRY_CUDA(cudaStreamSynchronize(h->stream), "stream synchronize");
   return EFG_OK;
 }

@@ -151,7 +151,9 @@ int efg_row_f32(float* d_out, int qtype, const uint8_t* d_W, size_t rows, size_t
  * range registered with efg_host_register_weights() (the reference passes read-only
  * views of a memory-mapped .efq, src/model.cpp:71-74: register the file's data once at
  * load); otherwise it is uploaded on every call, so a caller that rewrites its buffer
- * between calls always gets results for the current bytes.
+ * between calls always gets results for the current bytes. A page-locked y (cudaHostAlloc,
+ * cudaHostRegister, torch pin_memory) is written by the matvec kernel's own stores over the
+ * bus, saving a separate device-to-host copy per call; pageable y is copied after it.
  */
 int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols);
 int efg_host_quantize_row(int qtype, const float* x, size_t n, void* out, int search);

@@ -212,3 +212,31 @@ def test_reference_cpp_cases_through_the_shim(efg_lib, cuda, tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "0 failures" in r.stdout
+
+
+def test_host_matvec_pinned_buffers_reused(efg_lib, cuda, oracle):
+    """Repeated host calls with the same page-locked x and y buffers (y then written by the
+    kernel's own stores) read the current x every time and overwrite all of y, for registered
+    weights, views inside them and, after unregistering, weights read from host memory."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    W = random_packed(Q8_0, 700, 2048, rng)
+    efg_lib.host_register_weights(W)
+    x = torch.empty(2048, dtype=torch.float32).pin_memory().numpy()
+    y = torch.empty(700, dtype=torch.float32).pin_memory().numpy()
+    sub = W[200:300]
+    ys = torch.empty(100, dtype=torch.float32).pin_memory().numpy()
+    for _ in range(4):
+        x[:] = rng.standard_normal(2048).astype(np.float32)
+        y[:] = np.nan
+        efg_lib.host_matvec(Q8_0, W, x, 700, y=y)
+        assert rel_dot_errors(oracle, Q8_0, W, x, 700, y).max() < TOL
+        efg_lib.host_matvec(Q8_0, sub, x, 100, y=ys)
+        assert np.array_equal(ys.view(np.uint32), y[200:300].view(np.uint32))
+    efg_lib.host_unregister_weights(W)
+    W[:, 0:2] = 0  # first-block scales zeroed: now read from host memory on every call
+    efg_lib.host_matvec(Q8_0, W, x, 700, y=y)
+    assert rel_dot_errors(oracle, Q8_0, W, x, 700, y).max() < TOL
+    efg_lib.host_release_weights()
+    assert efg_lib.device_error() == 0
