@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the packed matrix-product path (one JSON line on rank 0).
 
-Workload: the Q8_0 matvec at TinyLlama lm_head shape,
+Workload (the headline benchmark's configuration 1): the Q8_0 matvec at TinyLlama lm_head shape,
 W 32000 x 2048 drawn N(0, 0.02) and quantized with the reference's Q8_0 rule (bit-exact
 GPU quantizer), x ~ N(0, 1). A step is one matvec. Six device copies of W (418 MB,
 > 3x the 126 MB L2) are used in rotation, so every step streams its weights from HBM.

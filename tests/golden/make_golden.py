@@ -11,7 +11,7 @@ Sources:
     (tests/golden/prompts/p0_factual/layer0 in the reference tree): a slice that pins
     the weight-free decode ops (RoPE, attention, SwiGLU).
 
-    python tests/golden/make_golden.py [--ref-tree /root/reference]
+    python tests/golden/make_golden.py [--ref-tree <reference source tree>]
 """
 from __future__ import annotations
 

@@ -1,7 +1,7 @@
 """Batched Q4_0 GEMM on the tensor cores (efg_gemm_q4_0) against the reference's per-column
 matvec semantics: every output column within 1e-5 of sum|w x| of the exact (float64) dot of
 the dequantized weights with that column (the reference's own check, test_qinfer.cpp:58-67),
-at BASELINE config 3's shapes and at ragged ones."""
+at benchmark config 3's shapes and at ragged ones."""
 from __future__ import annotations
 
 import numpy as np

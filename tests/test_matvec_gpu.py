@@ -157,7 +157,7 @@ def test_deterministic_and_jobs_equal_single_calls(efg_lib, cuda, oracle):
 
 @pytest.mark.parametrize("cfg", ["c0_q4_5632x2048", "c1_q8_32000x2048", "down_q4_2048x5632"])
 def test_config_shapes_quantized_gaussian(efg_lib, cuda, oracle, cfg):
-    """BASELINE configs 0/1 (and the down_proj shape of config 3): W ~ N(0, 0.02)
+    """Benchmark configs 0/1 (and the down_proj shape of config 3): W ~ N(0, 0.02)
     quantized by the reference algorithm, x ~ N(0, 1)."""
     qt, rows, cols = {"c0_q4_5632x2048": (Q4_0, 5632, 2048), "c1_q8_32000x2048": (Q8_0, 32000, 2048),
                       "down_q4_2048x5632": (Q4_0, 2048, 5632)}[cfg]

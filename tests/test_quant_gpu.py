@@ -77,7 +77,7 @@ def test_random_bit_patterns(efg_lib, cuda, oracle):
 
 
 def test_config1_round_trip_bit_exact(efg_lib, cuda, oracle):
-    """the seeded 32000x2048 N(0, 0.02) matrix through Q4_0 and Q8_0
+    """Benchmark config 1: the seeded 32000x2048 N(0, 0.02) matrix through Q4_0 and Q8_0
     quantize -> dequantize, bit-exact with quant.cpp."""
     rng = np.random.default_rng(1)
     X = (rng.standard_normal((32000, 2048)) * 0.02).astype(np.float32)
