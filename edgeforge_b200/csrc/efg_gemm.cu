@@ -538,6 +538,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
   // epilogue for every MMA, so Y is written after all earlier kernels (which may read Y)
   // have completed.
   if (warp >= kBWarp0) pdl_wait();
+  // The next kernel may be scheduled now (it only starts once every CTA of this grid has
+  // run this, and waits for this grid's completion before reading what it writes): its
+  // launch overlaps this kernel instead of following it.
+  pdl_launch_dependents();
   const uint32_t tmem = tmem_slot;
   const uint32_t a_col0 = 2 * N <= 128 ? 128u : 256u;
   bool ok = true;
@@ -738,7 +742,6 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
     }
     cluster_sync();  // peers keep their shared memory until every read is done
   }
-  pdl_launch_dependents();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
