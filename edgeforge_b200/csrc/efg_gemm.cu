@@ -1,26 +1,29 @@
-// efg_gemm.cu - batched Q4_0 x activation GEMM on the 5th-generation tensor cores.
+// efg_gemm.cu - batched Q4_0 / Q8_0 x activation GEMM on the 5th-generation tensor cores.
 //
-//   Y[b][m] = sum_k W[m][k] X[b][k]      W: Q4_0 rows [M][K/32 blocks], X: FP32 [B][K],
-//                                         Y: FP32 [B][M]
+//   Y[b][m] = sum_k W[m][k] X[b][k]      W: Q4_0 or Q8_0 rows [M][K/32 blocks], X: FP32
+//                                         [B][K], Y: FP32 [B][M]
 //
 // The reference has no GEMM: its prompt and multi-sequence work is one ef::kern::matvec per
 // column (src/qkernels.cpp:275-297), which is the oracle here. The tensor-core formulation
 // keeps that FP32 result within 1e-5 of sum |w x| per output:
 //   * a Q4_0 weight w = (c - 8) * d (4-bit code, FP16 scale) has at most 14 significant
-//     bits, so w = w_hi + w_lo with w_hi = bf16(w) and w_lo = bf16(w - w_hi) is EXACT;
+//     bits, so w = w_hi + w_lo with w_hi = bf16(w) and w_lo = bf16(w - w_hi) is EXACT; a
+//     Q8_0 weight q * d has at most 18, and three BF16 terms represent it exactly;
 //   * x = x1 + x2 with x1 = bf16(x), x2 = bf16(x - x1) keeps 16 significant bits;
-//   * D = W_hi X1 + W_hi X2 + W_lo X1 in FP32 (tcgen05.mma kind::f16, BF16 operands): every
-//     product is exact in FP32, the dropped terms (W_lo X2 and the residual of x) are at most
-//     2^-16 of each |w x| and of random sign.
+//   * products of BF16 operands (tcgen05.mma kind::f16) are exact in FP32; the only error
+//     is the dropped residual of x, at most 2^-16 of each |w x| and of random sign.
 //
-// One CTA computes a 128-row x N_TILE tile (N_TILE = B rounded up to 16, at most 256), the
-// accumulator in TMEM (128 lanes x N_TILE FP32 columns). K advances in 64-wide chunks
-// through two shared-memory stages: all 256 threads dequantize the chunk's W rows into the
-// W_hi / W_lo tiles and split X into X1 / X2 (K-major, 128-byte swizzled, the canonical
-// UMMA layout), then one thread issues the 12 MMAs of the chunk (3 products x 4 K-steps)
-// and commits them to the stage's mbarrier, which the threads wait on before they refill
-// that stage two chunks later. The epilogue reads TMEM with tcgen05.ld (warp w sees lanes
-// 32 (w % 4) ..) and writes Y with coalesced stores.
+// Two kernels. gemm_ws_kernel (K % 256 == 0, every shape the decoder uses) is warp-
+// specialised, with the dequantised weights in TMEM, X stacked along N and split-K over a
+// thread-block cluster; its role notes are above it. gemm_q4_0_kernel handles Q4_0 with
+// K % 256 != 0: one CTA computes a 128-row x N_TILE tile (N_TILE = B rounded up to 16, at
+// most 256), K advances in 64-wide chunks through two shared-memory stages: all 256 threads
+// dequantize the chunk's W rows into W_hi / W_lo tiles and split X into X1 / X2 (K-major,
+// 128-byte swizzled, the canonical UMMA layout), then one thread issues the 12 MMAs of the
+// chunk (W_hi X1 + W_hi X2 + W_lo X1 over 4 K-steps) and commits them to the stage's
+// mbarrier, which the threads wait on before they refill that stage two chunks later. The
+// epilogue reads TMEM with tcgen05.ld (warp w sees lanes 32 (w % 4) ..) and writes Y with
+// coalesced stores.
 #include <algorithm>
 #include <cstdint>
 #include <mutex>
