@@ -282,13 +282,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4_0_kernel(const __grid
 
 // ================================================================ warp-specialised kernel
 //
-// For K a multiple of 256 (every config-3 shape). The dequantised W operand lives in TMEM,
+// For K a multiple of 256 (every config-3 shape), Q4_0 or Q8_0 (template argument kQ), one
+// to three matrices sharing X per launch (each CTA finds its matrix from blockIdx.x), and
+// optionally Y += product (the residual add). The dequantised W operand lives in TMEM,
 // not shared memory: the MMAs read A from tensor memory ("A in TMEM" form of tcgen05.mma),
 // so the dequantising threads write their rows with tcgen05.st (one lane per row, no
 // swizzle, no generic->async proxy fence) and the tensor core reads no A bytes from shared
 // memory. Roles per CTA (22 warps):
-//   warp 0      streams the CTA's raw W rows, 256 columns (144 bytes) per row and chunk, into
-//               a 4-stage ring with one 2-D tensor copy per chunk;
+//   warp 0      streams the CTA's raw W rows, 256 columns (144 bytes for Q4_0, 272 for Q8_0)
+//               per row and chunk, into a 4-stage (Q8_0: 3-stage) ring with one 2-D tensor
+//               copy per chunk;
 //   warps 18..21 fill the B operand stages, hi rows then lo rows of the swizzled UMMA layout,
 //               so one stage is one MMA operand of 2 N rows. For N <= 64 they build the tiles
 //               from X (read the tile's N rows of FP32, split every value into BF16 hi / lo
@@ -299,16 +302,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_q4_0_kernel(const __grid
 //   warps 2..17 dequantize the 64-column sub-chunks in two groups of 8 (warps 2..9 the even
 //               sub-chunks, 10..17 the odd ones, so one group's waits overlap the other's
 //               arithmetic): warp w owns TMEM lanes 32 (w % 4) .. +31 (one row each) and half
-//               of the sub-chunk's columns (one Q4_0 block), writing W_hi and W_lo as packed
-//               BF16 pairs; warps 2..9 then run the epilogue;
-//   warp 1      allocates TMEM and issues the MMAs (one thread): per 16-wide K step
-//               D[:, 0:2N] += W_hi [X_hi | X_lo] and D[:, 0:2N] += W_lo [X_hi | X_lo], so
-//               D[:, n] collects the X_hi products and D[:, N + n] the X_lo products
-//               (their sum is the FP32 result; W_lo X_lo is below 2^-16 of |w x| and adds
-//               nothing harmful). Each sub-chunk is committed to its stage's "empty"
-//               barrier, the last one to "acc_full".
-// TMEM: the accumulator at columns [0, 2N), the A stages (64 columns: 32 of W_hi pairs, 32
-// of W_lo pairs) from column 128 (N <= 64, six stages) or 256 (N <= 128, four stages).
+//               of the sub-chunk's columns (one block), writing the weight's exact BF16 terms
+//               (two for Q4_0, three for Q8_0) as packed pairs; warps 2..9 then run the
+//               epilogue;
+//   warp 1      allocates TMEM and issues the MMAs (one thread): per 16-wide K step and
+//               weight term t, D[:, 0:2N] += W_t [X_hi | X_lo], so D[:, n] collects the X_hi
+//               products and D[:, N + n] the X_lo products (their sum is the FP32 result;
+//               the W_lo X_lo parts are below 2^-16 of |w x| and add nothing harmful). Each
+//               sub-chunk is committed to its stage's "empty" barrier, the last one to
+//               "acc_full".
+// TMEM: the accumulator at columns [0, 2N), then the A stages (32 columns per term) from
+// column 128 (N <= 64) or 256 (N <= 128), as many as fit (six / four for Q4_0).
 // Split-K: a cluster of S CTAs along z shares an output tile and splits its 64-column
 // sub-chunks evenly (a raw chunk at a split boundary is streamed by both CTAs, each using its
 // own sub-chunks); each CTA writes its partial tile into shared memory, and after a cluster
