@@ -523,6 +523,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
   uint8_t* raw = bst + n_stage * b_bytes;
 
   if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&job.wmap)) : "memory");
     for (uint32_t i = 0; i < kRawStages; ++i) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], kDequantWarps);
@@ -534,6 +535,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
     }
     mbar_init(&acc_full, 1);
     fence_barrier_init();
+    // the first raw chunks go out now, before the CTA-wide barrier and the TMEM allocation
+    const uint64_t pol = l2_evict_first_policy();
+    for (uint32_t rc = 0; rc < min(n_raw, kRawStages); ++rc) {
+      mbar_arrive_expect_tx(&raw_full[rc], kRawBytes);
+      tma_load_2d(raw + rc * kRawBytes, &job.wmap, static_cast<int32_t>((rc_first + rc) * (kRawRow / 8)),
+                  static_cast<int32_t>(m0), &raw_full[rc], pol);
+    }
   }
   if (warp == 1) tmem_alloc(&tmem_slot, kTmemCols);
   tc_fence_before();
@@ -556,8 +564,8 @@ __global__ void __launch_bounds__(kWsThreads, 1) gemm_ws_kernel(const __grid_con
   if (warp == 0) {
     // ---------------------------------------------------------- raw W producer
     const uint64_t pol = l2_evict_first_policy();
-    uint32_t issued_raw = 0;
-    for (uint32_t rc = 0; rc < n_raw && ok; ++rc) {
+    uint32_t issued_raw = min(n_raw, kRawStages);  // issued by thread 0 in the prologue
+    for (uint32_t rc = issued_raw; rc < n_raw && ok; ++rc) {
       const uint32_t rs = rc % kRawStages;
       if (rc >= kRawStages) ok = mbar_wait_idle(&raw_empty[rs], ((rc / kRawStages) - 1) & 1u, p.err);
       if (!__all_sync(0xFFFFFFFFu, ok)) {
