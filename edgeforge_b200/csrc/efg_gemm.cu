@@ -975,21 +975,32 @@ int launch_gemm_q8_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
   return launch_gemm_ws<8>(c, d_err, s);
 }
 
-int launch_gemm(const GemmCall& c, int* d_err, cudaStream_t s) {
-  if ((c.qtype != 4 && c.qtype != 8) || c.n_jobs < 1 || c.n_jobs > static_cast<int>(kMaxGemmJobs))
-    return fail(EFG_EINVAL, "gemm: %d jobs of type %d", c.n_jobs, c.qtype);
-  if (c.K == 0 || c.K % kRawK != 0 || c.K >= (1u << 30) || c.B == 0 || c.B >= (1u << 20) || !c.X)
-    return fail(EFG_EINVAL, "gemm: K = %zu, B = %zu", c.K, c.B);
-  if (reinterpret_cast<uintptr_t>(c.X) % 16 != 0)
-    return fail(EFG_EINVAL, "gemm: the B operand must be 16-byte aligned");
+int launch_gemm(const GemmCall& call, int* d_err, cudaStream_t s) {
+  if ((call.qtype != 4 && call.qtype != 8) || call.n_jobs < 1 || call.n_jobs > static_cast<int>(kMaxGemmJobs))
+    return fail(EFG_EINVAL, "gemm: %d jobs of type %d", call.n_jobs, call.qtype);
+  if (call.K % kRawK != 0 || call.K >= (1u << 30) || call.B >= (1u << 20))
+    return fail(EFG_EINVAL, "gemm: K = %zu, B = %zu", call.K, call.B);
+  GemmCall c = call;  // the jobs with rows
+  c.n_jobs = 0;
   size_t tiles = 0;
-  for (int j = 0; j < c.n_jobs; ++j) {
-    const GemmJob& jb = c.jobs[j];
-    if (!jb.W || !jb.Y || jb.M == 0 || jb.M >= (1u << 31) || reinterpret_cast<uintptr_t>(jb.W) % 16 != 0 ||
+  for (int j = 0; j < call.n_jobs; ++j) {
+    const GemmJob& jb = call.jobs[j];
+    if (jb.M == 0) continue;
+    if (!jb.Y || (call.K && !jb.W) || jb.M >= (1u << 31) || reinterpret_cast<uintptr_t>(jb.W) % 16 != 0 ||
         reinterpret_cast<uintptr_t>(jb.Y) % 4 != 0)
       return fail(EFG_EINVAL, "gemm: job %d (M = %zu) needs 16-byte aligned weights and an output", j, jb.M);
+    c.jobs[c.n_jobs++] = jb;
     tiles += (jb.M + kTileM - 1) / kTileM;
   }
+  if (c.n_jobs == 0 || c.B == 0) return EFG_OK;
+  if (c.K == 0) {  // every dot is empty: Y = 0, or Y unchanged when adding
+    if (!c.accumulate)
+      for (int j = 0; j < c.n_jobs; ++j)
+        EFG_TRY_CUDA(cudaMemsetAsync(c.jobs[j].Y, 0, c.jobs[j].M * c.B * sizeof(float), s), "gemm zero fill");
+    return EFG_OK;
+  }
+  if (!c.X || reinterpret_cast<uintptr_t>(c.X) % 16 != 0)
+    return fail(EFG_EINVAL, "gemm: the B operand must be 16-byte aligned");
   if (tiles >= (1u << 31)) return fail(EFG_EINVAL, "gemm: too many row tiles");
   return c.qtype == 4 ? launch_gemm_ws<4>(c, d_err, s) : launch_gemm_ws<8>(c, d_err, s);
 }

@@ -191,7 +191,8 @@ int efg_gemm_q8_0(float* d_Y, const uint8_t* d_W, const float* d_X, size_t M, si
 
 /* One launch for 1-3 matrices of one type (EFG_Q4_0 or EFG_Q8_0) that share X: Y_j = W_j X
  * for W_j of M[j] rows, or Y_j += W_j X when `accumulate` (fl(Y + product), bit-identical to
- * adding the product afterwards). K a multiple of 256, weights and X 16-byte aligned. The
+ * adding the product afterwards). K a multiple of 256 (K = 0 gives Y = 0, or Y unchanged when
+ * adding; B = 0 and jobs of M = 0 rows do nothing), weights and X 16-byte aligned. The
  * decoder's fused q/k/v projection (kern::matvec_jobs, src/model.cpp:230) and the o / down
  * projections with their residual adds (src/model.cpp:247-249, 260-262), for a batch. */
 int efg_gemm_jobs(int qtype, int n_jobs, const uint8_t* const* d_W, float* const* d_Y, const size_t* M,

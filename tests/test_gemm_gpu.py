@@ -176,4 +176,15 @@ def test_jobs_errors(cuda):
         efg.gemm_jobs(QType.Q4_0, [(W, Y, 256)], X, 480, 4)
     with pytest.raises(efg.EdgeForgeError, match="jobs"):
         efg.gemm_jobs(2, [(W, Y, 256)], X, 512, 4)
+    # empty cases, as efg_gemm_q4_0 has them: K = 0 zero-fills (or adds nothing), B = 0 and
+    # zero-row jobs do nothing
+    Y.fill_(5.0)
+    efg.gemm_jobs(QType.Q4_0, [(W, Y, 256)], X, 0, 4, accumulate=True)
+    efg.gemm_jobs(QType.Q4_0, [(W, Y, 256)], X, 512, 0)
+    efg.gemm_jobs(QType.Q4_0, [(W, Y, 0)], X, 512, 4)
+    torch.cuda.synchronize()
+    assert bool((Y == 5.0).all())
+    efg.gemm_jobs(QType.Q4_0, [(W, Y, 256)], X, 0, 4)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(Y).item() == 0
     assert efg.device_error() == 0
