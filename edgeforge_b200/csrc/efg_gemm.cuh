@@ -11,7 +11,8 @@ namespace efg {
 // Y [B][M]); the tcgen05 kernels of efg_gemm.cu. For B <= 64 (and K % 256 == 0) one kernel
 // launch and no scratch memory, safe to record in a CUDA graph; wider calls first split X into
 // a per-device scratch that grows with the largest call (do not record those in a graph that
-// may outlive a larger call). Returns an EFG_* status.
+// may outlive a larger call, and do not let wide calls on different streams overlap: they
+// share the scratch). Returns an EFG_* status.
 int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_t K, size_t B, int* d_err,
                      cudaStream_t s);
 // The same product for Q8_0 weights (K a multiple of 256, W and X 16-byte aligned).

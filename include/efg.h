@@ -181,7 +181,8 @@ int efg_host_matvec_static(int qtype, float* y, const uint8_t* W, const float* x
  * BF16 parts, FP32 accumulation in TMEM). Layout: W packed Q4_0 [M] rows, X FP32 [B][K]
  * (each column contiguous, 16-byte aligned), Y FP32 [B][M]. The reference has no GEMM; it
  * runs ef::kern::matvec (qkernels.h:66) once per column, which each Y column matches
- * within 1e-5 of sum|w x| for finite inputs. An infinite x or FP16 scale splits into an
+ * within 1e-5 of sum|w x| for finite inputs. For B > 64 the split X goes through one
+ * per-device scratch: such calls on different streams must not overlap. An infinite x or FP16 scale splits into an
  * infinite high part and a NaN residual, so an output the matvec gives as +-inf comes out
  * NaN here (NaN outputs stay NaN). */
 int efg_gemm_q4_0(float* d_Y, const uint8_t* d_W, const float* d_X, size_t M, size_t K, size_t B, void* stream);
