@@ -1,7 +1,8 @@
-"""Batched Q4_0 GEMM on the tensor cores (efg_gemm_q4_0) against the reference's per-column
-matvec semantics: every output column within 1e-5 of sum|w x| of the exact (float64) dot of
-the dequantized weights with that column (the reference's own check, test_qinfer.cpp:58-67),
-at benchmark config 3's shapes and at ragged ones."""
+"""Batched Q4_0 / Q8_0 GEMM on the tensor cores (efg_gemm_q4_0, efg_gemm_q8_0, efg_gemm_jobs)
+against the reference's per-column matvec semantics: every output column within 1e-5 of
+sum|w x| of the exact (float64) dot of the dequantized weights with that column (the
+reference's own check, test_qinfer.cpp:58-67), at benchmark config 3's shapes, the lm_head
+shape and ragged ones; multi-matrix launches and the residual-add epilogue."""
 from __future__ import annotations
 
 import numpy as np
