@@ -150,7 +150,7 @@ __device__ void attend_head(const float* __restrict__ qh, const float* __restric
       d[3] = v.w;
       if (one_round) reinterpret_cast<float4*>(vch + t * hd)[i4] = w;
     }
-    __syncthreads();
+    if (!staged) __syncthreads();  // (a caller that staged the rows synchronised after it)
     for (int t = tid; t < cn; t += blockDim.x) {
       const float* kt = kch + t * (hd + 1);
       // dot with 8 partial sums combined pairwise (src/kernels.cpp:28-43)
@@ -165,7 +165,9 @@ __device__ void attend_head(const float* __restrict__ qh, const float* __restric
       sc[c0 + t] = __fmul_rn(dot, scale);
       mx = fmaxf(mx, sc[c0 + t]);
     }
-    __syncthreads();  // kch is rewritten by the next round
+    // kch is rewritten by the next round; after the last one, the barrier of the max
+    // reduction below orders the scores for the threads that read them
+    if (c0 + kAttnChunkPos < n_pos) __syncthreads();
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
