@@ -1,20 +1,25 @@
 #!/usr/bin/env python3
 """Benchmark of the packed matrix-product path (one JSON line on rank 0).
 
-Workload (the headline benchmark's configuration 1): the Q8_0 matvec at TinyLlama lm_head shape,
-W 32000 x 2048 drawn N(0, 0.02) and quantized with the reference's Q8_0 rule (bit-exact
-GPU quantizer), x ~ N(0, 1). A step is one matvec. Six device copies of W (418 MB,
-> 3x the 126 MB L2) are used in rotation, so every step streams its weights from HBM.
+Workload (the headline benchmark's configuration 4): the Q4_0 matvec W x with W 131072 x 8192
+drawn N(0, 0.02) and quantized with the reference's Q4_0 rule (bit-exact GPU quantizer,
+603,979,776 packed bytes), x ~ N(0, 1), row-sharded over the job's GPUs: rank r holds the
+rows [R r / N, R (r + 1) / N) (ThreadPool::chunk_begin's split) and every rank ends the step
+with all 131072 outputs (efg_matvec_sharded). A step is one sharded matvec. Strong scaling:
+the matrix is the same at every N. Enough rotating copies of each rank's shard are used that
+they exceed twice the 126 MB L2, so every step streams its weights from HBM.
 
   python bench.py [--gpus N] [--steps K] [--warmup W]      # our B200 path
   python bench.py --impl reference                           # the reference's CPU path
 
-Metric: algorithmic bytes per step (packed W + x + y = 69,768,192 B) / time, in GB/s.
-value: device time of K steps (CUDA events, a CUDA graph of the C-ABI launches, max over
-ranks). e2e: the same steps through the host-pointer C-ABI call efg_host_matvec (pinned
-x in, y out every step; W resident after its first upload), wall clock.
-N > 1: each rank runs its own config-1 matvecs (weak scaling, no collective in the data
-path); value = bytes of all ranks / max time.
+Metric: algorithmic bytes per step (packed W + x + y = 604,536,832 B) / time, in GB/s.
+value: device time of K steps (CUDA events around CUDA graphs of the C-ABI calls, max over
+ranks). e2e: the same steps through the C ABI with host buffers: x copied in from page-locked
+memory, efg_matvec_sharded, y read back to page-locked memory, every step (wall clock, max
+over ranks). After timing, every rank checks that its slice of the gathered y is bit-identical
+to its own local matvec and that all ranks hold the same y ("verified").
+Extras at N = 1: configs 0 (Q4_0 5632 x 2048), 1 (Q8_0 32000 x 2048 and its quantize round
+trip), 2 (decode), 3 (GEMM); at every N: the row-sharded lm_head with its distributed argmax.
 """
 from __future__ import annotations
 
@@ -31,10 +36,12 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-ROWS, COLS = 32000, 2048
+ROWS, COLS = 32000, 2048          # config 1 (extra)
+ROWS4, COLS4 = 131072, 8192       # config 4 (headline)
 Q8_0, Q4_0 = 3, 4
 N_COPIES = 6
-METRIC = "Q8_0 matvec HBM GB/s (lm_head 32000x2048)"
+METRIC = "Q4_0 matvec HBM GB/s (config 4: 131072x8192, row-sharded over the job's GPUs)"
+L2_BYTES = 126 * 1024 * 1024
 
 
 def algo_bytes(qt, rows, cols):
@@ -116,33 +123,72 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- reference CPU leg
-def cpu_reference_matvec(seconds: float, qt=Q8_0, rows=ROWS, cols=COLS, copies=N_COPIES, steps=None, warmup=3,
-                         cap_seconds=150.0):
-    """The reference's AVX2 matvec (kern::matvec + ThreadPool, oracle/_ref) on the host
-    cores: rotating W copies (418 MB, larger than the host's last-level cache). Runs
-    `steps` matvecs (or for `seconds` when steps is None), never longer than cap_seconds."""
-    from oracle.oracle import Oracle, Reference
+def physical_cores():
+    """Physical cores the way the reference's sysinfo counts them on Linux
+    (src/sysinfo.cpp:177-195): distinct (physical id, core id) pairs in /proc/cpuinfo."""
+    cores, phys = set(), "0"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                k, _, v = line.partition(":")
+                k, v = k.strip(), v.strip()
+                if k == "physical id":
+                    phys = v
+                elif k == "core id":
+                    cores.add((phys, v))
+    except OSError:
+        return None
+    return len(cores) or None
 
-    ref, orc = Reference(), Oracle()
-    threads = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    X = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
-    W = orc.quantize_rows(qt, X, threads=threads)
-    del X
-    Ws = [W.copy() for _ in range(copies)]
-    x = rng.standard_normal(cols).astype(np.float32)
+
+def host_threads():
+    """Threads for the CPU legs: every logical CPU this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_info(threads):
+    return {"cores": threads, "physical_cores": physical_cores(), "logical_cpus": os.cpu_count()}
+
+
+def cpu_reference_matvec(qt, Ws, x, rows, cols, seconds=None, steps=None, warmup=1, cap_seconds=150.0):
+    """The reference's AVX2 matvec (kern::matvec + ThreadPool, oracle/_ref, its own sources)
+    on the host cores over the packed matrices Ws in rotation. Runs `steps` matvecs (or for
+    `seconds` when steps is None), never longer than cap_seconds. Returns (GB/s, threads,
+    matvecs, seconds)."""
+    from oracle.oracle import Reference
+
+    ref = Reference()
+    threads = host_threads()
     y = np.zeros(rows, np.float32)
     with ref.pool(threads) as pool:
-        for i in range(max(warmup, copies)):  # warm-up: page in every copy
-            ref.matvec_backend(qt, Ws[i % copies], x, rows, avx2=True, pool=pool, y=y)
+        for i in range(max(warmup, len(Ws))):  # warm-up: page in every copy
+            ref.matvec_backend(qt, Ws[i % len(Ws)], x, rows, avx2=True, pool=pool, y=y)
         n, t0 = 0, time.perf_counter()
         while True:
-            ref.matvec_backend(qt, Ws[n % copies], x, rows, avx2=True, pool=pool, y=y)
+            ref.matvec_backend(qt, Ws[n % len(Ws)], x, rows, avx2=True, pool=pool, y=y)
             n += 1
             el = time.perf_counter() - t0
             if (steps is not None and n >= steps) or (steps is None and el >= seconds) or el >= cap_seconds:
                 break
     return algo_bytes(qt, rows, cols) * n / el / 1e9, threads, n, el
+
+
+def host_config4_weights(threads):
+    """Config 4's matrix on the host: 131072 x 8192 weights ~ N(0, 0.02) (numpy, seed 0) quantized
+    to Q4_0 by the reference's own quantize_rows (MSE search), 4096 rows at a time."""
+    from oracle.oracle import Reference
+
+    ref = Reference()
+    rng = np.random.default_rng(0)
+    W = np.empty((ROWS4, COLS4 // 32 * 18), np.uint8)
+    with ref.pool(threads) as pool:
+        for r0 in range(0, ROWS4, 4096):
+            X = rng.standard_normal((4096, COLS4), dtype=np.float32) * np.float32(0.02)
+            W[r0:r0 + 4096] = ref.quantize_rows(Q4_0, X, pool=pool)
+    return W
 
 
 def run_reference_arm(args):
@@ -152,19 +198,23 @@ def run_reference_arm(args):
     if not (ROOT / "oracle" / "_ref" / "libefref.so").exists():
         emit({"impl": "reference", "unavailable": "oracle/_ref/libefref.so was not built"})
         return 0
-    # W untimed warm-up steps, then K timed steps (each one CPU matvec of the workload;
-    # stopped after 150 s, in which case "steps" reports the count actually timed)
-    gbs, threads, n, el = cpu_reference_matvec(0.0, steps=args.steps, warmup=args.warmup)
+    threads = host_threads()
+    W = host_config4_weights(threads)
+    x = np.random.default_rng(1).standard_normal(COLS4).astype(np.float32)
+    # W untimed warm-up steps, then K timed steps, each one CPU matvec of the whole matrix
+    # (stopped after 150 s, in which case "steps" reports the count actually timed)
+    gbs, threads, n, el = cpu_reference_matvec(Q4_0, [W], x, ROWS4, COLS4, steps=args.steps, warmup=args.warmup)
     args.steps = n
     line = {
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(el / n * 1e3, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32 (Q8_0 weights)", "data": "synthetic (seeded N(0,0.02) W, N(0,1) x)",
-        "config": {"workload": "config1_q8_0_matvec_32000x2048", "rows": ROWS, "cols": COLS, "copies": N_COPIES,
-                   "l2": "host LLC exceeded by rotating copies"},
+        "warmup": args.warmup, "ms_per_step": round(el / n * 1e3, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 (Q4_0 weights)", "data": "synthetic (seeded N(0,0.02) W, N(0,1) x)",
+        "config": {"workload": "config4_q4_0_matvec_131072x8192", "rows": ROWS4, "cols": COLS4,
+                   "l2": "604 MB matrix, far larger than the host's last-level cache"},
         "impl": "reference",
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "reference",
-                         "sample": f"{n} matvecs of the reference AVX2 kernel, ThreadPool({threads})"},
+        "cpu_baseline": dict(value=round(gbs, 3), unit="GB/s", kind="reference", **cpu_info(threads),
+                             sample=f"{n} matvecs of the whole 604 MB matrix by the reference AVX2 kernel, "
+                                    f"ThreadPool({threads})"),
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
@@ -181,30 +231,222 @@ def make_weights(efg, torch, qt, rows, cols, copies, seed=0):
     return [W] + [W.clone() for _ in range(copies - 1)]
 
 
-def graph_of_steps(efg, torch, qt, Ws, x, y, rows, cols, n):
-    """A CUDA graph of n matvec launches made through the C ABI (rotating copies)."""
+def config4_shard(efg, torch, begin, count, piece=8192):
+    """This rank's rows [begin, begin + count) of config 4's matrix, quantized on the device.
+    The matrix is drawn in 8192-row pieces, piece i from its own seeded generator, so every
+    rank at every N sees the same matrix."""
+    rb = COLS4 // 32 * 18
+    W = torch.empty(max(count, 1) * rb, dtype=torch.uint8, device="cuda")
+    for p0 in range(begin // piece * piece, begin + count, piece):
+        g = torch.Generator(device="cuda").manual_seed(1000 + p0 // piece)
+        X = torch.randn(piece, COLS4, generator=g, device="cuda") * 0.02
+        lo, hi = max(p0, begin), min(p0 + piece, begin + count)
+        efg.quantize_rows(Q4_0, X[lo - p0:hi - p0].contiguous(), hi - lo, COLS4, W[(lo - begin) * rb:], True)
+        del X
+    return W
+
+
+def graphs_of(torch, fn, steps, warmup, chunk=60):
+    """CUDA graphs of `fn(i)` for i in a step range: (full graph of `chunk` steps, graph of the
+    remainder or None, chunk), after `warmup` plain calls outside capture (lazy set-up)."""
+    chunk = max(1, min(chunk, steps))
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
     s = torch.cuda.Stream()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        for i in range(2):  # launch once outside capture (attributes, lazy init)
-            efg.matvec(qt, y, Ws[i % len(Ws)], x, rows, cols)
-        torch.cuda.synchronize()
-        with torch.cuda.graph(graph, stream=s):
+    s.wait_stream(torch.cuda.current_stream())
+
+    def cap(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
             for i in range(n):
-                efg.matvec(qt, y, Ws[i % len(Ws)], x, rows, cols)
-    return graph
+                fn(i)
+        return g
 
-
-def time_steps(efg, torch, qt, Ws, x, y, rows, cols, steps, warmup, chunk=60):
-    """Device time (ms) of exactly `steps` matvecs, launched as CUDA graphs."""
-    chunk = max(len(Ws), min(chunk, steps))
-    g_full = graph_of_steps(efg, torch, qt, Ws, x, y, rows, cols, chunk)
+    g_full = cap(chunk)
     rem = steps % chunk
-    g_rem = graph_of_steps(efg, torch, qt, Ws, x, y, rows, cols, rem) if rem else None
-    g_warm = graph_of_steps(efg, torch, qt, Ws, x, y, rows, cols, max(warmup, 1))
-    g_warm.replay()
+    g_rem = cap(rem) if rem else None
     torch.cuda.synchronize()
     return g_full, g_rem, chunk
+
+
+def replay_timed(torch, g_full, g_rem, chunk, steps, barrier, world, clocks=None):
+    """Device time (ms) of exactly `steps` steps replayed from the graphs, bracketed by a
+    barrier and a device synchronize on both sides; the max over ranks."""
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx = clocks if clocks is not None else _Null()
+    with ctx:
+        start.record()
+        for _ in range(steps // chunk):
+            g_full.replay()
+        if g_rem is not None:
+            g_rem.replay()
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+def y_digest(torch, y):
+    """An order-sensitive 64-bit digest of y's bits (equal digests on all ranks = same y)."""
+    v = y.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    w = torch.arange(1, v.numel() + 1, device=y.device, dtype=torch.int64) % 1000003 + 1
+    return int((v * w).sum().item())
+
+
+def config4_headline(torch, efg, args, world, rank, local, hbm_peak, barrier):
+    """Config 4 row-sharded over the job's GPUs: device time of K steps, the local matvec
+    alone, verification of the gathered y, and the host-buffer e2e loop."""
+    b, c = efg.shard_rows(ROWS4, world, rank)
+    rb = COLS4 // 32 * 18
+    shard_bytes = c * rb
+    copies = max(1, -(-2 * L2_BYTES // max(shard_bytes, 1)))  # rotating shards > 2x L2
+    W0 = config4_shard(efg, torch, b, c)
+    Ws = [W0] + [W0.clone() for _ in range(copies - 1)]
+    x = torch.randn(COLS4, generator=torch.Generator(device="cuda").manual_seed(5), device="cuda")
+    y = torch.empty(ROWS4, device="cuda")
+    comm = efg.Comm.from_torch() if world > 1 else efg.Comm(efg.Comm.unique_id(), 1, 0)
+    gather = "none (one rank)" if world == 1 else "ncclAllGather in place"
+    try:
+        def step(i):
+            efg.matvec_sharded(Q4_0, y, Ws[i % copies], x, ROWS4, COLS4, comm)
+
+        # W warm-up steps as plain calls, then the graphs are captured and replayed once
+        # untimed (a graph's first launch uploads it to the device)
+        g_full, g_rem, chunk = graphs_of(torch, step, args.steps, args.warmup)
+        g_full.replay()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(local)
+        ms = replay_timed(torch, g_full, g_rem, chunk, args.steps, barrier, world, clocks)
+        del g_full, g_rem
+
+        # the local matvec alone (this rank's rows, no exchange): the dominant kernel
+        yl = y[b:b + c]
+
+        def local_step(i):
+            efg.matvec(Q4_0, yl, Ws[i % copies], x, c, COLS4)
+
+        lf, lr, lc = graphs_of(torch, local_step, args.steps, args.warmup)
+        lf.replay()
+        ms_local = replay_timed(torch, lf, lr, lc, args.steps, barrier, world)
+        del lf, lr
+
+        # verification: this rank's slice of the gathered y equals its own local matvec bit for
+        # bit, and every rank holds the same y
+        y.fill_(float("nan"))
+        efg.matvec_sharded(Q4_0, y, Ws[0], x, ROWS4, COLS4, comm)
+        mine = torch.empty(max(c, 1), device="cuda")
+        efg.matvec(Q4_0, mine, Ws[0], x, c, COLS4)
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(y[b:b + c], mine[:c])) and not bool(torch.isnan(y).any())
+        dg = y_digest(torch, y)
+        if world > 1:
+            t = torch.tensor([1 if ok else 0, dg, -dg], device="cuda", dtype=torch.int64)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+            ok = bool(t[0].item() == 1) and int(t[1].item()) == -int(t[2].item()) == dg
+        # e2e: x from page-locked host memory in, the C-ABI call, y back to page-locked memory
+        x_h = x.cpu().pin_memory()
+        y_h = torch.empty(ROWS4).pin_memory()
+        x_d = torch.empty_like(x)
+        cur = torch.cuda.current_stream()
+
+        def e2e_step(i):
+            x_d.copy_(x_h, non_blocking=True)
+            efg.matvec_sharded(Q4_0, y, Ws[i % copies], x_d, ROWS4, COLS4, comm)
+            y_h.copy_(y, non_blocking=True)
+            cur.synchronize()
+
+        for i in range(args.warmup):
+            e2e_step(i)
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            e2e_step(i)
+        el = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([el], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            el = float(t.item())
+        assert efg.device_error() == 0
+    finally:
+        comm.close()
+    total = algo_bytes(Q4_0, ROWS4, COLS4)
+    local_bytes = shard_bytes + 4 * COLS4 + 4 * c
+    return {"ms": ms, "ms_local": ms_local, "el_e2e": el, "total": total, "local_bytes": local_bytes,
+            "rows_per_rank": c, "copies": copies, "verified": ok, "gather": gather, "clocks": clocks.summary(),
+            "W_host": Ws[0].cpu().numpy() if (world == 1 and not args.no_cpu_baseline) else None,
+            "x_host": x.cpu().numpy()}
+
+
+def config1_extra(torch, efg, hbm_peak, steps=2000, warmup=60):
+    """Config 1: the Q8_0 matvec at lm_head shape (32000 x 2048), 6 rotating W copies (418 MB),
+    device time of CUDA graphs of C-ABI launches; e2e through efg_host_matvec (page-locked x in
+    and y out every call, W registered resident once, like a model load)."""
+    Ws = make_weights(efg, torch, Q8_0, ROWS, COLS, N_COPIES, seed=1)
+    x = torch.randn(COLS, generator=torch.Generator(device="cuda").manual_seed(2), device="cuda")
+    y = torch.empty(ROWS, device="cuda")
+
+    def step(i):
+        efg.matvec(Q8_0, y, Ws[i % N_COPIES], x, ROWS, COLS)
+
+    g_full, g_rem, chunk = graphs_of(torch, step, steps, warmup)
+    g_full.replay()
+    ms = replay_timed(torch, g_full, g_rem, chunk, steps, torch.cuda.synchronize, 1) / steps
+    del g_full, g_rem
+    nbytes = algo_bytes(Q8_0, ROWS, COLS)
+    x_h = torch.empty(COLS, dtype=torch.float32).pin_memory().numpy()
+    y_h = torch.empty(ROWS, dtype=torch.float32).pin_memory().numpy()
+    x_h[:] = x.cpu().numpy()
+    Whs = [Ws[0].cpu().numpy() for _ in range(N_COPIES)]
+    for w in Whs:
+        efg.host_register_weights(w)
+    for i in range(10):
+        efg.host_matvec(Q8_0, Whs[i % N_COPIES], x_h, ROWS, y=y_h)
+    t0 = time.perf_counter()
+    n = 500
+    for i in range(n):
+        efg.host_matvec(Q8_0, Whs[i % N_COPIES], x_h, ROWS, y=y_h)
+    el = (time.perf_counter() - t0) / n
+    efg.host_release_weights()
+    assert efg.device_error() == 0
+    return {"us_per_launch": round(ms * 1e3, 3), "gbs": round(nbytes / ms / 1e6, 1),
+            "frac_of_hbm": round(nbytes / ms / 1e6 / hbm_peak, 4), "bytes_per_launch": nbytes, "copies": N_COPIES,
+            "e2e_us_per_call": round(el * 1e6, 2), "e2e_gbs": round(nbytes / el / 1e9, 1),
+            "e2e_api": "efg_host_matvec (page-locked x, y; W registered)"}
+
+
+def config0_extra(torch, efg, hbm_peak, x_seed=2, launches=1280):
+    """Config 0: the Q4_0 matvec at TinyLlama gate_proj shape (5632 x 2048), 64 rotating copies
+    (415 MB), launched back to back in CUDA graphs (weight prefetch on, PDL)."""
+    rows, cols, copies = 5632, 2048, 64
+    W4 = make_weights(efg, torch, Q4_0, rows, cols, copies, seed=3)
+    x = torch.randn(cols, generator=torch.Generator(device="cuda").manual_seed(x_seed), device="cuda")
+    y4 = torch.empty(rows, device="cuda")
+
+    def step(i):
+        efg.matvec(Q4_0, y4, W4[i % copies], x, rows, cols)
+
+    g, gr, c = graphs_of(torch, step, launches, 64, chunk=640)
+    g.replay()
+    ms = replay_timed(torch, g, gr, c, launches, torch.cuda.synchronize, 1) / launches
+    del g, gr, W4
+    nb = algo_bytes(Q4_0, rows, cols)
+    return {"gbs": round(nb / ms / 1e6, 1), "frac_of_hbm": round(nb / ms / 1e6 / hbm_peak, 4),
+            "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": nb, "copies": copies}
 
 
 def run_ours(args):
@@ -223,128 +465,76 @@ def run_ours(args):
     efg.set_weight_prefetch(True)  # static weights: stream them during the previous kernel's tail
     hbm_peak, peak_kind = peaks()
     bf16_peak = bf16_peak_tflops()
-    nbytes = algo_bytes(Q8_0, ROWS, COLS)
-
-    Ws = make_weights(efg, torch, Q8_0, ROWS, COLS, N_COPIES, seed=1 + rank)
-    x = torch.randn(COLS, generator=torch.Generator(device="cuda").manual_seed(2), device="cuda")
-    y = torch.empty(ROWS, device="cuda")
-    g_full, g_rem, chunk = time_steps(efg, torch, Q8_0, Ws, x, y, ROWS, COLS, args.steps, args.warmup)
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record()
-        for _ in range(args.steps // chunk):
-            g_full.replay()
-        if g_rem is not None:
-            g_rem.replay()
-        end.record()
-        torch.cuda.synchronize()
-    barrier()
-    ms = start.elapsed_time(end)
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / args.steps
-    value = nbytes * world * args.steps / (ms / 1e3) / 1e9
-    achieved = nbytes / (ms_step / 1e3) / 1e9  # per launch, one GPU
+    # Extras run first; besides their own figures they bring the GPU to its working clocks
+    # before the headline's timed region.
+    extra = {}
+    if world == 1:
+        extra["config1_q8_0_matvec_32000x2048"] = config1_extra(torch, efg, hbm_peak)
+        extra["config0_q4_0_matvec_5632x2048"] = config0_extra(torch, efg, hbm_peak)
+        if not args.no_decode:
+            extra["config2_decode_tinyllama"] = decode_extra(hbm_peak, with_cpu=not args.no_cpu_baseline)
+        if not args.no_gemm:
+            extra["config3_gemm_q4_0"] = gemm_extra(torch, efg, bf16_peak)
+            extra["config1_quantize_round_trip"] = quant_extra(torch, efg, hbm_peak)
+    if not args.no_sharded:
+        extra["lm_head_sharded_argmax_32000x2048"] = lm_head_extra(torch, efg, world, rank, barrier)
 
-    # ---- e2e: the host-pointer C-ABI call, pinned x in and y out every step
-    x_h = torch.empty(COLS, dtype=torch.float32).pin_memory().numpy()
-    y_h = torch.empty(ROWS, dtype=torch.float32).pin_memory().numpy()
-    x_h[:] = x.cpu().numpy()
-    Wh = Ws[0].cpu().numpy()
-    Whs = [Wh.copy() for _ in range(N_COPIES)]
-    for w in Whs:  # like a model load: each weight copy is registered (uploaded) once
-        efg.host_register_weights(w)
-    for i in range(args.warmup):
-        efg.host_matvec(Q8_0, Whs[i % N_COPIES], x_h, ROWS, y=y_h)
-    barrier()
-    e2e_steps = max(args.steps, 1)
-    t0 = time.perf_counter()
-    for i in range(e2e_steps):
-        efg.host_matvec(Q8_0, Whs[i % N_COPIES], x_h, ROWS, y=y_h)
-    el = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([el], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        el = float(t.item())
-    e2e = nbytes * world * e2e_steps / el / 1e9
-    efg.host_release_weights()
-    assert efg.device_error() == 0
-
-    # ---- extra: the Q4_0 matvec at TinyLlama gate_proj shape (config 0), same protocol
-    q4_rows, q4_cols = 5632, 2048
-    q4_copies = 64  # 64 x 6.5 MB = 415 MB in rotation
-    W4 = make_weights(efg, torch, Q4_0, q4_rows, q4_cols, q4_copies, seed=3)
-    y4 = torch.empty(q4_rows, device="cuda")
-    k4 = 1280  # kept well below the headline's launch count so the Q8_0 kernel dominates
-    g4, _, c4 = time_steps(efg, torch, Q4_0, W4, x, y4, q4_rows, q4_cols, k4, 64, chunk=640)
-    torch.cuda.synchronize()
-    s4, e4 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s4.record()
-    for _ in range(k4 // c4):
-        g4.replay()
-    e4.record()
-    torch.cuda.synchronize()
-    ms4 = s4.elapsed_time(e4) / k4
-    gbs4 = algo_bytes(Q4_0, q4_rows, q4_cols) / (ms4 / 1e3) / 1e9
-    del W4
-
-    dec = decode_extra(hbm_peak, with_cpu=not args.no_cpu_baseline) if world == 1 and not args.no_decode else None
-    shard = None if args.no_sharded else sharded_extra(torch, efg, world, rank, hbm_peak)
-    lmh = None if args.no_sharded else lm_head_extra(torch, efg, world, rank)
-    gemm = gemm_extra(torch, efg, bf16_peak) if world == 1 and not args.no_gemm else None
-    quant = quant_extra(torch, efg, hbm_peak) if world == 1 and not args.no_gemm else None
+    h = config4_headline(torch, efg, args, world, rank, local, hbm_peak, barrier)
+    ms_step = h["ms"] / args.steps
+    value = h["total"] * args.steps / (h["ms"] / 1e3) / 1e9
+    ms_local = h["ms_local"] / args.steps
+    achieved = h["local_bytes"] / (ms_local / 1e3) / 1e9  # the local matvec kernel, per launch
+    e2e = h["total"] * args.steps / h["el_e2e"] / 1e9
 
     # DRAM bytes per launch of this kernel from the committed ncu capture summary
     traffic = None
-    tpath = ROOT / "profiles" / "matvec_q8_0_32000x2048.json"
+    tpath = ROOT / "profiles" / "matvec_q4_0_config4.json"
     if tpath.exists():
-        traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+        tr = json.loads(tpath.read_text())
+        traffic = tr.get("dram_bytes_per_launch_scaled", {}).get(str(h["rows_per_rank"]))
 
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu_baseline and (ROOT / "oracle" / "_ref" / "libefref.so").exists():
-            gbs_c, thr, n_c, el_c = cpu_reference_matvec(args.cpu_seconds)
-            cpu = {"value": round(gbs_c, 3), "unit": "GB/s", "cores": thr, "kind": "reference",
-                   "sample": f"{n_c} matvecs ({el_c:.1f} s) of the reference AVX2 kernel + ThreadPool({thr}) "
-                             f"on config 1, {N_COPIES} rotating W copies"}
+            gbs_c, thr, n_c, el_c = cpu_reference_matvec(Q4_0, [h["W_host"].reshape(ROWS4, -1)], h["x_host"],
+                                                         ROWS4, COLS4, seconds=args.cpu_seconds)
+            cpu = dict(value=round(gbs_c, 3), unit="GB/s", kind="reference", **cpu_info(thr),
+                       sample=f"{n_c} matvecs ({el_c:.1f} s) of the whole 604 MB config-4 matrix by the reference "
+                              f"AVX2 kernel + ThreadPool({thr})")
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32 (Q8_0 weights)", "data": "synthetic (seeded N(0,0.02) W, N(0,1) x)",
-            "config": {"workload": "config1_q8_0_matvec_32000x2048", "rows": ROWS, "cols": COLS,
-                       "copies": N_COPIES, "l2": "inputs larger than L2: 6 rotating W copies (418 MB)",
-                       "launch": "CUDA graph of C-ABI launches with early weight prefetch (PDL)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 (Q4_0 weights)", "data": "synthetic (seeded N(0,0.02) W, N(0,1) x)",
+            "config": {"workload": "config4_q4_0_matvec_131072x8192", "rows": ROWS4, "cols": COLS4,
+                       "rows_per_rank": h["rows_per_rank"], "copies_per_rank": h["copies"],
+                       "l2": f"inputs larger than L2: {h['copies']} rotating copies of each rank's shard "
+                             f"({h['copies'] * h['rows_per_rank'] * COLS4 // 32 * 18 / 1e6:.0f} MB)",
+                       "launch": "CUDA graphs of C-ABI calls, weight prefetch on (PDL)",
+                       "gather": h["gather"],
+                       "parallelism": f"row-sharded x{world}" if world > 1 else "single GPU"},
+            "verified": h["verified"],
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": nbytes},
+                         "algorithmic_bytes_per_launch": h["local_bytes"],
+                         "kernel": "local Q4_0 matvec (integer tensor-core MMA), this rank's rows",
+                         "kernel_us": round(ms_local * 1e3, 3)},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * COLS,
-                    "d2h_bytes_per_step": 4 * ROWS,
-                    "api": "efg_host_matvec (host pointers; W registered resident once, like a model load)"},
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * COLS4,
+                    "d2h_bytes_per_step": 4 * ROWS4,
+                    "api": "efg_matvec_sharded (C ABI) with x copied in from and y read back to page-locked host "
+                           "memory every step"},
             "gpu_launches": args.steps,
-            "clocks": clocks.summary(),
-            "extra": {"config0_q4_0_matvec_5632x2048": {
-                "gbs": round(gbs4, 1), "frac_of_hbm": round(gbs4 / hbm_peak, 4), "us_per_launch": round(ms4 * 1e3, 3),
-                "bytes_per_launch": algo_bytes(Q4_0, q4_rows, q4_cols), "copies": q4_copies},
-                "config2_decode_tinyllama": dec,
-                "config4_sharded_q4_0_131072x8192": shard,
-                "lm_head_sharded_argmax_32000x2048": lmh,
-                "config3_gemm_q4_0": gemm,
-                "config1_quantize_round_trip": quant},
+            "clocks": h["clocks"],
+            "extra": extra,
         }
         emit(line)
     if world > 1:
-        del g_full, g_rem
         torch.distributed.destroy_process_group()
     return 0
 
@@ -433,69 +623,12 @@ def decode_extra(hbm_peak, with_cpu, prompt_len=23, steps=32, reps=5):
     return out
 
 
-def sharded_extra(torch, efg, world, rank, hbm_peak, steps=200, warmup=10, rows=131072, cols=8192):
-    """Config 4: the Q4_0 131072 x 8192 matvec (604 MB) row-sharded over the job's GPUs, y
-    all-gathered over NVLink every step (efg_matvec_sharded). Strong scaling: the matrix is
-    fixed, each rank holds rows/world of it. Device time of `steps` steps, max over ranks."""
-    b, c = efg.shard_rows(rows, world, rank)
-    rb = cols // 32 * 18
-    W = torch.empty(max(c, 1) * rb, dtype=torch.uint8, device="cuda")
-    g = torch.Generator(device="cuda").manual_seed(100 + rank)
-    for r0 in range(0, c, 8192):  # quantize the shard in 8192-row pieces (bounded FP32 temp)
-        n = min(8192, c - r0)
-        X = torch.randn(n, cols, generator=g, device="cuda") * 0.02
-        efg.quantize_rows(Q4_0, X, n, cols, W[r0 * rb:], True)
-    del X
-    x = torch.randn(cols, generator=torch.Generator(device="cuda").manual_seed(5), device="cuda")
-    y = torch.empty(rows, device="cuda")
-    comm = efg.Comm.from_torch() if world > 1 else efg.Comm(efg.Comm.unique_id(), 1, 0)
-
-    def timed(fn, n):
-        for _ in range(warmup):
-            fn()
-        if world > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(n):
-            fn()
-        s1.record()
-        torch.cuda.synchronize()
-        ms = s0.elapsed_time(s1)
-        if world > 1:
-            t = torch.tensor([ms], device="cuda")
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms / n
-
-    ms_all = timed(lambda: efg.matvec_sharded(Q4_0, y, W, x, rows, cols, comm), steps)
-    ms_local = timed(lambda: efg.matvec(Q4_0, y[b:], W, x, c, cols), steps)
-    efg.set_q4_mma(False)  # the same local matvec on the CUDA-core kernel, for comparison
-    try:
-        ms_local_cc = timed(lambda: efg.matvec(Q4_0, y[b:], W, x, c, cols), steps)
-    finally:
-        efg.set_q4_mma(True)
-    comm.close()
-    assert efg.device_error() == 0
-    total = rows * rb + 4 * cols + 4 * rows
-    shard_bytes = c * rb + 4 * cols + 4 * c
-    del W
-    return {"us_per_step": round(ms_all * 1e3, 3), "gbs_total": round(total / (ms_all / 1e3) / 1e9, 1),
-            "local_matvec_us": round(ms_local * 1e3, 3),
-            "local_frac_of_hbm": round(shard_bytes / (ms_local / 1e3) / 1e9 / hbm_peak, 4),
-            "local_kernel": "int8 tensor-core MMA (efg_matvec_mma.cu)",
-            "local_matvec_us_cuda_cores": round(ms_local_cc * 1e3, 3),
-            "local_frac_of_hbm_cuda_cores": round(shard_bytes / (ms_local_cc / 1e3) / 1e9 / hbm_peak, 4),
-            "gather_bytes": 4 * rows, "ranks": world, "rows_per_rank": c, "matrix_bytes": rows * rb,
-            "scaling": "strong"}
-
-
-def lm_head_extra(torch, efg, world, rank, steps=200, warmup=10, rows=32000, cols=2048):
+def lm_head_extra(torch, efg, world, rank, barrier, steps=200, warmup=10, rows=32000, cols=2048):
     """The decode step's last operation with lm_head (Q8_0 32000 x 2048) row-sharded over the
     job's GPUs: this rank's logits with the final RMSNorm fused, then the argmax over all
-    ranks (efg_lm_head_argmax_sharded: one 8-byte-per-rank all-gather). Device time per call,
-    max over ranks; strong scaling."""
+    ranks (efg_lm_head_argmax_sharded). Device time per call (CUDA graphs, max over ranks;
+    strong scaling). Verified: the token on every rank equals the argmax of all ranks'
+    logits gathered afterwards."""
     b, c = efg.shard_rows(rows, world, rank)
     rb = cols // 32 * 34
     g = torch.Generator(device="cuda").manual_seed(200)
@@ -510,26 +643,38 @@ def lm_head_extra(torch, efg, world, rank, steps=200, warmup=10, rows=32000, col
     logits = torch.empty(max(c, 1), device="cuda")
     tok = torch.empty(1, dtype=torch.int32, device="cuda")
     comm = efg.Comm.from_torch() if world > 1 else efg.Comm(efg.Comm.unique_id(), 1, 0)
-    for _ in range(warmup):
-        efg.lm_head_argmax_sharded(Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s0.record()
-    for _ in range(steps):
-        efg.lm_head_argmax_sharded(Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
-    s1.record()
-    torch.cuda.synchronize()
-    ms = s0.elapsed_time(s1) / steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    comm.close()
-    assert efg.device_error() == 0
+    try:
+        def step(i):
+            efg.lm_head_argmax_sharded(Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
+
+        gf, gr, ch = graphs_of(torch, step, steps, warmup)
+        gf.replay()
+        ms = replay_timed(torch, gf, gr, ch, steps, barrier, world) / steps
+        del gf, gr
+        tok.fill_(-1)
+        step(0)
+        torch.cuda.synchronize()
+        if world > 1 and rows % world == 0:
+            full = torch.empty(rows, device="cuda")
+            torch.distributed.all_gather_into_tensor(full, logits[:c].contiguous())
+        elif world > 1:
+            parts = [torch.empty(efg.shard_rows(rows, world, r)[1], device="cuda") for r in range(world)]
+            torch.distributed.all_gather(parts, logits[:c].contiguous())
+            full = torch.cat(parts)
+        else:
+            full = logits[:c]
+        want = efg.argmax(full)
+        torch.cuda.synchronize()
+        ok = int(tok.item()) == int(want.item())
+        if world > 1:
+            t = torch.tensor([1 if ok else 0], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+            ok = bool(t.item() == 1)
+        assert efg.device_error() == 0
+    finally:
+        comm.close()
     return {"us_per_call": round(ms * 1e3, 3), "ranks": world, "rows_per_rank": c, "token": int(tok.item()),
-            "scaling": "strong"}
+            "verified": ok, "scaling": "strong"}
 
 
 def quant_extra(torch, efg, hbm_peak, reps=5):
@@ -685,7 +830,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode measurement")
-    ap.add_argument("--no-sharded", action="store_true", help="skip the config-4 sharded matvec measurement")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the row-sharded lm_head extra")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-3 GEMM measurement")
     ap.add_argument("--profile", choices=["q8", "q4", "q4big", "gemm", "decode", "decode_persistent", "prefill", "batch"],
                     help="a few plain launches for ncu")

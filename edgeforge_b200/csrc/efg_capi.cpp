@@ -107,7 +107,25 @@ int host_stream(HostCtx* h) {
   return EFG_OK;
 }
 
-// Device address of page-locked host memory (null for pageable memory): kernels can store
+using PointerAttrFn = CUresult (*)(void*, CUpointer_attribute, CUdeviceptr);
+
+// cuPointerGetAttribute from the driver, looked up once (the library links the CUDA
+// runtime statically and has no link-time dependency on libcuda).
+PointerAttrFn pointer_attr_fn() {
+  static const PointerAttrFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuPointerGetAttribute", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PointerAttrFn>(f);
+  }();
+  return fn;
+}
+
+// Device address of page-locked host memory that the device may write (null for pageable
+// memory, and for page-locked memory whose access flags the driver does not report as
+// read-write, e.g. a range registered with cudaHostRegisterReadOnly): kernels can store
 // into it directly over the bus.
 void* mapped_host(void* p) {
   cudaPointerAttributes a{};
@@ -115,7 +133,13 @@ void* mapped_host(void* p) {
     cudaGetLastError();
     return nullptr;
   }
-  return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+  if (a.type != cudaMemoryTypeHost || !a.devicePointer) return nullptr;
+  const PointerAttrFn fn = pointer_attr_fn();
+  unsigned int flags = 0;
+  if (!fn || fn(&flags, CU_POINTER_ATTRIBUTE_ACCESS_FLAGS, reinterpret_cast<CUdeviceptr>(a.devicePointer)) !=
+                 CUDA_SUCCESS)
+    return nullptr;
+  return flags == CU_POINTER_ATTRIBUTE_ACCESS_FLAG_READWRITE ? a.devicePointer : nullptr;
 }
 
 }  // namespace

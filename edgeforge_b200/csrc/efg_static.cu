@@ -15,8 +15,9 @@
 //   then x (cols floats), y (rows floats), W (rows packed rows), each 256-byte aligned.
 // Every byte of x, y and W is written before it is read in the same call, so nothing
 // else must start at zero. A call whose x, y and W do not fit is rejected (EFG_EINVAL).
-// Calls that overlap in time (from several host threads, or on several devices of one
-// process sharing a thread) race on the one area; callers serialize them.
+// Each device that loads the library holds its own copy of the area. Calls that overlap
+// in time on the same device (from several host threads) race on that device's copy;
+// callers serialize them. Calls on different devices do not share storage.
 #include <cstdint>
 #include <mutex>
 

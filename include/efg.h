@@ -153,7 +153,8 @@ int efg_row_f32(float* d_out, int qtype, const uint8_t* d_W, size_t rows, size_t
  * load); otherwise it is uploaded on every call, so a caller that rewrites its buffer
  * between calls always gets results for the current bytes. A page-locked y (cudaHostAlloc,
  * cudaHostRegister, torch pin_memory) is written by the matvec kernel's own stores over the
- * bus, saving a separate device-to-host copy per call; pageable y is copied after it.
+ * bus, saving a separate device-to-host copy per call; pageable y, and page-locked y that
+ * the device may not write (registered with cudaHostRegisterReadOnly), is copied after it.
  */
 int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols);
 int efg_host_quantize_row(int qtype, const float* x, size_t n, void* out, int search);
@@ -169,7 +170,8 @@ int efg_host_release_weights(void);
 /* efg_host_matvec without device allocation: x, y and W are staged through one static
  * 8 MiB device area (its address taken once per device by the first call, which must come
  * before any stream capture); calls needing more than the area are rejected (EFG_EINVAL).
- * Overlapping calls race on the area and must be serialized by the caller. This entry
+ * Every device has its own copy of the area: calls that overlap on the same device race on
+ * it and must be serialized by the caller; calls on different devices do not. This entry
  * point has no reference counterpart: the reference's kern::matvec_q4_0/q8_0 allocate
  * nothing because they run on host memory. */
 int efg_host_matvec_static(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols);

@@ -490,6 +490,29 @@ void efo_exact_dot(int qtype, const uint8_t* row, const float* x, size_t n, doub
   *mag = m;
 }
 
+typedef struct {
+  int qtype;
+  const uint8_t* W;
+  const float* x;
+  size_t cols, rb;
+  double *exact, *mag;
+} exact_ctx;
+
+static void exact_range(void* vc, size_t b, size_t e) {
+  const exact_ctx* c = (const exact_ctx*)vc;
+  for (size_t r = b; r < e; ++r) efo_exact_dot(c->qtype, c->W + r * c->rb, c->x, c->cols, &c->exact[r], &c->mag[r]);
+}
+
+int efo_exact_dots(int qtype, const uint8_t* W, const float* x, size_t rows, size_t cols, double* exact, double* mag,
+                   int threads) {
+  int ok = 0;
+  const uint64_t rb = efo_row_bytes(qtype, cols, &ok);
+  if (!ok) return -1;
+  exact_ctx c = {qtype, W, x, cols, (size_t)rb, exact, mag};
+  parallel_rows(rows, threads, exact_range, &c);
+  return 0;
+}
+
 double efo_rel_dot_error(int qtype, const uint8_t* row, const float* x, size_t n, float got) {
   double exact, mag;
   efo_exact_dot(qtype, row, x, n, &exact, &mag);

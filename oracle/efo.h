@@ -65,6 +65,10 @@ void efo_matvec_mt(int qtype, float* y, const uint8_t* W, const float* x, size_t
 double efo_rel_dot_error(int qtype, const uint8_t* row, const float* x, size_t n, float got);
 /* Exact (double) dot of a dequantized row with x and its magnitude sum|w x|. */
 void efo_exact_dot(int qtype, const uint8_t* row, const float* x, size_t n, double* exact, double* mag);
+/* efo_exact_dot for every row of a packed [rows][cols] matrix, rows split over `threads`
+ * POSIX threads. Returns -1 when cols is not a multiple of 32. */
+int efo_exact_dots(int qtype, const uint8_t* W, const float* x, size_t rows, size_t cols, double* exact, double* mag,
+                   int threads);
 
 /* ---- FP32 transformer ops (src/kernels.cpp) ----------------------------- */
 float efo_dot_f32(const float* a, const float* b, size_t n);                             /* :28-47 */

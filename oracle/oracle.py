@@ -21,6 +21,30 @@ HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libefref.so"
 
+
+def reference_tree() -> Path | None:
+    """The reference's source tree, when this machine has it: $EFG_REF_TREE, else the
+    `reference_path` that the benchmark's BASELINE.json at the repository root names.
+    None when neither points at a tree holding src/quant.cpp (as on a GPU box, which runs
+    the prebuilt oracle/_ref library instead)."""
+    cands = []
+    if os.environ.get("EFG_REF_TREE"):
+        cands.append(Path(os.environ["EFG_REF_TREE"]))
+    base = HERE.parent / "BASELINE.json"
+    if base.exists():
+        import json
+
+        try:
+            rp = json.loads(base.read_text()).get("reference_path")
+        except ValueError:
+            rp = None
+        if rp:
+            cands.append(Path(rp))
+    for c in cands:
+        if (c / "src" / "quant.cpp").exists():
+            return c
+    return None
+
 F32, F16, BF16, Q8_0, Q4_0 = 0, 1, 2, 3, 4
 BLOCK_BYTES = {Q4_0: 18, Q8_0: 34}
 
@@ -162,6 +186,8 @@ class Oracle(_Lib):
         self._mvmt = self._fn("matvec_mt", None, C.c_int, _fp, _u8, _fp, _sz, _sz, C.c_int)
         self._exact = self._fn("exact_dot", None, C.c_int, _u8, _fp, _sz,
                                C.POINTER(C.c_double), C.POINTER(C.c_double))
+        self._exact_rows = self._fn("exact_dots", C.c_int, C.c_int, _u8, _fp, _sz, _sz,
+                                    C.POINTER(C.c_double), C.POINTER(C.c_double), C.c_int)
 
     def quantize_rows(self, qtype, X, search=True, threads=os.cpu_count() or 1):
         X = np.ascontiguousarray(X, dtype=np.float32)
@@ -192,10 +218,14 @@ class Oracle(_Lib):
         x = np.ascontiguousarray(x, dtype=np.float32)
         ex = np.zeros(rows)
         mag = np.zeros(rows)
-        e, m = C.c_double(), C.c_double()
-        for r in range(rows):
-            self._exact(qtype, _p(W[r], _u8), _p(x, _fp), x.size, C.byref(e), C.byref(m))
-            ex[r], mag[r] = e.value, m.value
+        if rows and W.shape[1] != row_bytes(qtype, x.size):
+            raise ValueError(f"rows of {W.shape[1]} bytes do not hold {x.size} weights")
+        if rows:
+            threads = min(os.cpu_count() or 1, max(1, rows * x.size // (1 << 20)))
+            rc = self._exact_rows(qtype, _p(W, _u8), _p(x, _fp), rows, x.size, _p(ex, C.POINTER(C.c_double)),
+                                  _p(mag, C.POINTER(C.c_double)), threads)
+            if rc != 0:
+                raise ValueError(f"cols={x.size} is not a multiple of 32")
         return ex, mag
 
 

@@ -37,10 +37,11 @@ def oracle():
 @pytest.fixture(scope="session")
 def reference():
     """The reference implementation compiled from its own sources, if it was built."""
-    from oracle.oracle import REF_SO, Reference
+    from oracle.oracle import REF_SO, Reference, reference_tree
 
-    if not REF_SO.exists() and Path("/root/reference/src/quant.cpp").exists():
-        _make(ROOT / "oracle", REF_SO)
+    tree = reference_tree()
+    if not REF_SO.exists() and tree is not None:
+        subprocess.run(["make", "-C", str(ROOT / "oracle"), "-j8", f"REF={tree}"], check=True, capture_output=True)
     if not REF_SO.exists():
         pytest.skip("oracle/_ref/libefref.so not built (reference sources absent)")
     return Reference()

@@ -26,7 +26,7 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
 sys.path.insert(0, str(ROOT))
 
-from oracle.oracle import Q4_0, Q8_0, Reference, row_bytes  # noqa: E402
+from oracle.oracle import Q4_0, Q8_0, Reference, reference_tree, row_bytes  # noqa: E402
 
 
 def f32_from_bits(u):
@@ -72,8 +72,13 @@ def random_rows(qtype, rows, cols, rng) -> np.ndarray:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-tree", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--ref-tree", type=Path, default=None,
+                    help="reference source tree (default: $EFG_REF_TREE or BASELINE.json's reference_path)")
     args = ap.parse_args()
+    if args.ref_tree is None:
+        args.ref_tree = reference_tree()
+    if args.ref_tree is None:
+        ap.error("no reference source tree: pass --ref-tree or set EFG_REF_TREE")
     ref = Reference()
     rng = np.random.default_rng(20261201)
     manifest = {"generator": "tests/golden/make_golden.py", "reference": "oracle/_ref/libefref.so", "files": {}}

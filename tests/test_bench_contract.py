@@ -22,11 +22,13 @@ def test_reference_arm_prints_one_contract_line():
     assert len(lines) == 1
     d = json.loads(lines[0])
     assert d["impl"] == "reference"
-    assert d["metric"] == "Q8_0 matvec HBM GB/s (lm_head 32000x2048)" and d["unit"] == "GB/s"
+    assert d["metric"] == "Q4_0 matvec HBM GB/s (config 4: 131072x8192, row-sharded over the job's GPUs)"
+    assert d["unit"] == "GB/s"
     assert d["n_gpus"] == 1 and d["steps"] == 2 and d["warmup"] == 3 and d["higher_is_better"] is True
     assert d["value"] > 0 and d["ms_per_step"] > 0
-    assert d["config"]["workload"] == "config1_q8_0_matvec_32000x2048"
+    assert d["config"]["workload"] == "config4_q4_0_matvec_131072x8192"
     cb = d["cpu_baseline"]
     assert cb["kind"] == "reference" and cb["value"] == d["value"] and cb["cores"] >= 1
+    assert cb["physical_cores"] is None or 1 <= cb["physical_cores"] <= cb["logical_cpus"]
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0

@@ -240,3 +240,54 @@ def test_host_matvec_pinned_buffers_reused(efg_lib, cuda, oracle):
     assert rel_dot_errors(oracle, Q8_0, W, x, 700, y).max() < TOL
     efg_lib.host_release_weights()
     assert efg_lib.device_error() == 0
+
+
+@pytest.mark.parametrize("n", [32, 64, 96, 2048, 5632])
+@pytest.mark.parametrize("qt", [Q4_0, Q8_0])
+def test_dot_golden_vectors(efg_lib, cuda, oracle, n, qt):
+    """efg_dot_q4_0 / efg_dot_q8_0 (kern::dot_q4_0 / dot_q8_0, include/ef/qkernels.h:47-48)
+    on each golden row: within 1e-5 of sum|w x|, and equal to the matvec's row result."""
+    import torch
+
+    g = golden("matvec.npz")
+    name = "q4" if qt == Q4_0 else "q8"
+    W, x = g[f"{name}_W_{n}"], g[f"x_{n}"]
+    y = run_matvec(efg_lib, cuda, qt, W, x, 24)
+    dx = dev(x.astype(np.float32), cuda)
+    out = torch.full((1,), float("nan"), device=cuda)
+    fn = efg_lib.dot_q4_0 if qt == Q4_0 else efg_lib.dot_q8_0
+    for r in range(W.shape[0]):
+        fn(out, dev(W[r], cuda), dx, n)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        assert rel_dot_errors(oracle, qt, W[r:r + 1], x, 1, got).max() < TOL
+        assert got[0] == y[r]
+
+
+def test_dot_hand_blocks(efg_lib, cuda):
+    """Hand-built blocks of the reference's tests (test_qinfer.cpp:100-122): exact answers."""
+    import torch
+
+    x = np.ones(32, np.float32)
+    q8 = np.zeros(34, np.uint8)
+    q8[0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+    q8[2:34] = np.array([127, 256 - 127] * 16, np.uint8)  # +-127 cancel
+    out = torch.full((1,), float("nan"), device=cuda)
+    efg_lib.dot_q8_0(out, dev(q8, cuda), dev(x, cuda), 32)
+    torch.cuda.synchronize()
+    assert out.item() == 0.0
+    q8[2:34] = 0
+    q8[2] = 3  # a single code 3 with d = 1
+    efg_lib.dot_q8_0(out, dev(q8, cuda), dev(x, cuda), 32)
+    torch.cuda.synchronize()
+    assert out.item() == 3.0
+    q4 = np.zeros(18, np.uint8)
+    q4[0:2] = np.frombuffer(np.float16(0.5).tobytes(), np.uint8)
+    q4[2:18] = 0x88  # every code 8 -> weight 0
+    q4[2] = 0x8A     # code 10 at column 0 -> 2 * 0.5
+    efg_lib.dot_q4_0(out, dev(q4, cuda), dev(x, cuda), 32)
+    torch.cuda.synchronize()
+    assert out.item() == 1.0
+    efg_lib.dot_q4_0(out, dev(q4, cuda), dev(x, cuda), 0)  # n = 0: a sum over no blocks is 0
+    torch.cuda.synchronize()
+    assert out.item() == 0.0

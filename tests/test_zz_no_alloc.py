@@ -19,8 +19,12 @@ def _case(qt, rows, cols, seed):
 
 
 @pytest.mark.parametrize("qt,rows,cols", [(QType.Q4_0, 5632, 2048), (QType.Q8_0, 1000, 2048), (QType.Q4_0, 37, 96)])
-def test_static_matches_host_matvec_twice(qt, rows, cols):
+def test_static_matches_host_matvec_twice(qt, rows, cols, oracle):
+    """Two calls in a row with different inputs: each result equals efg_host_matvec's bit
+    for bit and is within the reference's 1e-5 of sum|w x| of the exact dot."""
     import torch
+
+    from conftest import rel_dot_errors
 
     for call, seed in enumerate((1, 2)):  # two calls in a row, different inputs
         W, x = _case(qt, rows, cols, seed)
@@ -31,6 +35,8 @@ def test_static_matches_host_matvec_twice(qt, rows, cols):
         np.testing.assert_array_equal(got, want)
         if call == 1:
             assert torch.cuda.mem_get_info(0)[0] == free0  # nothing allocated by the call
+        err = rel_dot_errors(oracle, qt, W.reshape(rows, -1), x, rows, got)
+        assert err.max() <= 1e-5, err.max()
     assert efg.device_error() == 0
 
 
