@@ -293,6 +293,32 @@ def replay_timed(torch, g_full, g_rem, chunk, steps, barrier, world, clocks=None
     return ms
 
 
+def time_calls(torch, fn, steps, warmup, barrier, world):
+    """ms per call of fn(i): CUDA graphs of the calls when they can be captured, otherwise
+    (a library that refuses capture) the same calls launched one by one; max over ranks."""
+    try:
+        gf, gr, ch = graphs_of(torch, fn, steps, warmup)
+    except Exception:  # noqa: BLE001 - measured eagerly instead
+        torch.cuda.synchronize()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for i in range(steps):
+            fn(i)
+        s1.record()
+        torch.cuda.synchronize()
+        ms = s0.elapsed_time(s1)
+        if world > 1:
+            t = torch.tensor([ms], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms / steps
+    gf.replay()
+    ms = replay_timed(torch, gf, gr, ch, steps, barrier, world) / steps
+    del gf, gr
+    return ms
+
+
 class _Null:
     def __enter__(self):
         return self
@@ -320,8 +346,24 @@ def config4_headline(torch, efg, args, world, rank, local, hbm_peak, barrier):
     x = torch.randn(COLS4, generator=torch.Generator(device="cuda").manual_seed(5), device="cuda")
     y = torch.empty(ROWS4, device="cuda")
     comm = efg.Comm.from_torch() if world > 1 else efg.Comm(efg.Comm.unique_id(), 1, 0)
-    gather = "none (one rank)" if world == 1 else "ncclAllGather in place"
+    gather = "none (one rank)"
+    ms_nccl = None
+    registered = False
     try:
+        if world > 1:
+            # the same step with y not registered: the slices go through ncclAllGather (for
+            # comparison; device time of CUDA graphs of the calls)
+            y_n = torch.empty(ROWS4, device="cuda")
+            ms_nccl = time_calls(torch, lambda i: efg.matvec_sharded(Q4_0, y_n, Ws[i % copies], x, ROWS4, COLS4, comm),
+                                 args.steps, args.warmup, barrier, world)
+            del y_n
+            try:
+                comm.register(y)
+                registered = True
+                gather = "in-kernel: every CTA stores its rows into each peer's y over NVLink (efg_comm_register)"
+            except efg.EdgeForgeError as e:  # every rank gets the same outcome
+                gather = f"ncclAllGather in place (registration failed: {e})"
+
         def step(i):
             efg.matvec_sharded(Q4_0, y, Ws[i % copies], x, ROWS4, COLS4, comm)
 
@@ -383,10 +425,13 @@ def config4_headline(torch, efg, args, world, rank, local, hbm_peak, barrier):
             el = float(t.item())
         assert efg.device_error() == 0
     finally:
+        if registered:
+            comm.deregister(y)
         comm.close()
     total = algo_bytes(Q4_0, ROWS4, COLS4)
     local_bytes = shard_bytes + 4 * COLS4 + 4 * c
     return {"ms": ms, "ms_local": ms_local, "el_e2e": el, "total": total, "local_bytes": local_bytes,
+            "ms_nccl": ms_nccl,
             "rows_per_rank": c, "copies": copies, "verified": ok, "gather": gather, "clocks": clocks.summary(),
             "W_host": Ws[0].cpu().numpy() if (world == 1 and not args.no_cpu_baseline) else None,
             "x_host": x.cpu().numpy()}
@@ -519,6 +564,8 @@ def run_ours(args):
                        "gather": h["gather"],
                        "parallelism": f"row-sharded x{world}" if world > 1 else "single GPU"},
             "verified": h["verified"],
+            "sharded_step_us": {"this_run": round(ms_step * 1e3, 3), "local_matvec_alone": round(ms_local * 1e3, 3),
+                                "with_ncclAllGather": round(h["ms_nccl"] * 1e3, 3) if h["ms_nccl"] else None},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": h["local_bytes"],
@@ -647,10 +694,7 @@ def lm_head_extra(torch, efg, world, rank, barrier, steps=200, warmup=10, rows=3
         def step(i):
             efg.lm_head_argmax_sharded(Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
 
-        gf, gr, ch = graphs_of(torch, step, steps, warmup)
-        gf.replay()
-        ms = replay_timed(torch, gf, gr, ch, steps, barrier, world) / steps
-        del gf, gr
+        ms = time_calls(torch, step, steps, warmup, barrier, world)
         tok.fill_(-1)
         step(0)
         torch.cuda.synchronize()

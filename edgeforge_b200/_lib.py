@@ -78,6 +78,8 @@ SIGNATURES = {
     "efg_comm_unique_id": (_i, [_vp]),
     "efg_comm_init": (_i, [_vp, _i, _i, C.POINTER(_vp)]),
     "efg_comm_destroy": (_i, [_vp]),
+    "efg_comm_register": (_i, [_vp, _vp, _sz]),
+    "efg_comm_deregister": (_i, [_vp, _vp]),
     "efg_matvec_sharded": (_i, [_i, _vp, _vp, _vp, _sz, _sz, _vp, _vp]),
     "efg_argmax": (_i, [_vp, _sz, _vp, _vp]),
     "efg_lm_head_argmax_sharded": (_i, [C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_float, _sz, _sz, _vp, _vp]),

@@ -274,6 +274,14 @@ class Comm:
     def handle(self) -> C.c_void_p:
         return self._h
 
+    def register(self, buf) -> None:
+        """efg_comm_register: every rank registers its own CUDA tensor of the same size, so
+        that efg_matvec_sharded into it moves the slices by the kernel's own peer stores."""
+        check(load().efg_comm_register(self._h, _ptr(buf), buf.numel() * buf.element_size()))
+
+    def deregister(self, buf) -> None:
+        check(load().efg_comm_deregister(self._h, _ptr(buf)))
+
     def close(self) -> None:
         if self._h:
             check(load().efg_comm_destroy(self._h))

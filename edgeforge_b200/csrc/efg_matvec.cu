@@ -32,6 +32,7 @@
 
 #include "efg_device.cuh"
 #include "efg_dot.cuh"
+#include "efg_gather.cuh"
 #include "efg_host.h"
 #include "efg_matvec.cuh"
 
@@ -53,6 +54,7 @@ struct KParams {
   uint32_t x_vec4;  // x and norm_w are 16-byte aligned: staged with float4 loads
   uint32_t job_tile_start[kMaxJobs + 1];
   MatvecJobDev jobs[kMaxJobs];
+  GatherDev g;  // the in-kernel all-gather of the row-sharded matvec (GATHER kernels only)
 };
 
 // Which job a tile belongs to, and its first row.
@@ -64,7 +66,7 @@ __device__ __forceinline__ void locate_tile(const KParams& p, uint32_t tile, uin
   nrows = min(p.TR, p.jobs[j].rows - r0);
 }
 
-template <Fmt F, int RB, Epi E, bool NORM>
+template <Fmt F, int RB, Epi E, bool NORM, bool GATHER>
 __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __grid_constant__ KParams p) {
   // A tile (one stage) holds TR = BPS * H * RB/n_mat rows of each matrix and is consumed
   // by one row group: G x H warps, G warps covering the 64-column slots of a row and H
@@ -176,6 +178,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
     }
   }
   pdl_wait();  // x and y belong to the previous kernel in the stream
+  uint32_t epoch = 0;
+  if constexpr (GATHER) {
+    epoch = gather_epoch(p.g);
+    if (blockIdx.x == 0 && tid == 0) gather_announce(p.g, epoch);
+  }
   double ss = 0.0;
   if (p.x_vec4) {
     const float4* x4 = reinterpret_cast<const float4*>(p.x);
@@ -269,6 +276,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
   // After a failed (timed-out) wait a warp stops reading and writing but keeps walking
   // its tiles, so the named barriers of its row group still see every warp.
   bool alive = true;
+  uint32_t ready = 0;  // gather: 0 = peers not checked yet, 1 = every peer ready, 2 = gave up
   uint32_t buf = 0, s = rg, phase = 0;
   for (uint32_t tile = blockIdx.x + rg * gridDim.x; tile < p.tiles_total; tile += p.RG * gridDim.x) {
     if (alive && !mbar_wait(&full[s], phase, p.err)) alive = false;
@@ -309,6 +317,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
         buf ^= 1u;
       }
       const uint32_t lr = b * batch_rows + h * RBH + lane;
+      if constexpr (GATHER) {
+        if (g == 0 && ready == 0) ready = gather_wait_ready(p.g, epoch, p.err) ? 1u : 2u;  // warp-uniform
+        if (writer && lr < nrows && alive && ready == 1) gather_store(p.g, r0 + lr, total);
+      }
       if constexpr (E == Epi::SwiGLU) {
         const float up = __shfl_down_sync(0xFFFFFFFFu, total, RBH);
         if (writer && lane < static_cast<int>(RBH) && lr < nrows) y[r0 + lr] = silu(total) * up;
@@ -325,20 +337,35 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
       phase ^= 1u;
     }
   }
+  if constexpr (GATHER) {
+    __threadfence_system();  // this thread's stores into peers' y, before the CTA is counted
+    named_barrier(kNormBarrier, nc * 32);
+    if (warp == 0) gather_finish(p.g, epoch, p.err);
+  }
 }
 
 // ------------------------------------------------------------------ generic path
 // Any cols % 32 == 0 and any pointer alignment: one warp per row, lanes stride over
 // blocks, bytes read one at a time. Used only for shapes the fast path rejects.
-template <Fmt F, Epi E>
+template <Fmt F, Epi E, bool GATHER>
 __global__ void matvec_generic_kernel(const __grid_constant__ KParams p) {
   pdl_wait();
   pdl_launch_dependents();
+  uint32_t epoch = 0;
+  if constexpr (GATHER) {
+    epoch = gather_epoch(p.g);
+    if (blockIdx.x == 0 && threadIdx.x == 0) gather_announce(p.g, epoch);
+  }
+  bool ready = true;
   constexpr uint32_t BB = F == Fmt::Q4 ? 18 : 34;
   const uint32_t nb = p.cols / 32;
   const int lane = threadIdx.x & 31;
   const uint32_t warps = gridDim.x * (blockDim.x / 32);
   // Work items are single rows here: job_tile_start holds row offsets.
+  if constexpr (GATHER) {
+    if (blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5) < p.tiles_total)
+      ready = gather_wait_ready(p.g, epoch, p.err);  // warps with rows, before their first store
+  }
   for (uint32_t t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); t < p.tiles_total; t += warps) {
     uint32_t j = 0;
     while (j + 1 < p.n_jobs && t >= p.job_tile_start[j + 1]) ++j;
@@ -369,7 +396,15 @@ __global__ void matvec_generic_kernel(const __grid_constant__ KParams p) {
       if constexpr (E == Epi::SwiGLU) y[r] = silu(sums[0]) * sums[1];
       else if constexpr (E == Epi::Add) y[r] += sums[0];
       else y[r] = sums[0];
+      if constexpr (GATHER) {
+        if (ready) gather_store(p.g, r, sums[0]);
+      }
     }
+  }
+  if constexpr (GATHER) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < 32) gather_finish(p.g, epoch, p.err);
   }
 }
 
@@ -384,7 +419,7 @@ using FastFn = void (*)(KParams);
 
 template <Fmt F, int RB, Epi E>
 FastFn pick_norm(bool norm) {
-  return norm ? matvec_fast_kernel<F, RB, E, true> : matvec_fast_kernel<F, RB, E, false>;
+  return norm ? matvec_fast_kernel<F, RB, E, true, false> : matvec_fast_kernel<F, RB, E, false, false>;
 }
 
 template <Fmt F, int RB>
@@ -408,20 +443,38 @@ FastFn pick_rb(int rb, Epi e, bool norm) {
   }
 }
 
-FastFn pick_fast(Fmt f, int rb, Epi e, bool norm) {
+// The gather kernels: one plain product (Store, no norm), any RB.
+template <Fmt F>
+FastFn pick_gather(int rb) {
+  switch (rb) {
+    case 1: return matvec_fast_kernel<F, 1, Epi::Store, false, true>;
+    case 2: return matvec_fast_kernel<F, 2, Epi::Store, false, true>;
+    default: return matvec_fast_kernel<F, 4, Epi::Store, false, true>;
+  }
+}
+
+FastFn pick_fast(Fmt f, int rb, Epi e, bool norm, bool gather) {
+  if (gather) {
+    if (e != Epi::Store || norm) return nullptr;
+    return f == Fmt::Q4 ? pick_gather<Fmt::Q4>(rb) : pick_gather<Fmt::Q8>(rb);
+  }
   return f == Fmt::Q4 ? pick_rb<Fmt::Q4>(rb, e, norm) : pick_rb<Fmt::Q8>(rb, e, norm);
 }
 
 using GenFn = void (*)(KParams);
-GenFn pick_generic(Fmt f, Epi e) {
-  if (f == Fmt::Q4) {
-    return e == Epi::Store ? matvec_generic_kernel<Fmt::Q4, Epi::Store>
-           : e == Epi::Add ? matvec_generic_kernel<Fmt::Q4, Epi::Add>
-                           : matvec_generic_kernel<Fmt::Q4, Epi::SwiGLU>;
+GenFn pick_generic(Fmt f, Epi e, bool gather) {
+  if (gather) {
+    if (e != Epi::Store) return nullptr;
+    return f == Fmt::Q4 ? matvec_generic_kernel<Fmt::Q4, Epi::Store, true> : matvec_generic_kernel<Fmt::Q8, Epi::Store, true>;
   }
-  return e == Epi::Store ? matvec_generic_kernel<Fmt::Q8, Epi::Store>
-         : e == Epi::Add ? matvec_generic_kernel<Fmt::Q8, Epi::Add>
-                         : matvec_generic_kernel<Fmt::Q8, Epi::SwiGLU>;
+  if (f == Fmt::Q4) {
+    return e == Epi::Store ? matvec_generic_kernel<Fmt::Q4, Epi::Store, false>
+           : e == Epi::Add ? matvec_generic_kernel<Fmt::Q4, Epi::Add, false>
+                           : matvec_generic_kernel<Fmt::Q4, Epi::SwiGLU, false>;
+  }
+  return e == Epi::Store ? matvec_generic_kernel<Fmt::Q8, Epi::Store, false>
+         : e == Epi::Add ? matvec_generic_kernel<Fmt::Q8, Epi::Add, false>
+                         : matvec_generic_kernel<Fmt::Q8, Epi::SwiGLU, false>;
 }
 
 struct Plan {
@@ -552,6 +605,12 @@ int launch_matvec_on(const MatvecArgs& a, const DeviceInfo& devinfo, int* d_err,
   k.cols = static_cast<uint32_t>(a.cols);
   k.n_jobs = static_cast<uint32_t>(a.epi == Epi::SwiGLU ? 1 : a.n_jobs);
   for (int j = 0; j < n_mat; ++j) k.jobs[j] = a.jobs[j];
+  k.g = a.gather;
+  if (a.gather.nranks > 0) {
+    if (a.gather.nranks > kMaxGatherRanks || a.epi != Epi::Store || a.norm_w || a.pos || a.n_jobs != 1 ||
+        a.cols == 0 || a.gather.rank < 0 || a.gather.rank >= a.gather.nranks)
+      return fail(EFG_EINVAL, "matvec: the in-kernel gather takes one plain product of cols > 0 rows");
+  }
 
   if (a.cols == 0) {  // every dot is over zero blocks: y = 0 (sum32 of zero lanes)
     for (int j = 0; j < (a.epi == Epi::SwiGLU ? 1 : a.n_jobs); ++j) {
@@ -595,7 +654,7 @@ int launch_matvec_on(const MatvecArgs& a, const DeviceInfo& devinfo, int* d_err,
     }
     k.job_tile_start[k.n_jobs] = t;
     k.tiles_total = t;
-    FastFn fn = pick_fast(a.fmt, static_cast<int>(pl.RB), a.epi, a.norm_w != nullptr);
+    FastFn fn = pick_fast(a.fmt, static_cast<int>(pl.RB), a.epi, a.norm_w != nullptr, k.g.nranks > 0);
     if (!fn) return fail(EFG_EINVAL, "matvec: no kernel for this configuration");
     if (direct_smem_attr) {
       EFG_TRY_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -630,7 +689,9 @@ int launch_matvec_on(const MatvecArgs& a, const DeviceInfo& devinfo, int* d_err,
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = a.pdl ? 1 : 0;
-  EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, pick_generic(a.fmt, a.epi), k), "matvec launch");
+  GenFn gfn = pick_generic(a.fmt, a.epi, k.g.nranks > 0);
+  if (!gfn) return fail(EFG_EINVAL, "matvec: the in-kernel gather takes one plain product (no norm, no add)");
+  EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, gfn, k), "matvec launch");
   return EFG_OK;
 }
 

@@ -12,6 +12,22 @@ enum class Epi : int { Store = 0, Add = 1, SwiGLU = 2 };
 
 constexpr int kMaxJobs = 4;
 
+// The all-gather that the matvec kernels can do in their epilogue (efg_gather.cuh): flag
+// words of each rank's area, and the per-launch description (nranks == 0: no exchange).
+constexpr int kMaxGatherRanks = 8;
+constexpr uint32_t kReadyOff = 0;
+constexpr uint32_t kDoneOff = 32;
+constexpr uint32_t kEpochOff = 64;
+constexpr uint32_t kCountOff = 96;
+constexpr size_t kGatherFlagBytes = 128 * 4;
+
+struct GatherDev {
+  int nranks = 0, rank = 0;
+  uint32_t* flags = nullptr;                   // this rank's flag area
+  uint32_t* peer_flags[kMaxGatherRanks] = {};  // every rank's flag area (mapped)
+  float* peer_y[kMaxGatherRanks] = {};         // every rank's y at the launch's first row
+};
+
 struct MatvecJobDev {
   const uint8_t* W;
   float* y;
@@ -34,6 +50,9 @@ struct MatvecArgs {
   int n_jobs = 0;
   MatvecJobDev jobs[kMaxJobs] = {};
   bool pdl = false;               // launch with programmatic stream serialization
+  GatherDev gather;               // nranks > 0: store every output into each peer's y too, and
+                                  // return only once every peer's rows are here (one job, Store,
+                                  // no norm; efg_gather.cuh)
 };
 
 // Validates and launches. Returns an EFG_* status; on EFG_EINVAL/ECUDA the message is

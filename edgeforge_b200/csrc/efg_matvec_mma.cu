@@ -46,6 +46,7 @@
 #include "../../include/efg.h"
 #include "efg_device.cuh"
 #include "efg_dot.cuh"
+#include "efg_gather.cuh"
 #include "efg_host.h"
 #include "efg_matvec.cuh"
 
@@ -88,6 +89,7 @@ struct MmaParams {
   uint32_t rt_total, n_jobs;
   uint32_t job_rt_start[kMaxJobs + 1];
   MatvecJobDev jobs[kMaxJobs];
+  GatherDev g;  // the in-kernel all-gather of the row-sharded matvec (GATHER kernels only)
 };
 
 __device__ __forceinline__ uint32_t a_lo(uint32_t w) {
@@ -118,7 +120,7 @@ __device__ __forceinline__ void locate_rt(const MmaParams& p, uint32_t rt, uint3
   nrows = min(kTileRows, p.jobs[j].rows - r0);
 }
 
-template <Epi E, bool NORM>
+template <Epi E, bool NORM, bool GATHER>
 __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __grid_constant__ MmaParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -181,6 +183,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __g
   // -------------------------------------------------------------- consumers
   const uint32_t tid = threadIdx.x, nthr = kMmaConsumers * 32;
   pdl_wait();  // x, norm weights and y belong to the previous kernel in the stream
+  uint32_t epoch = 0;
+  if constexpr (GATHER) {
+    epoch = gather_epoch(p.g);
+    if (blockIdx.x == 0 && tid == 0) gather_announce(p.g, epoch);
+  }
   float inv = 1.f;
   if constexpr (NORM) {  // rmsnorm scale (src/kernels.cpp:69-73): double sum of squares
     double ss = 0.0;
@@ -282,7 +289,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __g
   const bool fallback = *bad_x != 0;
   const uint32_t SG = p.Wk * p.nseg;  // warps per tile
   const uint32_t gi = warp / SG, u = warp % SG, ks = u / p.Wk, kidx = u % p.Wk;
-  if (gi >= p.Gs) return;  // consumer warps beyond Gs * SG have no work
+  // Consumer warps beyond Gs * SG have no tiles (with the gather they still meet the others
+  // at the closing barrier).
+  if (!GATHER && gi >= p.Gs) return;
   // this warp's share of its segment: block pairs [p0, p1)
   const uint32_t kb = min(kSegBlk, p.nblk - ks * kSegBlk);
   const uint32_t p0 = (kb / 2) * kidx / p.Wk, p1 = (kb / 2) * (kidx + 1) / p.Wk;
@@ -305,8 +314,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __g
   const float* xs_l = xsc + t;                                                                          // + 2 / block
   const uint32_t off_g = g * kRowStride, off_g8 = (g + 8) * kRowStride;
   bool ok = true;
-  uint32_t m = 0;  // tiles this group has finished
-  for (uint32_t tl = gi; tl < R; tl += p.Gs, ++m) {
+  uint32_t ready = 0;  // gather: 0 = peers not checked yet, 1 = every peer ready, 2 = gave up
+  uint32_t m = 0;      // tiles this group has finished
+  for (uint32_t tl = gi; gi < p.Gs && tl < R; tl += p.Gs, ++m) {
     uint32_t j, r0, nrows;
     locate_rt(p, rt_b + tl, j, r0, nrows);
     float acc_g = 0.f, acc_g8 = 0.f;  // MMA path: rows g, g + 8
@@ -401,20 +411,35 @@ __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __g
       named_barrier(kGroupBarrier0 + gi, SG * 32);
     else
       __syncwarp();
-    if (u == 0 && lane < nrows) {
-      float v = 0.f;
-      for (uint32_t k = 0; k < SG; ++k) v += red[((gi * SG + k) * 2 + (m & 1u)) * kTileRows + lane];
-      float* y = p.jobs[j].y + (p.pos ? *p.pos * p.jobs[j].y_pos_stride : 0);
-      if (ok) y[r0 + lane] = E == Epi::Add ? y[r0 + lane] + v : v;
+    if (u == 0) {
+      if constexpr (GATHER) {
+        if (ready == 0) ready = gather_wait_ready(p.g, epoch, p.err) ? 1u : 2u;  // the whole warp
+      }
+      if (lane < nrows) {
+        float v = 0.f;
+        for (uint32_t k = 0; k < SG; ++k) v += red[((gi * SG + k) * 2 + (m & 1u)) * kTileRows + lane];
+        float* y = p.jobs[j].y + (p.pos ? *p.pos * p.jobs[j].y_pos_stride : 0);
+        if (ok) y[r0 + lane] = E == Epi::Add ? y[r0 + lane] + v : v;
+        if constexpr (GATHER) {
+          if (ok && ready == 1) gather_store(p.g, r0 + lane, v);
+        }
+      }
     }
+  }
+  if constexpr (GATHER) {
+    __threadfence_system();  // this thread's stores into peers' y, before the CTA is counted
+    named_barrier(1, nthr);
+    if (warp == 0) gather_finish(p.g, epoch, p.err);
   }
 }
 
 using MmaFn = void (*)(MmaParams);
 
-MmaFn pick_mma(Epi e, bool norm) {
-  if (e == Epi::Add) return norm ? matvec_q4_mma_kernel<Epi::Add, true> : matvec_q4_mma_kernel<Epi::Add, false>;
-  return norm ? matvec_q4_mma_kernel<Epi::Store, true> : matvec_q4_mma_kernel<Epi::Store, false>;
+MmaFn pick_mma(Epi e, bool norm, bool gather) {
+  if (gather) return e == Epi::Store && !norm ? matvec_q4_mma_kernel<Epi::Store, false, true> : nullptr;
+  if (e == Epi::Add)
+    return norm ? matvec_q4_mma_kernel<Epi::Add, true, false> : matvec_q4_mma_kernel<Epi::Add, false, false>;
+  return norm ? matvec_q4_mma_kernel<Epi::Store, true, false> : matvec_q4_mma_kernel<Epi::Store, false, false>;
 }
 
 struct MmaPlan {
@@ -506,7 +531,9 @@ int launch_matvec_q4_mma(const MatvecArgs& a, const DeviceInfo& dev, int* d_err,
   p.job_rt_start[a.n_jobs] = rt;
   p.rt_total = rt;
   if (rt == 0) return EFG_OK;
-  MmaFn fn = pick_mma(a.epi, a.norm_w != nullptr);
+  p.g = a.gather;
+  MmaFn fn = pick_mma(a.epi, a.norm_w != nullptr, a.gather.nranks > 0);
+  if (!fn) return fail(EFG_EINVAL, "matvec: the in-kernel gather takes one plain product (no norm, no add)");
   if (direct_smem_attr) {
     EFG_TRY_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(pl.smem)),

@@ -12,7 +12,10 @@
 
 #include <cstdint>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <string>
+#include <vector>
 
 #include <cuda_runtime.h>
 #include <nccl.h>
@@ -69,14 +72,121 @@ int nccl_check(Nccl* n, ncclResult_t r, const char* what) {
   return fail(EFG_ENCCL, "%s: %s", what, n->error_string ? n->error_string(r) : "NCCL error");
 }
 
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+// cuMemGetAddressRange from the driver, looked up once: the allocation that holds a pointer.
+AddressRangeFn address_range_fn() {
+  static const AddressRangeFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<AddressRangeFn>(f);
+  }();
+  return fn;
+}
+
+// What each rank tells the others when a buffer is registered for peer stores.
+struct RegRecord {
+  cudaIpcMemHandle_t buf;    // the allocation holding the buffer
+  cudaIpcMemHandle_t flags;  // the rank's gather flag area
+  uint64_t offset;           // of the buffer inside its allocation
+  uint64_t bytes;
+  int32_t ok;                // 0: this rank could not export its buffer
+  int32_t pad;
+};
+
 }  // namespace
 }  // namespace efg
+
+// A buffer registered on every rank: this rank's copy and the mapped copies of the peers.
+struct EfgRegBuf {
+  uint8_t* local = nullptr;
+  size_t bytes = 0;
+  uint8_t* peer[efg::kMaxGatherRanks] = {};  // peer[rank] == local
+  void* map_buf[efg::kMaxGatherRanks] = {};    // the peers' mapped allocations (to close)
+  void* map_flags[efg::kMaxGatherRanks] = {};  // the peers' mapped flag areas (to close)
+};
 
 struct efg_comm {
   ncclComm_t comm = nullptr;
   int nranks = 0, rank = 0, device = -1;
   efg::ArgmaxPair* d_pairs = nullptr;  // one per rank: the row-sharded argmax's exchange
+  // the in-kernel gather (efg_gather.cuh): flag areas and the registered buffers
+  uint32_t* d_flags = nullptr;
+  uint32_t* peer_flags[efg::kMaxGatherRanks] = {};
+  std::map<std::string, std::pair<void*, int>> opened;  // peer IPC handle -> (mapping, users)
+  std::vector<EfgRegBuf> bufs;
 };
+
+namespace efg {
+namespace {
+
+// All-gathers `n` bytes from every rank into all[nranks][n] (host memory), blocking.
+int allgather_host(efg_comm* c, const void* mine, size_t n, void* all) {
+  Nccl* nc = nullptr;
+  if (int st = load_nccl(&nc)) return st;
+  uint8_t* d = nullptr;
+  cudaStream_t s = nullptr;
+  int st = EFG_OK;
+  if (cudaMalloc(&d, n * static_cast<size_t>(c->nranks + 1)) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) {
+    st = fail(EFG_ECUDA, "comm: exchange buffer");
+  } else if (cudaMemcpyAsync(d + n * c->nranks, mine, n, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+    st = fail(EFG_ECUDA, "comm: exchange upload");
+  } else if ((st = nccl_check(nc, nc->all_gather(d + n * c->nranks, d, n, ncclUint8, c->comm, s), "ncclAllGather"))) {
+  } else if (cudaMemcpyAsync(all, d, n * c->nranks, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+             cudaStreamSynchronize(s) != cudaSuccess) {
+    st = fail(EFG_ECUDA, "comm: exchange download");
+  }
+  if (s) cudaStreamDestroy(s);
+  if (d) cudaFree(d);
+  return st;
+}
+
+std::string handle_key(int rank, const cudaIpcMemHandle_t& h) {
+  return std::to_string(rank) + ":" + std::string(reinterpret_cast<const char*>(&h), sizeof h);
+}
+
+// Maps rank q's allocation (reference counted per communicator).
+void* open_peer(efg_comm* c, int q, const cudaIpcMemHandle_t& h) {
+  const std::string key = handle_key(q, h);
+  auto it = c->opened.find(key);
+  if (it != c->opened.end()) {
+    ++it->second.second;
+    return it->second.first;
+  }
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  c->opened.emplace(key, std::make_pair(p, 1));
+  return p;
+}
+
+void close_peer(efg_comm* c, void* p) {
+  for (auto it = c->opened.begin(); it != c->opened.end(); ++it) {
+    if (it->second.first != p) continue;
+    if (--it->second.second == 0) {
+      cudaIpcCloseMemHandle(p);
+      c->opened.erase(it);
+    }
+    return;
+  }
+}
+
+const EfgRegBuf* registered(const efg_comm* c, const void* p, size_t n) {
+  const auto* b = static_cast<const uint8_t*>(p);
+  for (const EfgRegBuf& r : c->bufs)
+    if (b >= r.local && static_cast<size_t>(b - r.local) <= r.bytes && n <= r.bytes - static_cast<size_t>(b - r.local))
+      return &r;
+  return nullptr;
+}
+
+}  // namespace
+}  // namespace efg
 
 using efg::fail;
 
@@ -134,10 +244,115 @@ int efg_comm_destroy(efg_comm* c) {
   if (!c) return EFG_OK;
   efg::Nccl* n = nullptr;
   int st = EFG_OK;
+  if (c->device >= 0) cudaDeviceSynchronize();  // no kernel of ours may still store into a mapping
+  for (auto& kv : c->opened) cudaIpcCloseMemHandle(kv.second.first);
+  c->opened.clear();
   if (c->comm && efg::load_nccl(&n) == EFG_OK) st = efg::nccl_check(n, n->comm_destroy(c->comm), "ncclCommDestroy");
   if (c->d_pairs) cudaFree(c->d_pairs);
+  if (c->d_flags) cudaFree(c->d_flags);
   delete c;
   return st;
+}
+
+int efg_comm_register(efg_comm* c, void* d_buf, size_t bytes) {
+  using namespace efg;
+  if (!c || !c->comm) return fail(EFG_EINVAL, "comm_register: null communicator");
+  if (!d_buf || bytes == 0) return fail(EFG_EINVAL, "comm_register: empty buffer");
+  int dev = -1;
+  EFG_TRY_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != c->device)
+    return fail(EFG_EINVAL, "comm_register: current device %d is not the communicator's device %d", dev, c->device);
+  if (c->nranks > kMaxGatherRanks)  // the same on every rank: all of them return here
+    return fail(EFG_EINVAL, "comm_register: peer stores are limited to %d ranks, this communicator has %d",
+                kMaxGatherRanks, c->nranks);
+  if (registered(c, d_buf, bytes)) return fail(EFG_EINVAL, "comm_register: buffer already registered");
+  EfgRegBuf reg;
+  reg.local = static_cast<uint8_t*>(d_buf);
+  reg.bytes = bytes;
+  reg.peer[c->rank] = reg.local;
+  if (c->nranks == 1) {
+    c->bufs.push_back(reg);
+    return EFG_OK;
+  }
+  // this rank's record: the allocation holding the buffer and the flag area, exported
+  RegRecord mine{};
+  mine.bytes = bytes;
+  mine.ok = 1;
+  if (!c->d_flags) {
+    if (cudaMalloc(&c->d_flags, kGatherFlagBytes) != cudaSuccess ||
+        cudaMemset(c->d_flags, 0, kGatherFlagBytes) != cudaSuccess) {
+      cudaGetLastError();
+      if (c->d_flags) cudaFree(c->d_flags);
+      c->d_flags = nullptr;
+      mine.ok = 0;
+    }
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  const AddressRangeFn range = address_range_fn();
+  if (mine.ok && (!range || range(&base, &size, reinterpret_cast<CUdeviceptr>(d_buf)) != CUDA_SUCCESS ||
+                  reinterpret_cast<uintptr_t>(d_buf) + bytes > base + size))
+    mine.ok = 0;
+  mine.offset = reinterpret_cast<uintptr_t>(d_buf) - base;
+  if (mine.ok && (cudaIpcGetMemHandle(&mine.buf, reinterpret_cast<void*>(base)) != cudaSuccess ||
+                  cudaIpcGetMemHandle(&mine.flags, c->d_flags) != cudaSuccess)) {
+    cudaGetLastError();
+    mine.ok = 0;
+  }
+  std::vector<RegRecord> all(static_cast<size_t>(c->nranks));
+  if (int st = allgather_host(c, &mine, sizeof mine, all.data())) return st;
+  // every rank maps every peer's buffer and flag area; then all agree on the outcome
+  int32_t local_ok = 1;
+  for (int q = 0; q < c->nranks; ++q)
+    if (!all[q].ok || all[q].bytes != bytes) local_ok = 0;
+  std::vector<void*> mapped;
+  uint32_t* pflags[kMaxGatherRanks] = {};
+  for (int q = 0; q < c->nranks && local_ok; ++q) {
+    if (q == c->rank) continue;
+    void* pb = open_peer(c, q, all[q].buf);
+    void* pf = pb ? open_peer(c, q, all[q].flags) : nullptr;
+    if (pb) mapped.push_back(pb);
+    if (pf) mapped.push_back(pf);
+    if (!pb || !pf) {
+      local_ok = 0;
+      break;
+    }
+    reg.peer[q] = static_cast<uint8_t*>(pb) + all[q].offset;
+    reg.map_buf[q] = pb;
+    reg.map_flags[q] = pf;
+    pflags[q] = static_cast<uint32_t*>(pf);
+  }
+  std::vector<int32_t> oks(static_cast<size_t>(c->nranks));
+  if (int st = allgather_host(c, &local_ok, sizeof local_ok, oks.data())) {
+    for (void* p : mapped) close_peer(c, p);
+    return st;
+  }
+  for (int32_t v : oks) {
+    if (!v) {
+      for (void* p : mapped) close_peer(c, p);
+      return fail(EFG_ECUDA, "comm_register: a rank could not export or map the buffer for peer stores "
+                             "(cudaMalloc'd memory of one process per GPU is required)");
+    }
+  }
+  for (int q = 0; q < c->nranks; ++q) c->peer_flags[q] = q == c->rank ? c->d_flags : pflags[q];
+  c->bufs.push_back(reg);
+  return EFG_OK;
+}
+
+int efg_comm_deregister(efg_comm* c, void* d_buf) {
+  using namespace efg;
+  if (!c) return fail(EFG_EINVAL, "comm_deregister: null communicator");
+  for (auto it = c->bufs.begin(); it != c->bufs.end(); ++it) {
+    if (it->local != d_buf) continue;
+    cudaDeviceSynchronize();
+    for (int q = 0; q < c->nranks; ++q) {
+      if (it->map_buf[q]) close_peer(c, it->map_buf[q]);
+      if (it->map_flags[q]) close_peer(c, it->map_flags[q]);
+    }
+    c->bufs.erase(it);
+    return EFG_OK;
+  }
+  return fail(EFG_EINVAL, "comm_deregister: buffer not registered");
 }
 
 int efg_matvec_sharded(int qtype, float* d_y, const uint8_t* d_W_shard, const float* d_x, size_t rows, size_t cols,
@@ -160,6 +375,34 @@ int efg_matvec_sharded(int qtype, float* d_y, const uint8_t* d_W_shard, const fl
   size_t b = 0, cnt = 0;
   if (int st = efg_shard_rows(rows, comm->nranks, comm->rank, &b, &cnt)) return st;
   auto s = static_cast<cudaStream_t>(stream);
+  // The in-kernel gather: y registered on every rank (efg_comm_register) and at least one
+  // row per rank, which every rank decides alike. Each CTA stores its outputs into every
+  // rank's y; the launch returns once all ranks' rows are in this rank's y.
+  const EfgRegBuf* reg = comm->nranks > 1 ? registered(comm, d_y, rows * sizeof(float)) : nullptr;
+  if (reg && rows >= static_cast<size_t>(comm->nranks)) {
+    if (cols == 0) {  // every dot is over zero blocks: every rank fills its whole y with 0
+      EFG_TRY_CUDA(cudaMemsetAsync(d_y, 0, rows * sizeof(float), s), "matvec_sharded zero fill");
+      return EFG_OK;
+    }
+    DeviceInfo* di = current_device();
+    if (!di) return EFG_ECUDA;
+    MatvecArgs a;
+    a.fmt = qtype == EFG_Q4_0 ? Fmt::Q4 : Fmt::Q8;
+    a.x = d_x;
+    a.cols = cols;
+    a.pdl = weight_prefetch_flag();
+    a.n_jobs = 1;
+    a.jobs[0] = MatvecJobDev{d_W_shard, d_y + b, static_cast<uint32_t>(cnt), 0};
+    a.gather.nranks = comm->nranks;
+    a.gather.rank = comm->rank;
+    a.gather.flags = comm->d_flags;
+    const size_t off = reinterpret_cast<const uint8_t*>(d_y) - reg->local;
+    for (int q = 0; q < comm->nranks; ++q) {
+      a.gather.peer_flags[q] = comm->peer_flags[q];
+      a.gather.peer_y[q] = reinterpret_cast<float*>(reg->peer[q] + off) + b;
+    }
+    return launch_matvec(a, di->d_err, s);
+  }
   if (cnt) {
     DeviceInfo* di = current_device();
     if (!di) return EFG_ECUDA;

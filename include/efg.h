@@ -217,12 +217,26 @@ int efg_comm_unique_id(void* id);
 /* Joins the communicator `id` as `rank` of `nranks` on the current device (collective). */
 int efg_comm_init(const void* id, int nranks, int rank, efg_comm** out);
 int efg_comm_destroy(efg_comm* comm);
+/* Registers d_buf (`bytes`, device memory from cudaMalloc or a caching allocator built on
+ * it, on the communicator's device) so that the peers' kernels can store into it directly.
+ * Collective: every rank calls it with its own buffer of the same size, and all ranks get
+ * the same outcome (EFG_ECUDA on every rank when one cannot export or map its buffer, e.g.
+ * several ranks in one process). At most 8 ranks. The exchange of handles uses the
+ * communicator's NCCL; afterwards no library call is needed to move data. */
+int efg_comm_register(efg_comm* comm, void* d_buf, size_t bytes);
+/* Drops a registration (every rank calls it for its buffer; synchronises the device). */
+int efg_comm_deregister(efg_comm* comm, void* d_buf);
 /* Row-sharded ef::kern::matvec (qkernels.h:66) for a matrix too large for one GPU's share:
  * d_W_shard holds this rank's rows (efg_shard_rows) of the full [rows][cols] packed matrix,
- * d_x the whole x; on return (stream-ordered) d_y holds all `rows` outputs on every rank,
- * the slices exchanged in place over NVLink (one all-gather, or one broadcast per rank when
- * the split is uneven). Every rank calls it with the same rows/cols. EFG_ENCCL on a
- * collective failure. */
+ * d_x the whole x; on return (stream-ordered) d_y holds all `rows` outputs on every rank.
+ * When d_y lies in a buffer registered with efg_comm_register (at the same offset on every
+ * rank) and rows >= the rank count, the matvec kernel itself stores every output into every
+ * rank's y over NVLink and finishes once all ranks' rows have arrived (one launch, no
+ * collective call); every rank must then make the same sequence of these calls, and a rank
+ * that waits more than 2 s for a peer records EFG_ETIMEOUT (efg_device_error), after which
+ * the communicator must be destroyed. Otherwise the slices are exchanged in place through
+ * NCCL (one all-gather, or one broadcast per rank when the split is uneven). Every rank calls
+ * it with the same rows/cols. EFG_ENCCL on a collective failure. */
 int efg_matvec_sharded(int qtype, float* d_y, const uint8_t* d_W_shard, const float* d_x, size_t rows, size_t cols,
                        efg_comm* comm, void* stream);
 /* ef::kern::argmax (src/kernels.cpp:105-111) on the device: *d_index = the index of the

@@ -129,10 +129,39 @@ def _rank_main(rank, world, port, cases, out_dir):
             W, x = _make(torch, qt, rows, cols, 11)
             b, c = efg.shard_rows(rows, world, rank)
             shard = W[b:b + c].contiguous()
+            # through NCCL (y not registered) ...
             y = torch.full((rows,), float("nan"), device="cuda")
             efg.matvec_sharded(qt, y, shard, x, rows, cols, comm)
+            # ... and by the kernel's own peer stores (y registered on every rank), twice in a
+            # row, then as a CUDA graph of two calls replayed twice (the epoch lives on the device)
+            yf = torch.full((rows + 64,), float("nan"), device="cuda")
+            comm.register(yf)
+            yv = yf[32:32 + rows]  # the same offset on every rank
+            efg.matvec_sharded(qt, yv, shard, x, rows, cols, comm)
             torch.cuda.synchronize()
-            np.save(os.path.join(out_dir, f"y{i}_{rank}.npy"), y.cpu().numpy())
+            first = yv.clone()
+            yv.fill_(float("nan"))
+            efg.matvec_sharded(qt, yv, shard, x, rows, cols, comm)
+            torch.cuda.synchronize()
+            second = yv.clone()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+                for _ in range(2):
+                    efg.matvec_sharded(qt, yv, shard, x, rows, cols, comm)
+            yv.fill_(float("nan"))
+            torch.cuda.synchronize()
+            g.replay()
+            g.replay()
+            torch.cuda.synchronize()
+            graphed = yv.clone()
+            del g
+            torch.cuda.synchronize()
+            comm.deregister(yf)
+            assert torch.isnan(yf[:32]).all() and torch.isnan(yf[32 + rows:]).all()  # nothing outside y
+            for tag, t in (("nccl", y), ("fused", first), ("fused2", second), ("graph", graphed)):
+                np.save(os.path.join(out_dir, f"y{i}_{tag}_{rank}.npy"), t.cpu().numpy())
             if rank == 0:
                 np.save(os.path.join(out_dir, f"W{i}.npy"), W.cpu().numpy())
                 np.save(os.path.join(out_dir, f"x{i}.npy"), x.cpu().numpy())
@@ -159,17 +188,21 @@ def test_multi_rank(tmp_path, oracle):
     import torch
     import torch.multiprocessing as mp
 
-    n = min(torch.cuda.device_count(), 4)
+    n = min(torch.cuda.device_count(), 8)
     if n < 2:
         pytest.skip("needs two GPUs")
-    cases = [(QType.Q4_0, 16384, 8192), (QType.Q4_0, 1001, 256), (QType.Q8_0, 4099, 2048)]
+    # shards on the tensor-core kernel (>= 48 MB each at 2 ranks), the CUDA-core kernel, a
+    # ragged split, and the generic kernel (cols % 64 != 0)
+    cases = [(QType.Q4_0, 24576, 8192), (QType.Q4_0, 16384, 8192), (QType.Q4_0, 1001, 256),
+             (QType.Q8_0, 4099, 2048), (QType.Q8_0, 515, 96)]
     mp.start_processes(_rank_main, args=(n, _free_port(), cases, str(tmp_path)), nprocs=n, join=True,
                        start_method="spawn")
     from conftest import rel_dot_errors
 
     for i, (qt, rows, cols) in enumerate(cases):
-        ys = [np.load(tmp_path / f"y{i}_{r}.npy") for r in range(n)]
-        for y in ys[1:]:
+        ys = [np.load(tmp_path / f"y{i}_{tag}_{r}.npy") for tag in ("nccl", "fused", "fused2", "graph")
+              for r in range(n)]
+        for y in ys[1:]:  # every path, every rank, every call: the same bits
             np.testing.assert_array_equal(y, ys[0])
         W, x = np.load(tmp_path / f"W{i}.npy"), np.load(tmp_path / f"x{i}.npy")
         err = rel_dot_errors(oracle, qt, W, x, rows, ys[0])
