@@ -17,10 +17,12 @@ from .api import (  # noqa: F401
     dot_q4_0,
     dot_q8_0,
     efq_check,
+    fake_quant_q4_group,
     gemm_q4_0,
     gemm_q8_0,
     gemm_jobs,
     host_dequantize_row,
+    host_fake_quant_q4_group,
     host_matvec,
     host_matvec_static,
     host_quantize_row,

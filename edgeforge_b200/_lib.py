@@ -66,6 +66,8 @@ SIGNATURES = {
     "efg_row_f32": (_i, [_vp, _i, _vp, _sz, _sz, _i32p, _sz, _vp]),
     "efg_host_matvec": (_i, [_i, _vp, _vp, _vp, _sz, _sz]),
     "efg_host_quantize_row": (_i, [_i, _vp, _sz, _vp, _i]),
+    "efg_host_fake_quant_q4_group": (_i, [_vp, _sz, _vp, _i]),
+    "efg_fake_quant_q4_group": (_i, [_vp, _sz, _vp, _i, _vp]),
     "efg_host_dequantize_row": (_i, [_i, _vp, _sz, _vp]),
     "efg_host_register_weights": (_i, [_vp, _sz]),
     "efg_host_unregister_weights": (_i, [_vp]),

@@ -183,6 +183,20 @@ def host_quantize_row(qtype: int, x: np.ndarray, search: bool = True) -> np.ndar
     return out
 
 
+def host_fake_quant_q4_group(x: np.ndarray, search: bool = True) -> np.ndarray:
+    """ef::fake_quant_q4_group (quant.h:58): Q4 quantize -> dequantize of one group of any size
+    (the first min(n, 256) values are written; the rest of the result stays 0)."""
+    x, px = _np(x, np.float32)
+    out = np.zeros(x.size, dtype=np.float32)
+    check(load().efg_host_fake_quant_q4_group(px, x.size, C.c_void_p(out.ctypes.data), int(search)))
+    return out
+
+
+def fake_quant_q4_group(x, n: int, out, search: bool = True) -> None:
+    """efg_fake_quant_q4_group on CUDA tensors (torch's current stream)."""
+    check(load().efg_fake_quant_q4_group(_ptr(x), n, _ptr(out), int(search), _stream()))
+
+
 def host_dequantize_row(qtype: int, data: np.ndarray, n: int) -> np.ndarray:
     data, pd = _np(data, np.uint8)
     out = np.zeros(n, dtype=np.float32)

@@ -38,8 +38,11 @@ int check_cols(int qtype, uint64_t cols) {
   return EFG_OK;
 }
 
+bool is_plain(int qtype) { return qtype == EFG_F32 || qtype == EFG_F16 || qtype == EFG_BF16; }
+
 int matvec_one(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols, cudaStream_t s) {
-  if (!is_block(qtype)) return fail(EFG_EINVAL, "matvec: type %s is not a packed type (Q4_0, Q8_0)", type_name(qtype));
+  if (is_plain(qtype)) return launch_dense_matvec(qtype, y, W, x, rows, cols, s, weight_prefetch_flag());
+  if (!is_block(qtype)) return fail(EFG_EINVAL, "matvec: unknown type %d", qtype);
   if (int st = check_cols(qtype, cols)) return st;
   DeviceInfo* dev = current_device();
   if (!dev) return EFG_ECUDA;
@@ -228,6 +231,13 @@ int efg_matvec_jobs(const efg_matvec_job* jobs, size_t n_jobs, void* stream) {
     // Greedily group consecutive jobs that share type, cols and x (one launch each).
     MatvecArgs a;
     const efg_matvec_job& f = jobs[i];
+    if (is_plain(f.qtype)) {  // plain storage types: one launch per job
+      if (int st = launch_dense_matvec(f.qtype, f.d_y, f.d_W, f.d_x, f.rows, f.cols, as_stream(stream),
+                                       weight_prefetch_flag()))
+        return st;
+      ++i;
+      continue;
+    }
     if (!is_block(f.qtype)) return fail(EFG_EINVAL, "matvec_jobs: job %zu has type %s", i, type_name(f.qtype));
     if (int st = check_cols(f.qtype, f.cols)) return st;
     a.fmt = f.qtype == EFG_Q4_0 ? Fmt::Q4 : Fmt::Q8;
@@ -248,8 +258,12 @@ int efg_matvec_jobs(const efg_matvec_job* jobs, size_t n_jobs, void* stream) {
 }
 
 int efg_quantize_row(int qtype, const float* x, size_t n, void* out, int search, void* stream) {
-  if (!is_block(qtype)) return fail(EFG_EINVAL, "quantize_row: type %s is not a packed type", type_name(qtype));
+  if (!is_block(qtype) && !is_plain(qtype)) return fail(EFG_EINVAL, "quantize_row: unknown type %d", qtype);
   return launch_quantize(qtype, x, n, out, search != 0, as_stream(stream));
+}
+
+int efg_fake_quant_q4_group(const float* x, size_t n, float* out, int search, void* stream) {
+  return launch_fake_quant_q4_group(x, n, out, search != 0, as_stream(stream));
 }
 
 int efg_dequantize_row(int qtype, const void* in, size_t n, float* out, void* stream) {
@@ -257,7 +271,7 @@ int efg_dequantize_row(int qtype, const void* in, size_t n, float* out, void* st
 }
 
 int efg_quantize_rows(int qtype, const float* X, size_t rows, size_t cols, void* out, int search, void* stream) {
-  if (!is_block(qtype)) return fail(EFG_EINVAL, "quantize_rows: type %s is not a packed type", type_name(qtype));
+  if (!is_block(qtype) && !is_plain(qtype)) return fail(EFG_EINVAL, "quantize_rows: unknown type %d", qtype);
   if (int st = check_cols(qtype, cols)) return st;
   if (cols && rows > UINT64_MAX / cols) return fail(EFG_EINVAL, "quantize_rows: size overflows");
   return launch_quantize(qtype, X, static_cast<uint64_t>(rows) * cols, out, search != 0, as_stream(stream));
@@ -277,7 +291,7 @@ int efg_row_f32(float* out, int qtype, const uint8_t* W, size_t rows, size_t col
 // ---- host-pointer forms -------------------------------------------------------------
 
 int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols) {
-  if (!is_block(qtype)) return fail(EFG_EINVAL, "matvec: type %s is not a packed type (Q4_0, Q8_0)", type_name(qtype));
+  if (!is_block(qtype) && !is_plain(qtype)) return fail(EFG_EINVAL, "matvec: unknown type %d", qtype);
   if (int st = check_cols(qtype, cols)) return st;
   if (rows == 0) return EFG_OK;
   if (!y || (!W && cols) || (!x && cols)) return fail(EFG_EINVAL, "matvec: null pointer");
@@ -286,7 +300,7 @@ int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_
   if (!h) return st;
   std::lock_guard<std::mutex> lk(h->mu);
   if ((st = host_stream(h))) return st;
-  const size_t wbytes = rows * (cols / 32) * (qtype == EFG_Q4_0 ? 18 : 34);
+  const size_t wbytes = rows * static_cast<size_t>(efg_row_bytes(qtype, cols));
   const void* dW = resident(h, W, wbytes);
   if (!dW) {
     if ((st = ensure(h->wtmp, h->wtmp_cap, wbytes + 16))) return st;
@@ -309,7 +323,7 @@ int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_
 }
 
 int efg_host_quantize_row(int qtype, const float* x, size_t n, void* out, int search) {
-  if (!is_block(qtype)) return fail(EFG_EINVAL, "quantize_row: type %s is not a packed type", type_name(qtype));
+  if (!is_block(qtype) && !is_plain(qtype)) return fail(EFG_EINVAL, "quantize_row: unknown type %d", qtype);
   if (int st = check_cols(qtype, n)) return st;
   if (n == 0) return EFG_OK;
   if (!x || !out) return fail(EFG_EINVAL, "quantize_row: null pointer");
@@ -318,12 +332,32 @@ int efg_host_quantize_row(int qtype, const float* x, size_t n, void* out, int se
   if (!h) return st;
   std::lock_guard<std::mutex> lk(h->mu);
   if ((st = host_stream(h))) return st;
-  const size_t ob = n / 32 * (qtype == EFG_Q4_0 ? 18 : 34);
+  const size_t ob = static_cast<size_t>(efg_row_bytes(qtype, n));
   if ((st = ensure(h->in, h->in_cap, n * sizeof(float)))) return st;
   if ((st = ensure(h->out, h->out_cap, ob))) return st;
   EFG_TRY_CUDA(cudaMemcpyAsync(h->in, x, n * sizeof(float), cudaMemcpyHostToDevice, h->stream), "x upload");
   if ((st = launch_quantize(qtype, static_cast<const float*>(h->in), n, h->out, search != 0, h->stream))) return st;
   EFG_TRY_CUDA(cudaMemcpyAsync(out, h->out, ob, cudaMemcpyDeviceToHost, h->stream), "download");
+  EFG_TRY_CUDA(cudaStreamSynchronize(h->stream), "stream synchronize");
+  return EFG_OK;
+}
+
+int efg_host_fake_quant_q4_group(const float* x, size_t n, float* out, int search) {
+  const size_t m = n < 256 ? n : 256;
+  if (m == 0) return EFG_OK;
+  if (!x || !out) return fail(EFG_EINVAL, "fake_quant_q4_group: null pointer");
+  int st;
+  HostCtx* h = host_ctx(st);
+  if (!h) return st;
+  std::lock_guard<std::mutex> lk(h->mu);
+  if ((st = host_stream(h))) return st;
+  if ((st = ensure(h->in, h->in_cap, m * sizeof(float)))) return st;
+  if ((st = ensure(h->out, h->out_cap, m * sizeof(float)))) return st;
+  EFG_TRY_CUDA(cudaMemcpyAsync(h->in, x, m * sizeof(float), cudaMemcpyHostToDevice, h->stream), "x upload");
+  if ((st = launch_fake_quant_q4_group(static_cast<const float*>(h->in), m, static_cast<float*>(h->out), search != 0,
+                                       h->stream)))
+    return st;
+  EFG_TRY_CUDA(cudaMemcpyAsync(out, h->out, m * sizeof(float), cudaMemcpyDeviceToHost, h->stream), "download");
   EFG_TRY_CUDA(cudaStreamSynchronize(h->stream), "stream synchronize");
   return EFG_OK;
 }

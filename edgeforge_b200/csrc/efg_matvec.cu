@@ -408,6 +408,69 @@ __global__ void matvec_generic_kernel(const __grid_constant__ KParams p) {
   }
 }
 
+// ------------------------------------------------------------------ F32 / F16 / BF16 weights
+// y = W x for the plain storage types (src/qkernels.cpp:237-269; the reference's BF16 and F32
+// rows are its Stage 2 dot kernels, F16 widens per element): one warp per row, FP32
+// accumulation, 16-byte loads of W and x when both are 16-byte aligned (row bytes too).
+struct DenseParams {
+  const uint8_t* W;
+  float* y;
+  const float* x;
+  uint32_t rows, cols;
+  uint64_t row_bytes;
+  int vec;
+};
+
+template <int QT>
+__device__ __forceinline__ float dense_elem(const uint8_t* row, uint32_t c) {
+  if constexpr (QT == 0) {
+    return __uint_as_float(row[4 * c] | (row[4 * c + 1] << 8) | (row[4 * c + 2] << 16) |
+                           (static_cast<uint32_t>(row[4 * c + 3]) << 24));
+  } else {
+    const uint32_t h = row[2 * c] | (row[2 * c + 1] << 8);
+    return QT == 1 ? fp16_to_f32(h) : bf16_to_f32(h);
+  }
+}
+
+template <int QT>
+__global__ void __launch_bounds__(256) dense_matvec_kernel(const __grid_constant__ DenseParams p) {
+  pdl_wait();  // x and y belong to the previous kernel in the stream
+  pdl_launch_dependents();
+  constexpr uint32_t E = QT == 0 ? 4 : 8;  // weights per 16 bytes
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t warps = gridDim.x * (blockDim.x / 32);
+  const uint32_t n16 = p.vec ? p.cols / E : 0;
+  for (uint32_t r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); r < p.rows; r += warps) {
+    const uint8_t* row = p.W + static_cast<uint64_t>(r) * p.row_bytes;
+    float acc0 = 0.f, acc1 = 0.f;
+    for (uint32_t c = lane; c < n16; c += 32) {
+      const uint4 w = __ldcs(reinterpret_cast<const uint4*>(row) + c);  // streamed once
+      const float4* xv = reinterpret_cast<const float4*>(p.x) + c * (E / 4);
+      if constexpr (QT == 0) {
+        const float4 a = __ldg(xv);
+        acc0 = fmaf(__uint_as_float(w.x), a.x, acc0);
+        acc1 = fmaf(__uint_as_float(w.y), a.y, acc1);
+        acc0 = fmaf(__uint_as_float(w.z), a.z, acc0);
+        acc1 = fmaf(__uint_as_float(w.w), a.w, acc1);
+      } else {
+        const float4 a = __ldg(xv), b = __ldg(xv + 1);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const float xs[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float lo = QT == 1 ? fp16_to_f32(ws[k] & 0xFFFFu) : __uint_as_float(ws[k] << 16);
+          const float hi = QT == 1 ? fp16_to_f32(ws[k] >> 16) : __uint_as_float(ws[k] & 0xFFFF0000u);
+          acc0 = fmaf(lo, xs[2 * k], acc0);
+          acc1 = fmaf(hi, xs[2 * k + 1], acc1);
+        }
+      }
+    }
+    for (uint32_t c = n16 * E + lane; c < p.cols; c += 32) acc0 = fmaf(dense_elem<QT>(row, c), p.x[c], acc0);
+    const float v = warp_sum(acc0 + acc1);
+    if (lane == 0) p.y[r] = v;
+  }
+}
+
 // cols == 0: every dot is over zero blocks, which the reference returns as 0.
 __global__ void zero_rows_kernel(float* y, uint32_t n) {
   pdl_wait();
@@ -554,6 +617,36 @@ Plan plan_fast(const MatvecArgs& a, const DeviceInfo& dev) {
 }
 
 }  // namespace
+
+int launch_dense_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols,
+                        cudaStream_t stream, bool pdl) {
+  if (qtype < 0 || qtype > 2) return fail(EFG_EINVAL, "matvec: type %d is not F32, F16 or BF16", qtype);
+  if (rows == 0) return EFG_OK;
+  if (rows >= (1ull << 31) || cols >= (1ull << 31)) return fail(EFG_EINVAL, "matvec: shape too large");
+  if (!y || (cols && (!W || !x))) return fail(EFG_EINVAL, "matvec: null pointer");
+  DeviceInfo* dev = current_device();
+  if (!dev) return EFG_ECUDA;
+  DenseParams p{};
+  p.W = W;
+  p.y = y;
+  p.x = x;
+  p.rows = static_cast<uint32_t>(rows);
+  p.cols = static_cast<uint32_t>(cols);
+  p.row_bytes = static_cast<uint64_t>(cols) * (qtype == 0 ? 4 : 2);
+  p.vec = reinterpret_cast<uintptr_t>(W) % 16 == 0 && p.row_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(std::max<uint64_t>(1, std::min<uint64_t>((rows + 7) / 8, 16ull * dev->sm_count))));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  auto fn = qtype == 0 ? dense_matvec_kernel<0> : qtype == 1 ? dense_matvec_kernel<1> : dense_matvec_kernel<2>;
+  EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, fn, p), "matvec launch");
+  return EFG_OK;
+}
 
 bool matvec_fast_path_ok(const MatvecArgs& a) {
   DeviceInfo* dev = current_device();

@@ -59,6 +59,10 @@ struct MatvecArgs {
 // left in the thread-local error string.
 int launch_matvec(const MatvecArgs& a, int* d_err, cudaStream_t stream);
 
+// y = W x for W stored as 0 = F32, 1 = F16, 2 = BF16 ([rows][cols], any alignment).
+int launch_dense_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols,
+                        cudaStream_t stream, bool pdl);
+
 struct DeviceInfo;
 // The Q4_0 kernel on the integer tensor-core MMA (efg_matvec_mma.cu): taken for Q4_0
 // matrices of 48 MB and more with 2048 <= cols <= 8192, cols % 256 == 0, 16-byte aligned

@@ -265,6 +265,103 @@ __global__ void widen_kernel(int qtype, const uint8_t* __restrict__ in, float* _
   }
 }
 
+// binary32 -> bfloat16 of include/ef/fp16.h:34-42: NaN keeps its top bits with the quiet bit
+// forced; everything else rounds to nearest even (overflow becomes inf).
+__device__ __forceinline__ uint32_t f32_to_bf16(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u) return ((u >> 16) | 0x0040u) & 0xFFFFu;
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return u >> 16;
+}
+
+// F32 / F16 / BF16 rows from floats (src/quant.cpp:186-200): an exact copy of the bits, or
+// the reference's round-to-nearest-even narrowing, little-endian at any byte offset.
+__global__ void narrow_kernel(int qtype, const float* __restrict__ x, uint8_t* __restrict__ out, uint64_t n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint32_t u = __float_as_uint(x[i]);
+    if (qtype == 0) {
+      out[4 * i] = static_cast<uint8_t>(u);
+      out[4 * i + 1] = static_cast<uint8_t>(u >> 8);
+      out[4 * i + 2] = static_cast<uint8_t>(u >> 16);
+      out[4 * i + 3] = static_cast<uint8_t>(u >> 24);
+    } else {
+      const uint32_t h = qtype == 1 ? f32_to_fp16(x[i]) : f32_to_bf16(x[i]);
+      out[2 * i] = static_cast<uint8_t>(h);
+      out[2 * i + 1] = static_cast<uint8_t>(h >> 8);
+    }
+  }
+}
+
+// fake_quant_q4_group (src/quant.cpp:243-248): q4_group over the first min(n, 256) values of
+// one group of any size, written back as float(code - 8) * d. One thread runs the whole group
+// in the reference's order (analysis tooling, not a hot path).
+__global__ void fake_quant_q4_group_kernel(const float* __restrict__ x, uint32_t n, float* __restrict__ out,
+                                           int search) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  float amax = 0.0f, smax = 0.0f;
+  for (uint32_t j = 0; j < n; ++j) {
+    const float a = fabsf(x[j]);
+    if (a > amax) {
+      amax = a;
+      smax = x[j];
+    }
+  }
+  auto error_of = [&](float d) {
+    const float inv = __fdiv_rn(1.0f, d);
+    double err = 0.0;
+    for (uint32_t j = 0; j < n; ++j) {
+      const int c = q4_code(x[j], inv);
+      const double e = __dsub_rn(static_cast<double>(x[j]), static_cast<double>(__fmul_rn(static_cast<float>(c - 8), d)));
+      err = __dadd_rn(err, __dmul_rn(e, e));
+    }
+    return err;
+  };
+  float best_d = 0.0f;
+  if (amax > 0.0f && isfinite(amax)) {
+    double best = -1.0;
+    const int n_cand = search ? 6 : 1;
+    for (int c = 0; c < n_cand; ++c) {
+      const float div = c == 1 ? 7.0f : c == 2 ? 7.25f : c == 3 ? 7.5f : c == 4 ? 7.75f : 8.0f;
+      const float cand = c == 0 ? __fdiv_rn(smax, -8.0f) : __fdiv_rn(amax, div);
+      const float d = fp16_round(clamp_f(cand, -kFp16Max, kFp16Max));
+      if (d == 0.0f) continue;
+      const double err = error_of(d);
+      if (best < 0.0 || err < best) {
+        best = err;
+        best_d = d;
+      }
+    }
+    if (best >= 0.0 && search) {
+      for (int round = 0; round < 2; ++round) {
+        const float inv = __fdiv_rn(1.0f, best_d);
+        double sxc = 0.0, scc = 0.0;
+        for (uint32_t j = 0; j < n; ++j) {
+          const double c = static_cast<double>(q4_code(x[j], inv) - 8);
+          sxc = __dadd_rn(sxc, __dmul_rn(static_cast<double>(x[j]), c));
+          scc = __dadd_rn(scc, __dmul_rn(c, c));
+        }
+        if (scc == 0.0) break;
+        const float d = fp16_round(__double2float_rn(clamp_d(__ddiv_rn(sxc, scc), -65504.0, 65504.0)));
+        if (d == 0.0f || d == best_d) break;
+        const double err = error_of(d);
+        if (!(err < best)) break;
+        best = err;
+        best_d = d;
+      }
+    }
+  }
+  const float inv = best_d != 0.0f ? __fdiv_rn(1.0f, best_d) : 0.0f;
+  for (uint32_t j = 0; j < n; ++j) {
+    const int c = best_d != 0.0f ? q4_code(x[j], inv) : 8;
+    out[j] = __fmul_rn(static_cast<float>(c - 8), best_d);
+  }
+}
+
 // Reconstruction statistics of one quantized row per thread (src/quantizer.cpp:131-147):
 // e = double(src) - double(dequantized), sse += e * e, ref += src^2 (double, column order,
 // no contraction) and the largest |e|, so the totals the writer forms from them are the
@@ -351,7 +448,18 @@ cudaLaunchConfig_t config(unsigned grid, unsigned block, cudaStream_t s, cudaLau
 int launch_quantize(int qtype, const float* x, uint64_t n_values, void* out, bool search, cudaStream_t s, bool pdl) {
   DeviceInfo* dev = current_device();
   if (!dev) return EFG_ECUDA;
-  if (qtype != 4 && qtype != 3) return fail(EFG_EINVAL, "quantize: type must be Q4_0 or Q8_0 on the device");
+  if (qtype >= 0 && qtype <= 2) {  // F32 / F16 / BF16: plain conversions, any length
+    if (n_values == 0) return EFG_OK;
+    if (!x || !out) return fail(EFG_EINVAL, "quantize: null pointer");
+    const unsigned grid = static_cast<unsigned>(
+        std::max<uint64_t>(1, std::min<uint64_t>((n_values + 255) / 256, 32ull * dev->sm_count)));
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t c = config(grid, 256, s, attr, pdl);
+    EFG_TRY_CUDA(cudaLaunchKernelEx(&c, narrow_kernel, qtype, x, static_cast<uint8_t*>(out), n_values),
+                 "quantize launch");
+    return EFG_OK;
+  }
+  if (qtype != 4 && qtype != 3) return fail(EFG_EINVAL, "quantize: unknown type %d", qtype);
   if (n_values % 32 != 0) {
     return fail(EFG_EINVAL, "%s needs a row length divisible by 32, got %llu", qtype == 4 ? "Q4_0" : "Q8_0",
                 static_cast<unsigned long long>(n_values));
@@ -396,6 +504,17 @@ int launch_dequantize(int qtype, const void* in, uint64_t n_values, float* out, 
     cudaLaunchConfig_t c = config(grid, 256, s, attr, pdl);
     EFG_TRY_CUDA(cudaLaunchKernelEx(&c, widen_kernel, qtype, p, out, n_values), "dequantize launch");
   }
+  return EFG_OK;
+}
+
+int launch_fake_quant_q4_group(const float* x, uint64_t n, float* out, bool search, cudaStream_t s) {
+  if (n > 256) n = 256;  // the reference quantizes the first 256 values only
+  if (n == 0) return EFG_OK;
+  if (!x || !out) return fail(EFG_EINVAL, "fake_quant_q4_group: null pointer");
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t c = config(1, 32, s, attr, false);
+  EFG_TRY_CUDA(cudaLaunchKernelEx(&c, fake_quant_q4_group_kernel, x, static_cast<uint32_t>(n), out, search ? 1 : 0),
+               "fake_quant_q4_group launch");
   return EFG_OK;
 }
 

@@ -100,7 +100,9 @@ int efg_matvec_q4_0(float* d_y, const uint8_t* d_W, const float* d_x, size_t row
 /* Replaces ef::kern::matvec_q8_0 (include/ef/qkernels.h:51, src/qkernels.cpp:72-75). */
 int efg_matvec_q8_0(float* d_y, const uint8_t* d_W, const float* d_x, size_t rows, size_t cols, void* stream);
 /* Replaces ef::kern::matvec(y, WeightView, x, pool) (include/ef/qkernels.h:66,
- * src/qkernels.cpp:275-278) for the packed types EFG_Q4_0 / EFG_Q8_0. */
+ * src/qkernels.cpp:275-278) for every storage type: the packed EFG_Q4_0 / EFG_Q8_0 as above,
+ * and EFG_F32 / EFG_F16 / EFG_BF16 rows of `cols` plain values (src/qkernels.cpp:237-269; a
+ * tied BF16 lm_head, src/model.cpp:88,273), within the same 1e-5 of sum|w x|. */
 int efg_matvec(int qtype, float* d_y, const uint8_t* d_W, const float* d_x, size_t rows, size_t cols, void* stream);
 
 /* One job of a fused multi-matrix matvec: ef::kern::MatvecJob plus the WeightView it
@@ -129,8 +131,15 @@ int efg_dot_q8_0(float* d_out, const uint8_t* d_row, const float* d_x, size_t n,
 
 /* Replaces ef::quantize_row (include/ef/quant.h:52, src/quant.cpp:182-218) for
  * EFG_Q4_0 (search != 0: the MSE scale search + least-squares refinement of
- * src/quant.cpp:26-99; 0: the absmax scale) and EFG_Q8_0 (search ignored). */
+ * src/quant.cpp:26-99; 0: the absmax scale), EFG_Q8_0 (search ignored) and the plain
+ * conversions EFG_F32 (the bits), EFG_F16 and EFG_BF16 (round to nearest even, the
+ * reference's NaN rules; any n). */
 int efg_quantize_row(int qtype, const float* d_x, size_t n, void* d_out, int search, void* stream);
+/* Replaces ef::fake_quant_q4_group (include/ef/quant.h:58, src/quant.cpp:243-248): the Q4
+ * quantize -> dequantize of one group of n values with one FP16 scale (the scale search of
+ * q4_group when search != 0); only the first min(n, 256) values are written, as in the
+ * reference. Bit-exact. */
+int efg_fake_quant_q4_group(const float* d_x, size_t n, float* d_out, int search, void* stream);
 /* Replaces ef::dequantize_row (include/ef/quant.h:53, src/quant.cpp:220-249) for the
  * block types, and EFG_F32/EFG_F16/EFG_BF16 (exact widening). */
 int efg_dequantize_row(int qtype, const void* d_in, size_t n, float* d_out, void* stream);
@@ -158,6 +167,7 @@ int efg_row_f32(float* d_out, int qtype, const uint8_t* d_W, size_t rows, size_t
  */
 int efg_host_matvec(int qtype, float* y, const uint8_t* W, const float* x, size_t rows, size_t cols);
 int efg_host_quantize_row(int qtype, const float* x, size_t n, void* out, int search);
+int efg_host_fake_quant_q4_group(const float* x, size_t n, float* out, int search);
 int efg_host_dequantize_row(int qtype, const void* in, size_t n, float* out);
 /* Uploads [host, host + bytes) once and keeps it on the device; the caller promises not to
  * modify those bytes while registered. Registering a range again refreshes its copy. */

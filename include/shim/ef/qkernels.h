@@ -1,0 +1,4 @@
+// include/shim/ef/qkernels.h - stands in for the reference's include/ef/qkernels.h: the same
+// API, running on the GPU through libefg.so (include/efg_ref_shim.hpp).
+#pragma once
+#include "../../efg_ref_shim.hpp"

@@ -201,6 +201,15 @@ void efo_quantize_block_q4_0(const float* x, uint8_t out[18], int search) {
   for (int j = 0; j < 16; ++j) out[2 + j] = (uint8_t)(q[j] | (q[j + 16] << 4));
 }
 
+/* src/quant.cpp:243-248: q4_group on the first min(n, 256) values, written back as
+ * float(code - 8) * d. */
+void efo_fake_quant_q4_group(const float* x, size_t n, float* out, int search) {
+  uint8_t q[256];
+  const size_t m = n < 256 ? n : 256;
+  const float d = q4_group(x, m, search, q);
+  for (size_t j = 0; j < m; ++j) out[j] = (float)((int)q[j] - 8) * d;
+}
+
 /* src/quant.cpp:158-164 */
 void efo_dequantize_block_q4_0(const uint8_t in[18], float* out) {
   const float d = efo_fp16_to_f32((uint16_t)(in[0] | (in[1] << 8)));

@@ -42,6 +42,8 @@ uint64_t efo_row_bytes(int qtype, uint64_t cols, int* ok);
 void efo_quantize_block_q4_0(const float* x, uint8_t out[18], int search);
 void efo_quantize_block_q8_0(const float* x, uint8_t out[34]);
 void efo_dequantize_block_q4_0(const uint8_t in[18], float* out);
+/* quant.cpp:243-248: Q4 quantize -> dequantize of one group (first min(n, 256) values). */
+void efo_fake_quant_q4_group(const float* x, size_t n, float* out, int search);
 void efo_dequantize_block_q8_0(const uint8_t in[34], float* out);
 /* Rows (quant.cpp:182-249). Return 0 on success, -1 if n is not a multiple of 32
  * for a block type. */

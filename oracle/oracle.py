@@ -90,6 +90,7 @@ class _Lib:
         self.f32_to_bf16 = self._fn("f32_to_bf16", C.c_uint16, C.c_float)
         self._qrow = self._fn("quantize_row", C.c_int, C.c_int, _fp, _sz, _vp, C.c_int)
         self._drow = self._fn("dequantize_row", C.c_int, C.c_int, _vp, _sz, _fp)
+        self._fq = self._fn("fake_quant_q4_group", None, _fp, _sz, _fp, C.c_int)
         self._dot4 = self._fn("dot_q4_0", C.c_float, _u8, _fp, _sz)
         self._dot8 = self._fn("dot_q8_0", C.c_float, _u8, _fp, _sz)
         self._mv4 = self._fn("matvec_q4_0", None, _fp, _u8, _fp, _sz, _sz)
@@ -107,6 +108,13 @@ class _Lib:
         out = np.zeros(row_bytes(qtype, x.size), dtype=np.uint8)
         if self._qrow(qtype, _p(x, _fp), x.size, _p(out), int(search)) != 0:
             raise ValueError("quantize_row rejected the input")
+        return out
+
+    def fake_quant_q4_group(self, x: np.ndarray, search: bool = True) -> np.ndarray:
+        """quant.cpp:243-248; values past the first 256 stay 0."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.zeros(x.size, dtype=np.float32)
+        self._fq(_p(x, _fp), x.size, _p(out, _fp), int(search))
         return out
 
     def dequantize_row(self, qtype: int, data: np.ndarray, n: int) -> np.ndarray:

@@ -69,6 +69,9 @@ int efr_quantize_row(int t, const float* x, std::size_t n, void* out, int search
 int efr_dequantize_row(int t, const void* in, std::size_t n, float* out) {
   return guarded([&] { ef::dequantize_row(qt(t), in, n, out); });
 }
+void efr_fake_quant_q4_group(const float* x, std::size_t n, float* out, int search) {
+  ef::fake_quant_q4_group(x, n, out, search != 0);
+}
 void efr_quantize_block_q4_0(const float* x, std::uint8_t* out, int search) {
   ef::BlockQ4_0 b;
   ef::quantize_block_q4_0(x, b, search != 0);

@@ -9,7 +9,8 @@ quantized by the reference's quantize_model:
     BF16 embedding);
   * decode_tiny_mixed.efq: explicit overrides putting layer 0's k_proj and layer 1's
     up_proj in Q8_0, so q/k/v and gate/up mix storage types.
-For each, decode_tiny.npz holds a seeded 7-token prompt, 8 forced continuation ids, the
+A third model, decode_tiny_tied.efq (seed 6), ties lm_head to the BF16 embedding; its
+logits and greedy tokens are in decode_tiny_tied.npz. For the first two, decode_tiny.npz holds a seeded 7-token prompt, 8 forced continuation ids, the
 reference decoder's teacher-forced logits (scalar and AVX2 backends; the logits after
 the last prompt token and after each forced id but the last) and the reference's own
 greedy tokens (8 steps, argmax of its logits).
@@ -87,15 +88,30 @@ def main() -> int:
             out[f"{tag}_greedy"] = greedy(dec, prompt, 8, V)
             out[f"{tag}_bytes_per_token"] = np.array(dec.bytes_per_token(), np.uint64)
             dec.close()
+        # tied embeddings: lm_head is the BF16 embedding itself (src/model.cpp:88, 273)
+        tcfg = dict(cfg, tie_word_embeddings=True)
+        tsrc = synthetic.write_checkpoint(Path(td) / "ckpt_tied", tcfg, seed=6)
+        efq = HERE / "decode_tiny_tied.efq"
+        ref.quantize_model(tsrc, efq, policy="auto", threads=1)
+        dec = ref.decoder(efq, MAX_SEQ, threads=1)
+        tied = {"prompt": prompt, "forced": forced,
+                "tied_scalar": teacher_forced(dec, prompt, forced, V, avx2=False),
+                "tied_greedy": greedy(dec, prompt, 8, V)}
+        if ref.avx2:
+            tied["tied_avx2"] = teacher_forced(dec, prompt, forced, V, avx2=True)
+        dec.close()
     np.savez_compressed(HERE / "decode_tiny.npz", **out)
+    np.savez_compressed(HERE / "decode_tiny_tied.npz", **tied)
     man_path = HERE / "manifest.json"
     man = json.loads(man_path.read_text()) if man_path.exists() else {"files": {}}
     man["files"]["decode_tiny_uniform.efq"] = "tiny Llama model, reference quantize_model policy auto (uniform)"
     man["files"]["decode_tiny_mixed.efq"] = "same weights, overrides " + MIXED
+    man["files"]["decode_tiny_tied.efq"] = "tiny Llama model with tied embeddings (BF16 lm_head), policy auto"
+    man["files"]["decode_tiny_tied.npz"] = "reference decoder teacher-forced logits and greedy tokens of the tied model"
     man["files"]["decode_tiny.npz"] = ("prompt/forced ids; reference decoder teacher-forced logits (scalar, AVX2) "
                                        "and greedy tokens for both models (make_decode_golden.py)")
     man_path.write_text(json.dumps(man, indent=1) + "\n")
-    print("wrote decode_tiny_uniform.efq, decode_tiny_mixed.efq, decode_tiny.npz")
+    print("wrote decode_tiny_{uniform,mixed,tied}.efq, decode_tiny.npz, decode_tiny_tied.npz")
     return 0
 
 

@@ -60,8 +60,10 @@ def test_argument_errors_before_any_device_work(efg_lib):
     assert lib.efg_matvec_q4_0(None, None, None, 4, 30, None) == 1
     assert b"divisible by 32, got 30" in lib.efg_last_error()
     assert lib.efg_quantize_rows(4, None, 2, 33, None, 1, None) == 1
-    assert lib.efg_matvec(0, None, None, None, 1, 32, None) == 1  # F32 is not packed
-    assert b"not a packed type" in lib.efg_last_error()
+    assert lib.efg_matvec(7, None, None, None, 1, 32, None) == 1  # no such storage type
+    assert b"unknown type" in lib.efg_last_error()
+    assert lib.efg_matvec(0, None, None, None, 1, 32, None) == 1  # F32 rows need W, x and y
+    assert b"null pointer" in lib.efg_last_error()
     assert lib.efg_host_matvec(4, None, None, None, 1, 40) == 1
     assert lib.efg_host_quantize_row(2, None, 32, None, 1) == 1
 

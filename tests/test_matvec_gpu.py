@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 from conftest import golden, rel_dot_errors
 
-from oracle.oracle import Q4_0, Q8_0, row_bytes
+from oracle.oracle import BF16, F16, F32, Q4_0, Q8_0, row_bytes
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-5
@@ -291,3 +291,50 @@ def test_dot_hand_blocks(efg_lib, cuda):
     efg_lib.dot_q4_0(out, dev(q4, cuda), dev(x, cuda), 0)  # n = 0: a sum over no blocks is 0
     torch.cuda.synchronize()
     assert out.item() == 0.0
+
+
+def _plain_rows(qt, X):
+    """[rows][cols] float32 -> the plain storage bytes (F32 bits, F16 and BF16 rounded to nearest even)."""
+    from edgeforge_b200.synthetic import bf16_bits
+
+    if qt == F32:
+        return np.ascontiguousarray(X, np.float32).view(np.uint8).reshape(X.shape[0], -1)
+    if qt == F16:
+        return X.astype(np.float16).view(np.uint8).reshape(X.shape[0], -1)
+    return bf16_bits(X).view(np.uint8).reshape(X.shape[0], -1)
+
+
+@pytest.mark.parametrize("qt", [F32, F16, BF16])
+@pytest.mark.parametrize("rows,cols,offset", [(257, 2048, 0), (100, 96, 0), (33, 1003, 0), (64, 2048, 2), (5, 0, 0)])
+def test_plain_type_matvec(efg_lib, cuda, oracle, qt, rows, cols, offset):
+    """kern::matvec for F32 / F16 / BF16 views (src/qkernels.cpp:237-269): every row within 1e-5
+    of sum|w x| of the exact dot; ragged lengths and a misaligned W take the scalar loads."""
+    rng = np.random.default_rng(51 + rows + cols)
+    X = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    W = _plain_rows(qt, X)
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = run_matvec(efg_lib, cuda, qt, W, x, rows, offset)
+    if cols == 0:
+        assert (y == 0).all()
+        return
+    assert rel_dot_errors(oracle, qt, W, x, rows, y).max() < TOL
+
+
+def test_tied_bf16_lm_head_shape(efg_lib, cuda, oracle):
+    """A tied lm_head: the BF16 32000 x 2048 embedding as the matrix (src/model.cpp:88, 273), and
+    the same product through matvec_jobs next to a Q8_0 job."""
+    import torch
+
+    rng = np.random.default_rng(61)
+    rows, cols = 32000, 2048
+    W = _plain_rows(BF16, (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32))
+    x = rng.standard_normal(cols).astype(np.float32)
+    y = run_matvec(efg_lib, cuda, BF16, W, x, rows)
+    assert rel_dot_errors(oracle, BF16, W, x, rows, y).max() < TOL
+    Wq = random_packed(Q8_0, 64, cols, rng)
+    dW, dWq, dx = dev(W.reshape(-1), cuda), dev(Wq.reshape(-1), cuda), dev(x, cuda)
+    y1, y2 = torch.empty(rows, device=cuda), torch.empty(64, device=cuda)
+    efg_lib.matvec_jobs([(y1, BF16, dW, rows, cols, dx), (y2, Q8_0, dWq, 64, cols, dx)])
+    torch.cuda.synchronize()
+    assert np.array_equal(y1.cpu().numpy(), y)
+    assert rel_dot_errors(oracle, Q8_0, Wq, x, 64, y2.cpu().numpy()).max() < TOL

@@ -233,3 +233,18 @@ def test_oracle_equals_live_reference(oracle, reference):
             x = rng.standard_normal(512).astype(np.float32)
             y = reference.matvec_backend(qt, a, x, 300, avx2=False)
             assert np.array_equal(bits(oracle.matvec(qt, a, x, 300)), bits(y))
+
+
+def test_fake_quant_q4_group_matches_reference(oracle, reference):
+    """fake_quant_q4_group (src/quant.cpp:243-248): groups of 32/64/128/256 and a 300-value group
+    (only the first 256 are written), with and without the search; zero and non-finite groups."""
+    rng = np.random.default_rng(31)
+    cases = [(rng.standard_normal(n) * 0.02).astype(np.float32) for n in (32, 64, 100, 128, 256, 300)]
+    cases.append(np.zeros(64, np.float32))
+    bad = cases[1].copy(); bad[3] = np.inf; cases.append(bad)
+    tiny = (rng.standard_normal(64) * 1e-9).astype(np.float32); cases.append(tiny)
+    for x in cases:
+        for search in (True, False):
+            a = oracle.fake_quant_q4_group(x, search)
+            b = reference.fake_quant_q4_group(x, search)
+            np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))

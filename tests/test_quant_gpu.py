@@ -116,3 +116,47 @@ def test_host_pointer_quantize_roundtrip(efg_lib, cuda, oracle):
     q = efg_lib.host_quantize_row(Q4_0, x)
     assert np.array_equal(q, oracle.quantize_row(Q4_0, x))
     assert np.array_equal(bits(efg_lib.host_dequantize_row(Q4_0, q, 4096)), bits(oracle.dequantize_row(Q4_0, q, 4096)))
+
+
+def _edge_floats(rng, n):
+    """Random bit patterns (NaN payloads, infinities, subnormals) plus values at the F16/BF16
+    rounding and overflow edges."""
+    v = rng.integers(0, 2**32, n, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    edges = np.array([0.0, -0.0, 65504, 65519.996, 65520, -65520, 2.0**-24, 2.0**-25, 3 * 2.0**-26, 2.0**-14,
+                      np.inf, -np.inf, np.nan, 3.3895314e38, 1.0 + 2.0**-8, 1.0 + 3 * 2.0**-8], dtype=np.float32)
+    return np.concatenate([v, edges, (rng.standard_normal(n) * 0.02).astype(np.float32)])
+
+
+@pytest.mark.parametrize("qt", [F32, F16, BF16])
+def test_plain_type_quantize_row_bit_exact(efg_lib, cuda, oracle, qt):
+    """quantize_row for F32 / F16 / BF16 (src/quant.cpp:186-200) on the device: the bits of
+    every value, NaN payloads included, equal the oracle's (itself pinned to the reference);
+    an odd length and an odd byte offset of the output."""
+    import torch
+
+    rng = np.random.default_rng(41)
+    x = _edge_floats(rng, 4001)
+    want = oracle.quantize_row(qt, x)
+    got = efg_lib.host_quantize_row(qt, x)
+    np.testing.assert_array_equal(got, want)
+    buf = torch.zeros(want.size + 8, dtype=torch.uint8, device=cuda)
+    efg_lib.quantize_row(qt, dev(x, cuda), x.size, buf[3:3 + want.size])
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(buf.cpu().numpy()[3:3 + want.size], want)
+    assert not buf.cpu().numpy()[:3].any() and not buf.cpu().numpy()[3 + want.size:].any()
+
+
+@pytest.mark.parametrize("n", [32, 64, 100, 128, 256, 300])
+def test_fake_quant_q4_group_bit_exact(efg_lib, cuda, oracle, n):
+    """fake_quant_q4_group (src/quant.cpp:243-248) for groups of any size, with and without the
+    scale search; a zero group, a non-finite one and a group of tiny values."""
+    rng = np.random.default_rng(43 + n)
+    groups = [(rng.standard_normal(n) * 0.02).astype(np.float32), np.zeros(n, np.float32),
+              (rng.standard_normal(n) * 1e-9).astype(np.float32)]
+    bad = groups[0].copy()
+    bad[n // 2] = np.nan
+    groups.append(bad)
+    for x in groups:
+        for search in (True, False):
+            np.testing.assert_array_equal(bits(efg_lib.host_fake_quant_q4_group(x, search)),
+                                          bits(oracle.fake_quant_q4_group(x, search)))
