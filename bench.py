@@ -386,6 +386,11 @@ def config4_headline(torch, efg, args, world, rank, local, hbm_peak, barrier):
         lf.replay()
         ms_local = replay_timed(torch, lf, lr, lc, args.steps, barrier, world)
         del lf, lr
+        efg.set_q4_mma(False)  # the same local matvec on the CUDA-core kernel, for comparison
+        try:
+            ms_local_cc = time_calls(torch, local_step, args.steps, args.warmup, barrier, world) * args.steps
+        finally:
+            efg.set_q4_mma(True)
 
         # verification: this rank's slice of the gathered y equals its own local matvec bit for
         # bit, and every rank holds the same y
@@ -431,7 +436,7 @@ def config4_headline(torch, efg, args, world, rank, local, hbm_peak, barrier):
     total = algo_bytes(Q4_0, ROWS4, COLS4)
     local_bytes = shard_bytes + 4 * COLS4 + 4 * c
     return {"ms": ms, "ms_local": ms_local, "el_e2e": el, "total": total, "local_bytes": local_bytes,
-            "ms_nccl": ms_nccl,
+            "ms_nccl": ms_nccl, "ms_local_cc": ms_local_cc,
             "rows_per_rank": c, "copies": copies, "verified": ok, "gather": gather, "clocks": clocks.summary(),
             "W_host": Ws[0].cpu().numpy() if (world == 1 and not args.no_cpu_baseline) else None,
             "x_host": x.cpu().numpy()}
@@ -565,6 +570,7 @@ def run_ours(args):
                        "parallelism": f"row-sharded x{world}" if world > 1 else "single GPU"},
             "verified": h["verified"],
             "sharded_step_us": {"this_run": round(ms_step * 1e3, 3), "local_matvec_alone": round(ms_local * 1e3, 3),
+                                "local_matvec_alone_cuda_cores": round(h["ms_local_cc"] / args.steps * 1e3, 3),
                                 "with_ncclAllGather": round(h["ms_nccl"] * 1e3, 3) if h["ms_nccl"] else None},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "peak_kind": peak_kind,

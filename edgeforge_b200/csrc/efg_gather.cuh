@@ -17,8 +17,10 @@
 // Order of one launch on rank r (epoch e = epoch + 1):
 //   1. CTA 0 stores ready[r] = e into every peer's area (release, system scope).
 //   2. A warp that stores outputs first waits until ready[q] >= e here for every peer q.
-//   3. Each CTA: outputs to the local y and to every peer's y; each storing thread fences
-//      (system scope), the CTA barriers, one thread counts the CTA in `count`.
+//   3. Each CTA: outputs to the local y and to every peer's y; the CTA barriers, then one
+//      thread fences at system scope (cumulative: it orders every store the barrier ordered
+//      before it, one fence per CTA instead of one per storing thread) and counts the CTA in
+//      `count`.
 //   4. The last CTA of the launch resets `count`, fences, stores done[r] = e into every
 //      peer's area, then waits until done[q] >= e here for every peer q, and writes epoch.
 // Every wait is bounded (kWaitTimeoutNs) and records EFG_ETIMEOUT in the device error word;
@@ -93,21 +95,23 @@ __device__ __forceinline__ void gather_store(const GatherDev& g, uint32_t row, f
     if (q != g.rank) g.peer_y[q][row] = v;
 }
 
-// Steps 3 (count) and 4, by one full warp of each CTA after every storing thread of the CTA
-// has fenced (__threadfence_system) and the CTA has synchronised.
+// Steps 3 (count) and 4, by one full warp of each CTA after a CTA barrier that follows every
+// store of the CTA into the peers' y.
 __device__ __forceinline__ void gather_finish(const GatherDev& g, uint32_t epoch, int* err) {
   const int lane = threadIdx.x & 31;
   uint32_t prev = 0;
   if (lane == 0) {
-    __threadfence();
+    __threadfence_system();  // the CTA's peer stores (ordered before by the barrier), then the count
     prev = atomicAdd(g.flags + kCountOff, 1u);
   }
   prev = __shfl_sync(0xFFFFFFFFu, prev, 0);
   if (prev + 1u != gridDim.x) return;
   // The last CTA of this launch on this rank: every CTA fenced its stores before counting
   // itself; the fence below (after the count was read) orders them all before the done flags.
-  __threadfence_system();
-  if (lane == 0) *reinterpret_cast<volatile uint32_t*>(g.flags + kCountOff) = 0u;  // the next launch starts from 0
+  if (lane == 0) {
+    __threadfence_system();
+    *reinterpret_cast<volatile uint32_t*>(g.flags + kCountOff) = 0u;  // the next launch starts from 0
+  }
   __syncwarp();
   if (lane < g.nranks && lane != g.rank) st_release_sys(g.peer_flags[lane] + kDoneOff + g.rank, epoch);
   gather_wait_flags(g, kDoneOff, epoch, err);

@@ -338,8 +338,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
     }
   }
   if constexpr (GATHER) {
-    __threadfence_system();  // this thread's stores into peers' y, before the CTA is counted
-    named_barrier(kNormBarrier, nc * 32);
+    named_barrier(kNormBarrier, nc * 32);  // every store of the CTA into the peers' y is issued
     if (warp == 0) gather_finish(p.g, epoch, p.err);
   }
 }
@@ -402,8 +401,7 @@ __global__ void matvec_generic_kernel(const __grid_constant__ KParams p) {
     }
   }
   if constexpr (GATHER) {
-    __threadfence_system();
-    __syncthreads();
+    __syncthreads();  // every store of the CTA into the peers' y is issued
     if (threadIdx.x < 32) gather_finish(p.g, epoch, p.err);
   }
 }

@@ -427,8 +427,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __g
     }
   }
   if constexpr (GATHER) {
-    __threadfence_system();  // this thread's stores into peers' y, before the CTA is counted
-    named_barrier(1, nthr);
+    named_barrier(1, nthr);  // every store of the CTA into the peers' y is issued
     if (warp == 0) gather_finish(p.g, epoch, p.err);
   }
 }
