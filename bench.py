@@ -493,10 +493,22 @@ def config0_extra(torch, efg, hbm_peak, x_seed=2, launches=1280):
     g, gr, c = graphs_of(torch, step, launches, 64, chunk=640)
     g.replay()
     ms = replay_timed(torch, g, gr, c, launches, torch.cuda.synchronize, 1) / launches
-    del g, gr, W4
+    del g, gr
+    efg.set_q4_mma(False)  # the same launches on the CUDA-core kernel, for comparison
+    try:
+        g, gr, c = graphs_of(torch, step, launches, 64, chunk=640)
+        g.replay()
+        ms_cc = replay_timed(torch, g, gr, c, launches, torch.cuda.synchronize, 1) / launches
+        del g, gr
+    finally:
+        efg.set_q4_mma(True)
+    del W4
     nb = algo_bytes(Q4_0, rows, cols)
     return {"gbs": round(nb / ms / 1e6, 1), "frac_of_hbm": round(nb / ms / 1e6 / hbm_peak, 4),
-            "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": nb, "copies": copies}
+            "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": nb, "copies": copies,
+            "kernel": "small-matrix integer tensor-core kernel (weights fetched ahead, next launch co-resident)",
+            "us_per_launch_cuda_cores": round(ms_cc * 1e3, 3),
+            "frac_of_hbm_cuda_cores": round(nb / ms_cc / 1e6 / hbm_peak, 4)}
 
 
 def run_ours(args):

@@ -71,6 +71,15 @@ bool matvec_mma_ok(const MatvecArgs& a, const DeviceInfo& dev);
 int launch_matvec_q4_mma(const MatvecArgs& a, const DeviceInfo& dev, int* d_err, cudaStream_t stream,
                          bool direct_smem_attr);
 
+// The Q4_0 kernel for small matrices (efg_matvec_mma.cu): each CTA fetches all of its rows
+// into shared memory at once and is small enough that the next launch's CTA runs beside it,
+// fetching its own weights meanwhile. Taken for Q4_0 calls whose per-CTA share fits (a few MB
+// per matrix: the decode-step shapes), 2048 <= cols <= 8192, cols % 256 == 0, 16-byte aligned
+// W, x and norm weights; every epilogue, no in-kernel gather.
+bool matvec_small_ok(const MatvecArgs& a, const DeviceInfo& dev);
+int launch_matvec_q4_small(const MatvecArgs& a, const DeviceInfo& dev, int* d_err, cudaStream_t stream,
+                           bool direct_smem_attr);
+
 // launch_matvec on a caller-described device. With direct_smem_attr the kernel's
 // shared-memory limit is set by cudaFuncSetAttribute on every launch instead of through
 // the library's per-kernel cache, so the call touches no library-owned state.

@@ -112,6 +112,69 @@ __device__ __forceinline__ void mma_s8(const uint32_t (&a)[4], uint32_t b0, uint
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
+// x -> fixed-point digits of one 32-column block for the B fragments. Lane (q = lane >> 3,
+// c = lane & 7) holds columns 4c..4c+3 of block b (h, after any RMSNorm); the 8 lanes of the
+// block find its largest |x| and write its four int8 digit planes and two scales (2^(-4-s),
+// 2^(12-s)). For an odd block, columns 4c..4c+3 are B-fragment columns k = 16 v2 + 4 t + v0
+// with v2 = c / 4, t = c % 4, so digit g of the four is one 32-bit word at [t][g][v2]; even
+// blocks use the K order in which the consumers read their codes (two half-words). Returns
+// false (the same on every lane of the warp) when one of the warp's four blocks holds a
+// non-finite value or a maximum outside [2^-69, 2^100): the caller then uses plain FP32 dots,
+// so that d * 2^-s / 16 stays a normal float for every FP16 d. The 8 lanes of a block past the
+// caller's range pass write = false (and h = 0): they take part in the warp's vote and store
+// nothing.
+__device__ __forceinline__ bool x_block_digits(const float (&h)[4], uint32_t b, uint32_t c, uint8_t* xdig,
+                                               float* xsc, bool write = true) {
+  float amax = fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3])));
+  const bool fin = isfinite(h[0]) && isfinite(h[1]) && isfinite(h[2]) && isfinite(h[3]);
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127;
+  if (__any_sync(0xFFFFFFFFu, !fin || (amax != 0.f && (e < -69 || e >= 100)))) return false;
+  if (!write) return true;
+  const int s = amax == 0.f ? 0 : 29 - e;  // |x| * 2^s < 2^30; -70 <= s <= 98
+  // 2^s, 2^(-4-s) and 2^(12-s) are normal floats for these s: built from their bits.
+  // x * 2^s is exact wherever rint can see it (|x * 2^s| >= 2^-126 or it rounds to 0).
+  const float p2s = __uint_as_float(static_cast<uint32_t>(s + 127) << 23);
+  uint32_t words[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int v0 = 0; v0 < 4; ++v0) {
+    int X = __float2int_rn(h[v0] * p2s);
+    const int d0 = static_cast<int8_t>(X & 0xFF);
+    X = (X - d0) >> 8;
+    const int d1 = static_cast<int8_t>(X & 0xFF);
+    X = (X - d1) >> 8;
+    const int d2 = static_cast<int8_t>(X & 0xFF);
+    const int d3 = (X - d2) >> 8;
+    words[0] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * v0);
+    words[1] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * v0);
+    words[2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * v0);
+    words[3] |= (static_cast<uint32_t>(d3) & 0xFFu) << (8 * v0);
+  }
+  const uint32_t c3 = c & 3u, v2 = c >> 2;
+  if (b & 1u) {  // odd block: natural order, lane t holds code bytes 4t..4t+3
+    uint32_t* base = reinterpret_cast<uint32_t*>(xdig + b * 128 + c3 * 32 + v2 * 4);
+#pragma unroll
+    for (int gd = 0; gd < 4; ++gd) base[gd * 2] = words[gd];
+  } else {
+    // even block: lane t holds code bytes 2+4t..5+4t (t < 3) and 0, 1, 14, 15 (t = 3),
+    // so columns (4 c3, 4 c3 + 1) and (4 c3 + 2, 4 c3 + 3) land in two half-words
+    const uint32_t tA = c3 == 0 ? 3u : c3 - 1, vA = c3 == 0 ? 0u : 2u;
+    const uint32_t tB = c3 == 3 ? 3u : c3, vB = c3 == 3 ? 2u : 0u;
+    uint8_t* base = xdig + b * 128 + v2 * 4;
+#pragma unroll
+    for (int gd = 0; gd < 4; ++gd) {
+      *reinterpret_cast<uint16_t*>(base + tA * 32 + gd * 8 + vA) = static_cast<uint16_t>(words[gd]);
+      *reinterpret_cast<uint16_t*>(base + tB * 32 + gd * 8 + vB) = static_cast<uint16_t>(words[gd] >> 16);
+    }
+  }
+  if (c == 0) {
+    xsc[2 * b] = __uint_as_float(static_cast<uint32_t>(123 - s) << 23);      // digits 0, 1: 2^(-4-s)
+    xsc[2 * b + 1] = __uint_as_float(static_cast<uint32_t>(139 - s) << 23);  // digits 2, 3: 2^(12-s)
+  }
+  return true;
+}
+
 // Which job a row tile belongs to and its first row.
 __device__ __forceinline__ void locate_rt(const MmaParams& p, uint32_t rt, uint32_t& j, uint32_t& r0, uint32_t& nrows) {
   j = 0;
@@ -203,11 +266,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __g
     const double mean = p.cols ? tot / static_cast<double>(p.cols) : 0.0;
     inv = static_cast<float>(1.0 / sqrt(mean + static_cast<double>(p.norm_eps)));
   }
-  // x -> per-block fixed-point digits. 8 lanes per block, 4 consecutive columns per lane
-  // (one float4), 4 blocks per warp step; a warp's loads are all issued first. For an odd
-  // block, columns 4c..4c+3 are B-fragment columns k = 16 v2 + 4 t + v0 with v2 = c / 4,
-  // t = c % 4, so digit g of the four is one 32-bit word at [t][g][v2]. Even blocks use
-  // the K order in which the consumers read their codes (see below).
+  // x -> per-block fixed-point digits (x_block_digits). 8 lanes per block, 4 consecutive
+  // columns per lane (one float4), 4 blocks per warp step; a warp's loads are all issued first.
   {
     const uint32_t q = lane >> 3, c = lane & 7;
     constexpr uint32_t kSteps = kMaxBlk / (4 * kMmaConsumers) + 1;
@@ -232,56 +292,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __g
         h[2] = nw.z * (h[2] * inv);
         h[3] = nw.w * (h[3] * inv);
       }
-      float amax = fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3])));
-      const bool fin = isfinite(h[0]) && isfinite(h[1]) && isfinite(h[2]) && isfinite(h[3]);
-#pragma unroll
-      for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-      const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127;
-      // Outside 2^-69 <= max|x| < 2^100 (or non-finite) the CTA takes the FP32 path: there
-      // d * 2^-s / 16 stays a normal float for every FP16 d.
-      if (__any_sync(0xFFFFFFFFu, !fin || (amax != 0.f && (e < -69 || e >= 100)))) {
+      if (!x_block_digits(h, b, c, xdig, xsc)) {  // warp-uniform
         if (lane == 0) *bad_x = 1;
         continue;
-      }
-      const int s = amax == 0.f ? 0 : 29 - e;  // |x| * 2^s < 2^30; -70 <= s <= 98
-      // 2^s, 2^(-4-s) and 2^(12-s) are normal floats for these s: built from their bits.
-      // x * 2^s is exact wherever rint can see it (|x * 2^s| >= 2^-126 or it rounds to 0).
-      const float p2s = __uint_as_float(static_cast<uint32_t>(s + 127) << 23);
-      uint32_t words[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-      for (int v0 = 0; v0 < 4; ++v0) {
-        int X = __float2int_rn(h[v0] * p2s);
-        const int d0 = static_cast<int8_t>(X & 0xFF);
-        X = (X - d0) >> 8;
-        const int d1 = static_cast<int8_t>(X & 0xFF);
-        X = (X - d1) >> 8;
-        const int d2 = static_cast<int8_t>(X & 0xFF);
-        const int d3 = (X - d2) >> 8;
-        words[0] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * v0);
-        words[1] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * v0);
-        words[2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * v0);
-        words[3] |= (static_cast<uint32_t>(d3) & 0xFFu) << (8 * v0);
-      }
-      const uint32_t c3 = c & 3u, v2 = c >> 2;
-      if (b & 1u) {  // odd block: natural order, lane t holds code bytes 4t..4t+3
-        uint32_t* base = reinterpret_cast<uint32_t*>(xdig + b * 128 + c3 * 32 + v2 * 4);
-#pragma unroll
-        for (int gd = 0; gd < 4; ++gd) base[gd * 2] = words[gd];
-      } else {
-        // even block: lane t holds code bytes 2+4t..5+4t (t < 3) and 0, 1, 14, 15 (t = 3),
-        // so columns (4 c3, 4 c3 + 1) and (4 c3 + 2, 4 c3 + 3) land in two half-words
-        const uint32_t tA = c3 == 0 ? 3u : c3 - 1, vA = c3 == 0 ? 0u : 2u;
-        const uint32_t tB = c3 == 3 ? 3u : c3, vB = c3 == 3 ? 2u : 0u;
-        uint8_t* base = xdig + b * 128 + v2 * 4;
-#pragma unroll
-        for (int gd = 0; gd < 4; ++gd) {
-          *reinterpret_cast<uint16_t*>(base + tA * 32 + gd * 8 + vA) = static_cast<uint16_t>(words[gd]);
-          *reinterpret_cast<uint16_t*>(base + tB * 32 + gd * 8 + vB) = static_cast<uint16_t>(words[gd] >> 16);
-        }
-      }
-      if (c == 0) {
-        xsc[2 * b] = __uint_as_float(static_cast<uint32_t>(123 - s) << 23);      // digits 0, 1: 2^(-4-s)
-        xsc[2 * b + 1] = __uint_as_float(static_cast<uint32_t>(139 - s) << 23);  // digits 2, 3: 2^(12-s)
       }
     }
   }
@@ -479,6 +492,261 @@ bool encode_w_map(CUtensorMap* m, const uint8_t* W, uint32_t rows, uint32_t rb) 
   return encode_u64_rows_map(m, W, rows, rb, kBoxElems, kTileRows);
 }
 
+// ------------------------------------------------------------------ small matrices
+// Q4_0 matrices of a few MB (every decode-step matrix of a TinyLlama-sized model) are bound by
+// the chain of dependent launches, not by HBM: a matvec can only start on x once the kernel
+// that wrote x has finished. This kernel is shaped for that chain:
+//  * Each CTA owns a few 8-row units (8 rows of every K segment) and fetches all of their
+//    bytes with 2-D TMA copies the moment it starts, before waiting for the previous kernel
+//    (the weights are static: weight prefetch). It needs at most ~100 KB of shared memory and
+//    256 threads, so the next launch's CTA fits beside it on the same SM and fetches its own
+//    weights while this one computes: the weight stream of launch i + 1 overlaps launch i.
+//  * After the grid-dependency wait, each of the 8 warps reads only its own K range of x
+//    (one round of float4 loads), turns it into fixed-point digits (x_block_digits) in its
+//    own piece of shared memory, and multiplies it against every unit of the CTA with the
+//    exact integer MMA of the large kernel: one m16n8k32 per 8 rows and block pair.
+//  * The warps' row partials meet once in shared memory and are added in warp order (one
+//    CTA barrier), so results are deterministic. RMSNorm, residual-add, SwiGLU (gate and up
+//    units side by side) and a device-side output position are fused as in the other kernels.
+constexpr int kSmallWarps = 8;
+constexpr int kSmallThreads = kSmallWarps * 32;
+constexpr uint32_t kUnitRows = 8;
+constexpr uint32_t kSlotBytes = kUnitRows * kRowStride;  // one 8-row box of one K segment: 9344
+constexpr uint32_t kSmallMaxSlots = 10;                  // units x matrices x segments per CTA
+constexpr uint32_t kSmallMaxUnits = 10;
+constexpr size_t kSmallSmemCap = 108 * 1024;             // two CTAs (two launches) per SM
+
+struct SmallParams {
+  CUtensorMap maps[kMaxJobs];  // W as [rows][rb / 8] u64, box {146, 8}
+  const float* x;
+  const float* norm_w;
+  float norm_eps;
+  int* err;
+  const int32_t* pos;
+  uint32_t cols, nblk, nseg, npairs;
+  uint32_t units_total, n_jobs;  // SwiGLU: one unit space (gate's), two matrices per unit
+  uint32_t job_unit_start[kMaxJobs + 1];
+  MatvecJobDev jobs[kMaxJobs];
+  uint32_t xsc_offset, xdig_offset, red_offset, w_offset;
+};
+
+__device__ __forceinline__ void locate_unit(const SmallParams& p, uint32_t u, uint32_t& j, uint32_t& r0,
+                                            uint32_t& nrows) {
+  j = 0;
+  while (j + 1 < p.n_jobs && u >= p.job_unit_start[j + 1]) ++j;
+  r0 = (u - p.job_unit_start[j]) * kUnitRows;
+  nrows = min(kUnitRows, p.jobs[j].rows - r0);
+}
+
+template <Epi E, bool NORM>
+__global__ void __launch_bounds__(kSmallThreads, 2) matvec_q4_small_kernel(const __grid_constant__ SmallParams p) {
+  constexpr uint32_t NM = E == Epi::SwiGLU ? 2 : 1;  // matrices per unit
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);            // [kSmallMaxUnits]
+  double* dred = reinterpret_cast<double*>(smem + 128);         // [kSmallWarps]
+  float* xsc = reinterpret_cast<float*>(smem + p.xsc_offset);   // [nblk][2]
+  uint8_t* xdig = smem + p.xdig_offset;                         // [nblk][128]
+  float* red = reinterpret_cast<float*>(smem + p.red_offset);   // [warp][unit][NM][8]
+  uint8_t* wbuf = smem + p.w_offset;                            // [unit][NM][seg] slots
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t u_b = static_cast<uint32_t>(static_cast<uint64_t>(p.units_total) * blockIdx.x / gridDim.x);
+  const uint32_t u_e = static_cast<uint32_t>(static_cast<uint64_t>(p.units_total) * (blockIdx.x + 1) / gridDim.x);
+  const uint32_t nu = u_e - u_b;
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < nu; ++i) mbar_init(&bar[i], 1);
+    fence_barrier_init();
+    const uint64_t pol = l2_evict_first_policy();
+    for (uint32_t i = 0; i < nu; ++i) {
+      uint32_t j, r0, nrows;
+      locate_unit(p, u_b + i, j, r0, nrows);
+      mbar_arrive_expect_tx(&bar[i], NM * p.nseg * kSlotBytes);
+      for (uint32_t m = 0; m < NM; ++m)
+        for (uint32_t ks = 0; ks < p.nseg; ++ks)
+          tma_load_2d(wbuf + ((i * NM + m) * p.nseg + ks) * kSlotBytes, &p.maps[E == Epi::SwiGLU ? m : j],
+                      static_cast<int32_t>(ks * kSegBlk * 18 / 8), static_cast<int32_t>(r0), &bar[i], pol);
+    }
+  }
+  __syncthreads();  // the barriers are initialised before anyone waits on them
+  pdl_launch_dependents();
+
+  // this warp's K range: block pairs [p0, p1) of every row, blocks [2 p0, 2 p1)
+  const uint32_t p0 = p.npairs * warp / kSmallWarps, p1 = p.npairs * (warp + 1) / kSmallWarps;
+  const uint32_t b0 = 2 * p0, nb = 2 * (p1 - p0);
+  constexpr uint32_t kSteps = kMaxBlk / kSmallWarps / 4 + 1;  // float4 loads per lane, at most
+  const uint32_t q = lane >> 3, c = lane & 7;
+  float4 nwv[kSteps];
+  if constexpr (NORM) {  // model constants: fetched before the wait
+#pragma unroll
+    for (uint32_t i = 0; i < kSteps; ++i) {
+      const uint32_t k = i * 4 + q;
+      nwv[i] = k < nb ? __ldg(reinterpret_cast<const float4*>(p.norm_w) + (b0 + k) * 8 + c)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  pdl_wait();  // x (and y for the add epilogue) belong to the previous kernel in the stream
+  float4 hv[kSteps];
+#pragma unroll
+  for (uint32_t i = 0; i < kSteps; ++i) {
+    const uint32_t k = i * 4 + q;
+    hv[i] = k < nb ? __ldg(reinterpret_cast<const float4*>(p.x) + (b0 + k) * 8 + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float inv = 1.f;
+  if constexpr (NORM) {  // rmsnorm scale (src/kernels.cpp:69-73): double sum of squares of all x
+    double ss = 0.0;
+#pragma unroll
+    for (uint32_t i = 0; i < kSteps; ++i) {
+      ss += static_cast<double>(hv[i].x) * static_cast<double>(hv[i].x);
+      ss += static_cast<double>(hv[i].y) * static_cast<double>(hv[i].y);
+      ss += static_cast<double>(hv[i].z) * static_cast<double>(hv[i].z);
+      ss += static_cast<double>(hv[i].w) * static_cast<double>(hv[i].w);
+    }
+    ss = warp_sum_d(ss);
+    if (lane == 0) dred[warp] = ss;
+    __syncthreads();
+    double tot = 0.0;
+    for (int w = 0; w < kSmallWarps; ++w) tot += dred[w];
+    const double mean = p.cols ? tot / static_cast<double>(p.cols) : 0.0;
+    inv = static_cast<float>(1.0 / sqrt(mean + static_cast<double>(p.norm_eps)));
+  }
+  bool fast = true;
+#pragma unroll
+  for (uint32_t i = 0; i < kSteps; ++i) {
+    if (i * 4 >= nb) break;  // uniform per warp
+    const uint32_t k = i * 4 + q;
+    float h[4] = {hv[i].x, hv[i].y, hv[i].z, hv[i].w};
+    if constexpr (NORM) {  // w * (x * inv), src/kernels.cpp:74
+      h[0] = nwv[i].x * (h[0] * inv);
+      h[1] = nwv[i].y * (h[1] * inv);
+      h[2] = nwv[i].z * (h[2] * inv);
+      h[3] = nwv[i].w * (h[3] * inv);
+    }
+    // lanes past this warp's range (k >= nb) carry zeros, vote, and store nothing
+    fast = x_block_digits(h, b0 + (k < nb ? k : 0u), c, xdig, xsc, k < nb) && fast;
+  }
+  __syncwarp();
+
+  // Lane (g, t): row g of the unit, as in the large kernel (one useful digit-pair sum per MMA).
+  const uint32_t g = lane >> 2, t = lane & 3;
+  const uint32_t x1_off = 1 + t, x2_off = t == 2 ? 4u : 0u;
+  const uint32_t sel_code = t == 3 ? 0x1076u : 0x3210u;
+  const uint32_t sel_d = t < 2 ? 0x5454u : (t == 2 ? 0x7676u : 0x3232u);
+  const bool c_hi = t >= 2;
+  const uint2* xd = reinterpret_cast<const uint2*>(xdig + (g >> 2) * 128 + (t * 4 + (g & 3u)) * 8);
+  const float* xs_l = xsc + t;
+  bool ok = true;
+  for (uint32_t i = 0; i < nu; ++i) {
+    ok = ok && mbar_wait(&bar[i], 0, p.err);
+    for (uint32_t m = 0; m < NM; ++m) {
+      float acc = 0.f;
+      const uint8_t* slot0 = wbuf + (i * NM + m) * p.nseg * kSlotBytes;
+      if (ok && fast) {
+#pragma unroll 4
+        for (uint32_t pr = p0; pr < p1; ++pr) {
+          const uint32_t ks = pr / (kSegBlk / 2), w = (pr % (kSegBlk / 2)) * 9;
+          const uint32_t* rw = reinterpret_cast<const uint32_t*>(slot0 + ks * kSlotBytes + g * kRowStride);
+          const uint32_t X1 = rw[w + x1_off], X2 = rw[w + x2_off], Y = rw[w + 5 + t];
+          const uint32_t ce = __byte_perm(X1, X2, sel_code), db = __byte_perm(X1, X2, sel_d);
+          const uint2 bf = xd[2 * pr * 16];
+          const float sc = xs_l[4 * pr];
+          const uint32_t a[4] = {a_lo(ce), a_lo(Y), a_hi(ce), a_hi(Y)};
+          int cc[4];
+          mma_s8(a, bf.x, bf.y, cc);
+          const int v = (c_hi ? cc[2] : cc[0]) + ((c_hi ? cc[3] : cc[1]) << 8);
+          acc = fmaf(static_cast<float>(v), half_bits_to_float(db) * sc, acc);
+        }
+        acc += __shfl_xor_sync(0xFFFFFFFFu, acc, 1);
+        acc += __shfl_xor_sync(0xFFFFFFFFu, acc, 2);
+      } else if (ok) {
+        // plain FP32 dots of this warp's blocks (non-finite or out-of-range x): row r's sum
+        // lands in lane 4 r, where the MMA path leaves it
+        for (uint32_t r = 0; r < kUnitRows; ++r) {
+          float part = 0.f;
+          for (uint32_t bb = b0 + lane; bb < b0 + nb; bb += 32) {
+            const uint8_t* blkp = slot0 + (bb / kSegBlk) * kSlotBytes + r * kRowStride + (bb % kSegBlk) * 18;
+            const float d = fp16_to_f32(blkp[0] | (blkp[1] << 8));
+            float sacc = 0.f;
+            for (int k = 0; k < 32; ++k) {
+              const int cd = (k < 16 ? (blkp[2 + k] & 15) : (blkp[2 + k - 16] >> 4)) - 8;
+              float xv = __ldg(p.x + bb * 32 + k);
+              if constexpr (NORM) xv = __ldg(p.norm_w + bb * 32 + k) * (xv * inv);
+              sacc += static_cast<float>(cd) * xv;
+            }
+            part += d * sacc;
+          }
+          part = warp_sum(part);
+          if (g == r) acc = part;
+        }
+      }
+      if (t == 0) red[((warp * kSmallMaxUnits + i) * NM + m) * kUnitRows + g] = acc;
+    }
+  }
+  __syncthreads();
+  // one thread per (unit, row): the warps' partials in warp order, then the epilogue
+  const uint32_t tid = threadIdx.x;
+  if (ok && tid < nu * kUnitRows) {
+    const uint32_t i = tid / kUnitRows, r = tid % kUnitRows;
+    uint32_t j, r0, nrows;
+    locate_unit(p, u_b + i, j, r0, nrows);
+    if (r < nrows) {
+      float v[NM];
+#pragma unroll
+      for (uint32_t m = 0; m < NM; ++m) {
+        float s = 0.f;
+        for (int w = 0; w < kSmallWarps; ++w) s += red[((w * kSmallMaxUnits + i) * NM + m) * kUnitRows + r];
+        v[m] = s;
+      }
+      float* y = p.jobs[j].y + (p.pos ? *p.pos * p.jobs[j].y_pos_stride : 0);
+      if constexpr (E == Epi::SwiGLU) y[r0 + r] = silu(v[0]) * v[NM - 1];
+      else if constexpr (E == Epi::Add) y[r0 + r] += v[0];
+      else y[r0 + r] = v[0];
+    }
+  }
+}
+
+using SmallFn = void (*)(SmallParams);
+
+SmallFn pick_small(Epi e, bool norm) {
+  switch (e) {
+    case Epi::Store: return norm ? matvec_q4_small_kernel<Epi::Store, true> : matvec_q4_small_kernel<Epi::Store, false>;
+    case Epi::Add: return norm ? matvec_q4_small_kernel<Epi::Add, true> : matvec_q4_small_kernel<Epi::Add, false>;
+    case Epi::SwiGLU:
+      return norm ? matvec_q4_small_kernel<Epi::SwiGLU, true> : matvec_q4_small_kernel<Epi::SwiGLU, false>;
+  }
+  return nullptr;
+}
+
+struct SmallPlan {
+  uint32_t nblk, nseg, units, grid;
+  uint32_t xsc_offset, xdig_offset, red_offset, w_offset;
+  size_t smem;
+};
+
+// The small kernel's plan, or false when the call does not fit it (then the other kernels run).
+bool plan_small(const MatvecArgs& a, const DeviceInfo& dev, SmallPlan& pl) {
+  if (a.fmt != Fmt::Q4 || a.gather.nranks > 0) return false;
+  if (a.cols == 0 || a.cols % 256 != 0 || a.cols / 32 < kMinBlk || a.cols / 32 > kMaxBlk) return false;
+  if (reinterpret_cast<uintptr_t>(a.x) % 16 != 0 || reinterpret_cast<uintptr_t>(a.norm_w) % 16 != 0) return false;
+  const int n_mat = a.epi == Epi::SwiGLU ? 2 : a.n_jobs;
+  const uint32_t NM = a.epi == Epi::SwiGLU ? 2 : 1;
+  uint64_t units = 0;
+  for (int j = 0; j < n_mat; ++j)
+    if (reinterpret_cast<uintptr_t>(a.jobs[j].W) % 16 != 0) return false;
+  for (int j = 0; j < (a.epi == Epi::SwiGLU ? 1 : a.n_jobs); ++j) units += (a.jobs[j].rows + kUnitRows - 1) / kUnitRows;
+  if (units == 0) return false;
+  pl.nblk = static_cast<uint32_t>(a.cols / 32);
+  pl.nseg = (pl.nblk + kSegBlk - 1) / kSegBlk;
+  pl.units = static_cast<uint32_t>(units);
+  pl.grid = static_cast<uint32_t>(std::min<uint64_t>(units, static_cast<uint64_t>(dev.sm_count)));
+  const uint32_t upc = (pl.units + pl.grid - 1) / pl.grid;
+  if (upc > kSmallMaxUnits || upc * NM * pl.nseg > kSmallMaxSlots) return false;
+  pl.xsc_offset = 256;
+  pl.xdig_offset = (pl.xsc_offset + pl.nblk * 8 + 127) / 128 * 128;
+  pl.red_offset = pl.xdig_offset + pl.nblk * 128;
+  pl.w_offset = (pl.red_offset + kSmallWarps * kSmallMaxUnits * NM * kUnitRows * 4 + 127) / 128 * 128;
+  pl.smem = pl.w_offset + static_cast<size_t>(upc) * NM * pl.nseg * kSlotBytes;
+  return pl.smem <= kSmallSmemCap && pl.smem <= dev.smem_optin;
+}
+
 }  // namespace
 
 bool matvec_mma_ok(const MatvecArgs& a, const DeviceInfo& dev) {
@@ -543,6 +811,72 @@ int launch_matvec_q4_mma(const MatvecArgs& a, const DeviceInfo& dev, int* d_err,
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(std::min<uint32_t>(rt, static_cast<uint32_t>(dev.sm_count)));
   cfg.blockDim = dim3(kMmaThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, fn, p), "matvec launch");
+  return EFG_OK;
+}
+
+bool matvec_small_ok(const MatvecArgs& a, const DeviceInfo& dev) {
+  SmallPlan pl;
+  if (!plan_small(a, dev, pl)) return false;
+  CUtensorMap m;  // the driver must accept every matrix's map
+  const int n_mat = a.epi == Epi::SwiGLU ? 2 : a.n_jobs;
+  for (int j = 0; j < n_mat; ++j)
+    if (a.jobs[j].rows && !encode_u64_rows_map(&m, a.jobs[j].W, a.jobs[j].rows, a.cols / 32 * 18, kBoxElems, kUnitRows))
+      return false;
+  return true;
+}
+
+int launch_matvec_q4_small(const MatvecArgs& a, const DeviceInfo& dev, int* d_err, cudaStream_t stream,
+                           bool direct_smem_attr) {
+  SmallPlan pl;
+  if (!plan_small(a, dev, pl)) return fail(EFG_EINVAL, "matvec: no small-matrix plan for this call");
+  SmallParams p{};
+  p.x = a.x;
+  p.norm_w = a.norm_w;
+  p.norm_eps = a.norm_eps;
+  p.err = d_err;
+  p.pos = a.pos;
+  p.cols = static_cast<uint32_t>(a.cols);
+  p.nblk = pl.nblk;
+  p.nseg = pl.nseg;
+  p.npairs = pl.nblk / 2;
+  p.units_total = pl.units;
+  p.xsc_offset = pl.xsc_offset;
+  p.xdig_offset = pl.xdig_offset;
+  p.red_offset = pl.red_offset;
+  p.w_offset = pl.w_offset;
+  const int n_mat = a.epi == Epi::SwiGLU ? 2 : a.n_jobs;
+  p.n_jobs = static_cast<uint32_t>(a.epi == Epi::SwiGLU ? 1 : a.n_jobs);
+  const uint32_t rb = pl.nblk * 18;
+  for (int j = 0; j < n_mat; ++j) {
+    p.jobs[j] = a.jobs[j];
+    if (a.jobs[j].rows && !encode_u64_rows_map(&p.maps[j], a.jobs[j].W, a.jobs[j].rows, rb, kBoxElems, kUnitRows))
+      return fail(EFG_ECUDA, "matvec: tensor map for a %u x %u Q4_0 matrix", a.jobs[j].rows, p.cols);
+  }
+  uint32_t u = 0;
+  for (uint32_t j = 0; j < p.n_jobs; ++j) {
+    p.job_unit_start[j] = u;
+    u += (a.jobs[j].rows + kUnitRows - 1) / kUnitRows;
+  }
+  p.job_unit_start[p.n_jobs] = u;
+  SmallFn fn = pick_small(a.epi, a.norm_w != nullptr);
+  if (direct_smem_attr) {
+    EFG_TRY_CUDA(cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(pl.smem)),
+                 "kernel shared-memory attribute");
+  } else if (int st = ensure_smem_attr(reinterpret_cast<const void*>(fn), pl.smem)) {
+    return st;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kSmallThreads);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
