@@ -38,4 +38,13 @@ struct GemmCall {
 };
 int launch_gemm(const GemmCall& c, int* d_err, cudaStream_t s);
 
+struct DeviceInfo;
+// The Q4_0 GEMM for small batches (B <= 64) on the exact integer MMA (efg_matvec_mma.cu): the
+// X columns as the A operand in int8 digit planes, the codes as B; each CTA fetches its 8-row
+// units whole at its start. Taken for Q4_0 calls with 2048 <= K <= 8192, K % 256 == 0, 16-byte
+// aligned weights and X, and a per-CTA share that fits in shared memory; columns with
+// non-finite x come out as the FP32 matvec computes them. One launch, no scratch.
+bool gemm_q4_small_ok(const GemmCall& c, const DeviceInfo& dev);
+int launch_gemm_q4_small(const GemmCall& c, const DeviceInfo& dev, int* d_err, cudaStream_t s);
+
 }  // namespace efg

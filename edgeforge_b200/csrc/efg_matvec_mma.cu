@@ -47,6 +47,7 @@
 #include "efg_device.cuh"
 #include "efg_dot.cuh"
 #include "efg_gather.cuh"
+#include "efg_gemm.cuh"
 #include "efg_host.h"
 #include "efg_matvec.cuh"
 
@@ -747,6 +748,283 @@ bool plan_small(const MatvecArgs& a, const DeviceInfo& dev, SmallPlan& pl) {
   return pl.smem <= kSmallSmemCap && pl.smem <= dev.smem_optin;
 }
 
+// ------------------------------------------------------------------ small-batch GEMM
+// Y[b][m] = sum_k W[m][k] X[b][k] for B <= 64 columns of X (a short prompt, a few decoded
+// sequences): the reference's per-column matvec loop (src/qkernels.cpp:275-297) in one launch
+// on the same exact integer MMA, with the roles turned around so that no output is wasted:
+//  * A (16 x 32): 16 columns of X, one int8 digit plane of their fixed-point form per MMA
+//    (digit g of round(x 2^s), s per column and block), K in natural column order;
+//  * B (32 x 8): the codes of 8 weight rows of one block, (c - 8) * 16 as int8, taken from
+//    one code word per lane (bytes 4t..4t+3 hold columns 4t..4t+3 and 16+4t..19+4t, exactly
+//    the fragment's K split);
+//  * four MMAs (the digit planes) give 16 x 8 exact int32 dot products of the block; digits
+//    0, 1 and 2, 3 are combined in integers, and each pair becomes a float scaled by
+//    d * 2^-s / 16 (2^(16-s) / 16) and accumulates in FP32, as in the matvec kernels.
+// A CTA owns a few 8-row units, fetched whole with 2-D TMA copies at its start (before the
+// grid-dependency wait: static weights). X is turned into digits in chunks of 8 blocks by all
+// threads into a double-buffered shared area (one barrier per chunk); warp w multiplies block
+// w of each chunk against every unit, so each warp's sums cover the blocks w mod 8 and the 8
+// partial sums are added in warp order at the end (deterministic). A column whose X holds a
+// non-finite value or a block maximum outside [2^-69, 2^100) is computed afterwards with
+// plain FP32 dots, so every column equals what the FP32 matvec arithmetic gives.
+constexpr int kSgWarps = 8;
+constexpr int kSgThreads = kSgWarps * 32;
+constexpr uint32_t kSgCols = 16;                      // columns of X per MMA tile
+constexpr uint32_t kSgChunk = 8;                      // blocks per staged chunk (one per warp)
+constexpr uint32_t kSgColStride = 48;                 // bytes per column and digit plane (32 + pad)
+constexpr uint32_t kSgPlaneBytes = kSgCols * kSgColStride;              // 768
+constexpr uint32_t kSgBlockBytes = 4 * kSgPlaneBytes;                   // 3072
+constexpr uint32_t kSgBufBytes = kSgChunk * kSgBlockBytes;              // 24 KB
+constexpr uint32_t kSgMaxUnits = 10;
+constexpr uint32_t kSgMaxSlots = 18;
+constexpr uint32_t kSgMaxB = 64;
+constexpr uint32_t kSgMaxJobs = 3;
+
+struct SmallGemmParams {
+  CUtensorMap maps[kSgMaxJobs];  // W as [rows][rb / 8] u64, box {146, 8}
+  const float* X;                // [B][K]
+  float* Y[kSgMaxJobs];          // [B][M_j]
+  uint32_t M[kSgMaxJobs];
+  uint32_t K, nblk, nseg, B, n_jobs, units_total, accumulate;
+  uint32_t job_unit_start[kSgMaxJobs + 1];
+  int* err;
+  uint32_t xs_offset, xd_offset, w_offset;
+};
+
+__device__ __forceinline__ void sg_locate(const SmallGemmParams& p, uint32_t u, uint32_t& j, uint32_t& r0) {
+  j = 0;
+  while (j + 1 < p.n_jobs && u >= p.job_unit_start[j + 1]) ++j;
+  r0 = (u - p.job_unit_start[j]) * kUnitRows;
+}
+
+__global__ void __launch_bounds__(kSgThreads, 1) gemm_q4_small_kernel(const __grid_constant__ SmallGemmParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);         // [kSgMaxUnits]
+  uint32_t* badcol = reinterpret_cast<uint32_t*>(smem + 96);  // one bit per column (B <= 64)
+  float* xs = reinterpret_cast<float*>(smem + p.xs_offset);   // [2 buf][kSgChunk][kSgCols][2]
+  uint8_t* xd = smem + p.xd_offset;                           // [2 buf][kSgChunk][4 plane][16 col][48 B]
+  uint8_t* wbuf = smem + p.w_offset;                          // [unit][seg] slots
+  float* red = reinterpret_cast<float*>(xd);                  // after the MMAs: [warp][unit][128]
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const uint32_t u_b = static_cast<uint32_t>(static_cast<uint64_t>(p.units_total) * blockIdx.x / gridDim.x);
+  const uint32_t u_e = static_cast<uint32_t>(static_cast<uint64_t>(p.units_total) * (blockIdx.x + 1) / gridDim.x);
+  const uint32_t nu = u_e - u_b;
+  if (tid == 0) {
+    for (uint32_t i = 0; i < nu; ++i) mbar_init(&bar[i], 1);
+    badcol[0] = 0u;
+    badcol[1] = 0u;
+    fence_barrier_init();
+    const uint64_t pol = l2_evict_first_policy();
+    for (uint32_t i = 0; i < nu; ++i) {
+      uint32_t j, r0;
+      sg_locate(p, u_b + i, j, r0);
+      mbar_arrive_expect_tx(&bar[i], p.nseg * kSlotBytes);
+      for (uint32_t ks = 0; ks < p.nseg; ++ks)
+        tma_load_2d(wbuf + (i * p.nseg + ks) * kSlotBytes, &p.maps[j], static_cast<int32_t>(ks * kSegBlk * 18 / 8),
+                    static_cast<int32_t>(r0), &bar[i], pol);
+    }
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+  pdl_wait();  // X (and Y when adding) belong to the previous kernel in the stream
+
+  const uint32_t gq = lane >> 2, t = lane & 3;  // A rows (columns of X) gq, gq + 8; B column (row) gq
+  const uint32_t n_chunks = p.nblk / kSgChunk;
+  const uint32_t n_ct = (p.B + kSgCols - 1) / kSgCols;
+  bool ok = true, waited = false;
+  for (uint32_t ct = 0; ct < n_ct; ++ct) {
+    const uint32_t col0 = ct * kSgCols;
+    float acc[kSgMaxUnits][4];
+#pragma unroll
+    for (uint32_t i = 0; i < kSgMaxUnits; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    for (uint32_t kc = 0; kc < n_chunks; ++kc) {
+      const uint32_t buf = (ct * n_chunks + kc) & 1u;
+      // ---- X chunk -> digits: item = (column, block, 4-value group); 8 lanes share a block
+      {
+        uint8_t* xdb = xd + buf * kSgBufBytes;
+        float* xsb = xs + buf * kSgChunk * kSgCols * 2;
+        const uint32_t c8 = lane & 7;
+#pragma unroll
+        for (uint32_t it = 0; it < (kSgCols * kSgChunk * 8) / kSgThreads; ++it) {
+          const uint32_t item = (it * kSgThreads + tid) >> 3;   // (column, block) pair of these 8 lanes
+          const uint32_t col = item / kSgChunk, bi = item % kSgChunk;
+          const uint32_t gcol = col0 + col, blk = kc * kSgChunk + bi;
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (gcol < p.B) v = __ldg(reinterpret_cast<const float4*>(p.X + static_cast<size_t>(gcol) * p.K + blk * 32) + c8);
+          float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+          const bool fin = isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+#pragma unroll
+          for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+          const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 127;
+          const bool bad = !fin || (amax != 0.f && (e < -69 || e >= 100));
+          if (bad && gcol < p.B) atomicOr(&badcol[gcol >> 5], 1u << (gcol & 31));
+          const int s = (amax == 0.f || bad) ? 0 : 29 - e;
+          const float p2s = __uint_as_float(static_cast<uint32_t>(s + 127) << 23);
+          const float h[4] = {v.x, v.y, v.z, v.w};
+          uint32_t words[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+          for (int v0 = 0; v0 < 4; ++v0) {
+            int X = bad ? 0 : __float2int_rn(h[v0] * p2s);
+            const int d0 = static_cast<int8_t>(X & 0xFF);
+            X = (X - d0) >> 8;
+            const int d1 = static_cast<int8_t>(X & 0xFF);
+            X = (X - d1) >> 8;
+            const int d2 = static_cast<int8_t>(X & 0xFF);
+            const int d3 = (X - d2) >> 8;
+            words[0] |= (static_cast<uint32_t>(d0) & 0xFFu) << (8 * v0);
+            words[1] |= (static_cast<uint32_t>(d1) & 0xFFu) << (8 * v0);
+            words[2] |= (static_cast<uint32_t>(d2) & 0xFFu) << (8 * v0);
+            words[3] |= (static_cast<uint32_t>(d3) & 0xFFu) << (8 * v0);
+          }
+          uint8_t* dst = xdb + bi * kSgBlockBytes + col * kSgColStride + c8 * 4;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) *reinterpret_cast<uint32_t*>(dst + g * kSgPlaneBytes) = words[g];
+          if (c8 == 0) {
+            xsb[(bi * kSgCols + col) * 2] = __uint_as_float(static_cast<uint32_t>(123 - s) << 23);      // 2^(-4-s)
+            xsb[(bi * kSgCols + col) * 2 + 1] = __uint_as_float(static_cast<uint32_t>(139 - s) << 23);  // 2^(12-s)
+          }
+        }
+      }
+      __syncthreads();  // the chunk's digits are in place; the other buffer is free again
+      if (!waited) {    // the weights arrive once
+        for (uint32_t i = 0; i < nu; ++i) ok = mbar_wait(&bar[i], 0, p.err) && ok;
+        waited = true;
+      }
+      if (!ok) continue;
+      // ---- MMAs: warp w takes block w of the chunk, against every unit
+      const uint32_t blk = kc * kSgChunk + warp;
+      const uint8_t* xdb = xd + buf * kSgBufBytes + warp * kSgBlockBytes;
+      const float* xsb = xs + (buf * kSgChunk + warp) * kSgCols * 2;
+      uint32_t a[4][4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const uint8_t* pl = xdb + g * kSgPlaneBytes;
+        a[g][0] = *reinterpret_cast<const uint32_t*>(pl + gq * kSgColStride + 4 * t);
+        a[g][1] = *reinterpret_cast<const uint32_t*>(pl + (gq + 8) * kSgColStride + 4 * t);
+        a[g][2] = *reinterpret_cast<const uint32_t*>(pl + gq * kSgColStride + 16 + 4 * t);
+        a[g][3] = *reinterpret_cast<const uint32_t*>(pl + (gq + 8) * kSgColStride + 16 + 4 * t);
+      }
+      const float s01_a = xsb[gq * 2], s23_a = xsb[gq * 2 + 1];                // column gq
+      const float s01_b = xsb[(gq + 8) * 2], s23_b = xsb[(gq + 8) * 2 + 1];    // column gq + 8
+      const uint32_t seg = blk / kSegBlk, jb = (blk % kSegBlk) * 18;
+#pragma unroll
+      for (uint32_t i = 0; i < kSgMaxUnits; ++i) {  // unrolled: acc stays in registers
+        if (i >= nu) break;
+        const uint8_t* slot = wbuf + (i * p.nseg + seg) * kSlotBytes + jb;
+        // this lane's code word: bytes 4t..4t+3 of row gq's 16 code bytes (2 bytes into the block)
+        const uint8_t* cp = slot + gq * kRowStride + 2 + 4 * t;
+        uint32_t cw;
+        if (blk & 1u) {
+          cw = *reinterpret_cast<const uint32_t*>(cp);
+        } else {
+          const uint32_t w0 = *reinterpret_cast<const uint32_t*>(cp - 2), w1 = *reinterpret_cast<const uint32_t*>(cp + 2);
+          cw = __byte_perm(w0, w1, 0x5432);
+        }
+        const uint32_t b0 = a_lo(cw), b1 = a_hi(cw);
+        // the fp16 scales of rows 2t and 2t + 1 (this lane's two output rows)
+        const float d0 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(slot + (2 * t) * kRowStride));
+        const float d1 = half_bits_to_float(*reinterpret_cast<const uint16_t*>(slot + (2 * t + 1) * kRowStride));
+        int c[4][4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) mma_s8(a[g], b0, b1, c[g]);
+        // c[g][0..3]: (column gq, row 2t), (gq, 2t + 1), (gq + 8, 2t), (gq + 8, 2t + 1)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int v01 = c[0][q] + (c[1][q] << 8), v23 = c[2][q] + (c[3][q] << 8);
+          const float d = (q & 1) ? d1 : d0;
+          const float s01 = q < 2 ? s01_a : s01_b, s23 = q < 2 ? s23_a : s23_b;
+          acc[i][q] = fmaf(static_cast<float>(v01), d * s01, acc[i][q]);
+          acc[i][q] = fmaf(static_cast<float>(v23), d * s23, acc[i][q]);
+        }
+      }
+    }
+    // ---- the warps' sums over their blocks, added in warp order
+    __syncthreads();  // every MMA of this column tile has read its digits
+#pragma unroll
+    for (uint32_t i = 0; i < kSgMaxUnits; ++i) {
+      if (i >= nu) break;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t col = gq + (q >> 1) * 8, row = 2 * t + (q & 1);
+        red[(warp * kSgMaxUnits + i) * 128 + col * 8 + row] = acc[i][q];
+      }
+    }
+    __syncthreads();
+    const uint32_t bad_lo = badcol[0], bad_hi = badcol[1];
+    for (uint32_t e = tid; e < nu * 128; e += kSgThreads) {
+      const uint32_t i = e / 128, col = (e % 128) / 8, row = e % 8;
+      const uint32_t gcol = col0 + col;
+      uint32_t j, r0;
+      sg_locate(p, u_b + i, j, r0);
+      if (!ok || gcol >= p.B || r0 + row >= p.M[j]) continue;
+      if (((gcol < 32 ? bad_lo >> gcol : bad_hi >> (gcol - 32)) & 1u) != 0u) continue;  // FP32 path below
+      float v = 0.f;
+      for (int w = 0; w < kSgWarps; ++w) v += red[(w * kSgMaxUnits + i) * 128 + col * 8 + row];
+      float* y = p.Y[j] + static_cast<size_t>(gcol) * p.M[j] + r0 + row;
+      *y = p.accumulate ? *y + v : v;
+    }
+    __syncthreads();  // red (the digit area) is rewritten by the next column tile
+  }
+  // ---- columns with non-finite or out-of-range x: plain FP32 dots, one warp per (row, column)
+  const uint32_t bad_lo = badcol[0], bad_hi = badcol[1];
+  if (ok && (bad_lo | bad_hi) != 0u) {
+    for (uint32_t e = warp; e < nu * kUnitRows * p.B; e += kSgWarps) {
+      const uint32_t gcol = e % p.B, rr = e / p.B, i = rr / kUnitRows, row = rr % kUnitRows;
+      if (((gcol < 32 ? bad_lo >> gcol : bad_hi >> (gcol - 32)) & 1u) == 0u) continue;
+      uint32_t j, r0;
+      sg_locate(p, u_b + i, j, r0);
+      if (r0 + row >= p.M[j]) continue;
+      const float* xr = p.X + static_cast<size_t>(gcol) * p.K;
+      float part = 0.f;
+      for (uint32_t bb = lane; bb < p.nblk; bb += 32) {
+        const uint8_t* blkp = wbuf + (i * p.nseg + bb / kSegBlk) * kSlotBytes + row * kRowStride + (bb % kSegBlk) * 18;
+        const float d = fp16_to_f32(blkp[0] | (blkp[1] << 8));
+        float sacc = 0.f;
+        for (int k = 0; k < 32; ++k) {
+          const int cd = (k < 16 ? (blkp[2 + k] & 15) : (blkp[2 + k - 16] >> 4)) - 8;
+          sacc += static_cast<float>(cd) * __ldg(xr + bb * 32 + k);
+        }
+        part += d * sacc;
+      }
+      part = warp_sum(part);
+      if (lane == 0) {
+        float* y = p.Y[j] + static_cast<size_t>(gcol) * p.M[j] + r0 + row;
+        *y = p.accumulate ? *y + part : part;
+      }
+    }
+  }
+}
+
+struct SmallGemmPlan {
+  uint32_t nblk, nseg, units, grid;
+  uint32_t xs_offset, xd_offset, w_offset;
+  size_t smem;
+};
+
+bool plan_small_gemm(const GemmCall& c, const DeviceInfo& dev, SmallGemmPlan& pl) {
+  if (c.qtype != 4 || c.B == 0 || c.B > kSgMaxB || c.n_jobs < 1 || c.n_jobs > static_cast<int>(kSgMaxJobs))
+    return false;
+  if (c.K == 0 || c.K % 256 != 0 || c.K / 32 < kMinBlk || c.K / 32 > kMaxBlk) return false;
+  if (reinterpret_cast<uintptr_t>(c.X) % 16 != 0) return false;
+  uint64_t units = 0;
+  for (int j = 0; j < c.n_jobs; ++j) {
+    if (reinterpret_cast<uintptr_t>(c.jobs[j].W) % 16 != 0 || c.jobs[j].M == 0) return false;
+    units += (c.jobs[j].M + kUnitRows - 1) / kUnitRows;
+  }
+  pl.nblk = static_cast<uint32_t>(c.K / 32);
+  pl.nseg = (pl.nblk + kSegBlk - 1) / kSegBlk;
+  pl.units = static_cast<uint32_t>(units);
+  pl.grid = static_cast<uint32_t>(std::min<uint64_t>(units, static_cast<uint64_t>(dev.sm_count)));
+  const uint32_t upc = (pl.units + pl.grid - 1) / pl.grid;
+  if (upc > kSgMaxUnits || upc * pl.nseg > kSgMaxSlots) return false;
+  pl.xs_offset = 128;
+  pl.xd_offset = (pl.xs_offset + 2 * kSgChunk * kSgCols * 8 + 127) / 128 * 128;
+  const uint32_t xd_bytes = std::max<uint32_t>(2 * kSgBufBytes, kSgWarps * kSgMaxUnits * 128 * 4);
+  pl.w_offset = (pl.xd_offset + xd_bytes + 127) / 128 * 128;
+  pl.smem = pl.w_offset + static_cast<size_t>(upc) * pl.nseg * kSlotBytes;
+  return pl.smem <= dev.smem_optin;
+}
+
 }  // namespace
 
 bool matvec_mma_ok(const MatvecArgs& a, const DeviceInfo& dev) {
@@ -885,6 +1163,56 @@ int launch_matvec_q4_small(const MatvecArgs& a, const DeviceInfo& dev, int* d_er
   cfg.attrs = attr;
   cfg.numAttrs = a.pdl ? 1 : 0;
   EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, fn, p), "matvec launch");
+  return EFG_OK;
+}
+
+bool gemm_q4_small_ok(const GemmCall& c, const DeviceInfo& dev) {
+  SmallGemmPlan pl;
+  if (!plan_small_gemm(c, dev, pl)) return false;
+  CUtensorMap m;
+  for (int j = 0; j < c.n_jobs; ++j)
+    if (!encode_u64_rows_map(&m, c.jobs[j].W, c.jobs[j].M, c.K / 32 * 18, kBoxElems, kUnitRows)) return false;
+  return true;
+}
+
+int launch_gemm_q4_small(const GemmCall& c, const DeviceInfo& dev, int* d_err, cudaStream_t s) {
+  SmallGemmPlan pl;
+  if (!plan_small_gemm(c, dev, pl)) return fail(EFG_EINVAL, "gemm: no small-batch plan for this call");
+  SmallGemmParams p{};
+  p.X = c.X;
+  p.K = static_cast<uint32_t>(c.K);
+  p.nblk = pl.nblk;
+  p.nseg = pl.nseg;
+  p.B = static_cast<uint32_t>(c.B);
+  p.n_jobs = static_cast<uint32_t>(c.n_jobs);
+  p.units_total = pl.units;
+  p.accumulate = c.accumulate ? 1u : 0u;
+  p.err = d_err;
+  p.xs_offset = pl.xs_offset;
+  p.xd_offset = pl.xd_offset;
+  p.w_offset = pl.w_offset;
+  uint32_t u = 0;
+  for (int j = 0; j < c.n_jobs; ++j) {
+    if (!encode_u64_rows_map(&p.maps[j], c.jobs[j].W, c.jobs[j].M, pl.nblk * 18, kBoxElems, kUnitRows))
+      return fail(EFG_ECUDA, "gemm: tensor map for a %zu x %zu Q4_0 matrix", c.jobs[j].M, c.K);
+    p.Y[j] = c.jobs[j].Y;
+    p.M[j] = static_cast<uint32_t>(c.jobs[j].M);
+    p.job_unit_start[j] = u;
+    u += static_cast<uint32_t>((c.jobs[j].M + kUnitRows - 1) / kUnitRows);
+  }
+  p.job_unit_start[c.n_jobs] = u;
+  if (int st = ensure_smem_attr(reinterpret_cast<const void*>(gemm_q4_small_kernel), pl.smem)) return st;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kSgThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = weight_prefetch_flag() ? 1 : 0;
+  EFG_TRY_CUDA(cudaLaunchKernelEx(&cfg, gemm_q4_small_kernel, p), "gemm launch");
   return EFG_OK;
 }
 

@@ -189,3 +189,61 @@ def test_jobs_errors(cuda):
     torch.cuda.synchronize()
     assert torch.count_nonzero(Y).item() == 0
     assert efg.device_error() == 0
+
+
+@pytest.mark.parametrize("M,K,B", [(5632, 2048, 23), (2048, 5632, 8), (2560, 2048, 64), (300, 4096, 65)])
+def test_small_batch_path_and_switch(cuda, oracle, M, K, B):
+    """B <= 64 runs on the small-batch integer-MMA kernel (X columns as the A operand), B = 65 on
+    the tcgen05 kernel; efg_set_q4_mma(0) sends every size to the tcgen05 kernel. Both within
+    1e-5 of sum|w x|, each deterministic."""
+    import torch
+
+    W = _weights(torch, M, K, 21)
+    X = torch.randn(B, K, generator=torch.Generator(device="cuda").manual_seed(22), device="cuda") * 2
+    Ys = []
+    for mma in (True, False):
+        efg.set_q4_mma(mma)
+        try:
+            Y = torch.full((B, M), float("nan"), device="cuda")
+            efg.gemm_q4_0(Y, W, X, M, K, B)
+            Y2 = torch.empty_like(Y)
+            efg.gemm_q4_0(Y2, W, X, M, K, B)
+            torch.cuda.synchronize()
+        finally:
+            efg.set_q4_mma(True)
+        assert torch.equal(Y, Y2)
+        assert _rel_errors(oracle, W, X, Y, M, K).max() <= TOL
+        Ys.append(Y)
+    assert torch.equal(Ys[0], Ys[1]) == (B > 64)  # the switch only matters where the paths differ
+    assert efg.device_error() == 0
+
+
+def test_small_batch_non_finite_columns(cuda, oracle):
+    """A column of X with an infinity, one with a NaN and one with values beyond the fixed-point
+    range come out as the FP32 matvec computes them (signed infinities stay infinities); the
+    other columns keep the 1e-5 bound."""
+    import torch
+
+    M, K, B = 1000, 2048, 6
+    W = _weights(torch, M, K, 31)
+    X = torch.randn(B, K, generator=torch.Generator(device="cuda").manual_seed(32), device="cuda")
+    X[1, 77] = float("inf")
+    X[3, 1500] = float("nan")
+    X[4] *= 1e31
+    Y = torch.full((B, M), 7.0, device="cuda")
+    efg.gemm_q4_0(Y, W, X, M, K, B)
+    torch.cuda.synchronize()
+    y = torch.empty(M, device="cuda")
+    for b in range(B):
+        efg.matvec_q4_0(y, W, X[b].contiguous(), M, K)
+        torch.cuda.synchronize()
+        got, want = Y[b].cpu().numpy(), y.cpu().numpy()
+        assert np.array_equal(np.isnan(got), np.isnan(want)), b
+        assert np.array_equal(np.isinf(got), np.isinf(want)), b
+        fin = np.isfinite(want)
+        assert np.array_equal(np.sign(got[~fin & ~np.isnan(want)]), np.sign(want[~fin & ~np.isnan(want)]))
+        if b in (0, 2, 4, 5):
+            assert fin.all()
+            assert _rel_errors(oracle, W, X[b:b + 1], Y[b:b + 1], M, K).max() <= TOL, b
+    assert np.isinf(Y[1].cpu().numpy()).any()
+    assert efg.device_error() == 0
