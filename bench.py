@@ -502,9 +502,56 @@ def config0_extra(torch, efg, hbm_peak, x_seed=2, launches=1280):
         del g, gr
     finally:
         efg.set_q4_mma(True)
-    del W4
+    # Independent matvecs (no data dependence between them) on 4 streams at once, each stream a
+    # CUDA graph of its own chain over its own 16 weight copies: the kernel's throughput when it
+    # is not waiting on the launch before it (multi-sequence / multi-model serving).
+    n_streams, per = 4, launches // 4
+    ys = [torch.empty(rows, device="cuda") for _ in range(n_streams)]
+    streams = [torch.cuda.Stream() for _ in range(n_streams)]
+    graphs = []
+    for k, st in enumerate(streams):
+        def fn(i, k=k):
+            efg.matvec(Q4_0, ys[k], W4[(k * 16 + i % 16) % copies], x, rows, cols)
+        for i in range(8):
+            fn(i)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st), torch.cuda.graph(g, stream=st):
+            for i in range(per):
+                fn(i)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    main = torch.cuda.current_stream()
+
+    def run_all():
+        ev0 = torch.cuda.Event()
+        ev0.record(main)
+        ends = []
+        for st, g in zip(streams, graphs):
+            st.wait_event(ev0)
+            with torch.cuda.stream(st):
+                g.replay()
+            e = torch.cuda.Event()
+            e.record(st)
+            ends.append(e)
+        for e in ends:
+            main.wait_event(e)
+
+    run_all()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(main)
+    run_all()
+    s1.record(main)
+    torch.cuda.synchronize()
+    ms_ind = s0.elapsed_time(s1) / (per * n_streams)
+    del graphs, W4
     nb = algo_bytes(Q4_0, rows, cols)
     return {"gbs": round(nb / ms / 1e6, 1), "frac_of_hbm": round(nb / ms / 1e6 / hbm_peak, 4),
+            "measure": "dependent chain: each launch waits for the one before it (as in a decode step)",
+            "independent_4_streams": {"gbs": round(nb / ms_ind / 1e6, 1),
+                                      "frac_of_hbm": round(nb / ms_ind / 1e6 / hbm_peak, 4),
+                                      "us_per_launch": round(ms_ind * 1e3, 3), "launches": per * n_streams},
             "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": nb, "copies": copies,
             "kernel": "small-matrix integer tensor-core kernel (weights fetched ahead, next launch co-resident)",
             "us_per_launch_cuda_cores": round(ms_cc * 1e3, 3),

@@ -42,6 +42,7 @@ from .api import (  # noqa: F401
     row_bytes,
     row_f32,
     set_q4_mma,
+    set_small_gemm,
     set_weight_prefetch,
     shard_rows,
 )

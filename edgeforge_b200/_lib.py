@@ -52,6 +52,7 @@ SIGNATURES = {
     "efg_device_error": (_i, [C.POINTER(_i)]),
     "efg_set_weight_prefetch": (_i, [_i]),
     "efg_set_q4_mma": (_i, [_i]),
+    "efg_set_small_gemm": (_i, [_i]),
     "efg_row_bytes": (_u64, [_i, _u64]),
     "efg_matvec_q4_0": (_i, [_vp, _vp, _vp, _sz, _sz, _vp]),
     "efg_matvec_q8_0": (_i, [_vp, _vp, _vp, _sz, _sz, _vp]),

@@ -131,6 +131,12 @@ def set_q4_mma(enable: bool) -> bool:
     return bool(load().efg_set_q4_mma(int(enable)))
 
 
+def set_small_gemm(enable: bool) -> bool:
+    """efg_set_small_gemm: Q4_0 GEMMs of B <= 64 columns on this thread use the small-batch
+    integer-MMA kernel (default off). Returns the old setting."""
+    return bool(load().efg_set_small_gemm(int(enable)))
+
+
 def set_weight_prefetch(enable: bool) -> bool:
     """efg_set_weight_prefetch: lets later matvec launches on this thread stream their
     weights while the previous kernel finishes (weights must not be written just

@@ -183,6 +183,12 @@ int efg_set_weight_prefetch(int enable) {
   return old ? 1 : 0;
 }
 
+int efg_set_small_gemm(int enable) {
+  const bool old = small_gemm_flag();
+  small_gemm_flag() = enable != 0;
+  return old ? 1 : 0;
+}
+
 int efg_set_q4_mma(int enable) {
   const bool old = q4_mma_flag();
   q4_mma_flag() = enable != 0;

@@ -930,7 +930,7 @@ int launch_gemm_q4_0(float* Y, const uint8_t* W, const float* X, size_t M, size_
     c.X = X;
     c.K = K;
     c.B = B;
-    if (DeviceInfo* dev = current_device(); dev && q4_mma_flag() && gemm_q4_small_ok(c, *dev))
+    if (DeviceInfo* dev = current_device(); dev && small_gemm_flag() && gemm_q4_small_ok(c, *dev))
       return launch_gemm_q4_small(c, *dev, d_err, s);
     return launch_gemm_ws<4>(c, d_err, s);
   }
@@ -1005,7 +1005,7 @@ int launch_gemm(const GemmCall& call, int* d_err, cudaStream_t s) {
     return fail(EFG_EINVAL, "gemm: the B operand must be 16-byte aligned");
   if (tiles >= (1u << 31)) return fail(EFG_EINVAL, "gemm: too many row tiles");
   if (c.qtype == 4)
-    if (DeviceInfo* dev = current_device(); dev && q4_mma_flag() && gemm_q4_small_ok(c, *dev))
+    if (DeviceInfo* dev = current_device(); dev && small_gemm_flag() && gemm_q4_small_ok(c, *dev))
       return launch_gemm_q4_small(c, *dev, d_err, s);
   return c.qtype == 4 ? launch_gemm_ws<4>(c, d_err, s) : launch_gemm_ws<8>(c, d_err, s);
 }

@@ -25,6 +25,11 @@ bool& q4_mma_flag() {
   return on;
 }
 
+bool& small_gemm_flag() {
+  static thread_local bool on = false;
+  return on;
+}
+
 int ensure_smem_attr(const void* fn, size_t bytes) {
   static std::mutex mu;
   static std::map<std::pair<int, const void*>, size_t> done;

@@ -34,6 +34,10 @@ bool& weight_prefetch_flag();
 // Thread-local switch for the tensor-core Q4_0 matvec on large matrices (efg_set_q4_mma).
 bool& q4_mma_flag();
 
+// Thread-local switch for the small-batch Q4_0 GEMM on the integer MMA (efg_set_small_gemm;
+// off by default: measured slower than the tcgen05 GEMM at every config-3 shape).
+bool& small_gemm_flag();
+
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (device, kernel, size);
 // later calls are free, so launches can be captured into CUDA graphs.
 int ensure_smem_attr(const void* fn, size_t bytes);

@@ -635,31 +635,54 @@ __global__ void __launch_bounds__(kSmallThreads, 2) matvec_q4_small_kernel(const
   const uint2* xd = reinterpret_cast<const uint2*>(xdig + (g >> 2) * 128 + (t * 4 + (g & 3u)) * 8);
   const float* xs_l = xsc + t;
   bool ok = true;
-  for (uint32_t i = 0; i < nu; ++i) {
-    ok = ok && mbar_wait(&bar[i], 0, p.err);
-    for (uint32_t m = 0; m < NM; ++m) {
-      float acc = 0.f;
-      const uint8_t* slot0 = wbuf + (i * NM + m) * p.nseg * kSlotBytes;
-      if (ok && fast) {
-#pragma unroll 4
-        for (uint32_t pr = p0; pr < p1; ++pr) {
-          const uint32_t ks = pr / (kSegBlk / 2), w = (pr % (kSegBlk / 2)) * 9;
-          const uint32_t* rw = reinterpret_cast<const uint32_t*>(slot0 + ks * kSlotBytes + g * kRowStride);
+  for (uint32_t i = 0; i < nu; ++i) ok = mbar_wait(&bar[i], 0, p.err) && ok;  // fetched at the start
+  // Block pairs outer, units inner: the units' MMA chains are independent, so their latencies
+  // overlap, and the x fragment and scale of a pair are read once for all units.
+  float acc[kSmallMaxUnits][NM];
+#pragma unroll
+  for (uint32_t i = 0; i < kSmallMaxUnits; ++i)
+#pragma unroll
+    for (uint32_t m = 0; m < NM; ++m) acc[i][m] = 0.f;
+  if (ok && fast) {
+#pragma unroll 1
+    for (uint32_t pr = p0; pr < p1; ++pr) {
+      const uint32_t ks = pr / (kSegBlk / 2), w = (pr % (kSegBlk / 2)) * 9;
+      const uint2 bf = xd[2 * pr * 16];
+      const float sc = xs_l[4 * pr];
+#pragma unroll
+      for (uint32_t i = 0; i < kSmallMaxUnits; ++i) {
+        if (i >= nu) break;
+#pragma unroll
+        for (uint32_t m = 0; m < NM; ++m) {
+          const uint32_t* rw = reinterpret_cast<const uint32_t*>(wbuf + ((i * NM + m) * p.nseg + ks) * kSlotBytes +
+                                                                 g * kRowStride);
           const uint32_t X1 = rw[w + x1_off], X2 = rw[w + x2_off], Y = rw[w + 5 + t];
           const uint32_t ce = __byte_perm(X1, X2, sel_code), db = __byte_perm(X1, X2, sel_d);
-          const uint2 bf = xd[2 * pr * 16];
-          const float sc = xs_l[4 * pr];
           const uint32_t a[4] = {a_lo(ce), a_lo(Y), a_hi(ce), a_hi(Y)};
           int cc[4];
           mma_s8(a, bf.x, bf.y, cc);
           const int v = (c_hi ? cc[2] : cc[0]) + ((c_hi ? cc[3] : cc[1]) << 8);
-          acc = fmaf(static_cast<float>(v), half_bits_to_float(db) * sc, acc);
+          acc[i][m] = fmaf(static_cast<float>(v), half_bits_to_float(db) * sc, acc[i][m]);
         }
-        acc += __shfl_xor_sync(0xFFFFFFFFu, acc, 1);
-        acc += __shfl_xor_sync(0xFFFFFFFFu, acc, 2);
-      } else if (ok) {
-        // plain FP32 dots of this warp's blocks (non-finite or out-of-range x): row r's sum
-        // lands in lane 4 r, where the MMA path leaves it
+      }
+    }
+#pragma unroll
+    for (uint32_t i = 0; i < kSmallMaxUnits; ++i) {
+      if (i >= nu) break;
+#pragma unroll
+      for (uint32_t m = 0; m < NM; ++m) {
+        acc[i][m] += __shfl_xor_sync(0xFFFFFFFFu, acc[i][m], 1);
+        acc[i][m] += __shfl_xor_sync(0xFFFFFFFFu, acc[i][m], 2);
+        if (t == 0) red[((warp * kSmallMaxUnits + i) * NM + m) * kUnitRows + g] = acc[i][m];
+      }
+    }
+  } else if (ok) {
+    // plain FP32 dots of this warp's blocks (non-finite or out-of-range x): row r's sum lands
+    // in lane 4 r, where the MMA path leaves it
+    for (uint32_t i = 0; i < nu; ++i)
+      for (uint32_t m = 0; m < NM; ++m) {
+        const uint8_t* slot0 = wbuf + (i * NM + m) * p.nseg * kSlotBytes;
+        float accf = 0.f;
         for (uint32_t r = 0; r < kUnitRows; ++r) {
           float part = 0.f;
           for (uint32_t bb = b0 + lane; bb < b0 + nb; bb += 32) {
@@ -675,11 +698,10 @@ __global__ void __launch_bounds__(kSmallThreads, 2) matvec_q4_small_kernel(const
             part += d * sacc;
           }
           part = warp_sum(part);
-          if (g == r) acc = part;
+          if (g == r) accf = part;
         }
+        if (t == 0) red[((warp * kSmallMaxUnits + i) * NM + m) * kUnitRows + g] = accf;
       }
-      if (t == 0) red[((warp * kSmallMaxUnits + i) * NM + m) * kUnitRows + g] = acc;
-    }
   }
   __syncthreads();
   // one thread per (unit, row): the warps' partials in warp order, then the epilogue

@@ -81,6 +81,13 @@ int efg_set_weight_prefetch(int enable);
  * counterpart: the reference has one CPU kernel per format. */
 int efg_set_q4_mma(int enable);
 
+/* Whether the Q4_0 GEMM calls made afterwards on this thread with B <= 64 columns use the
+ * small-batch kernel on the exact integer MMA (X columns as int8 digit planes against the
+ * codes) instead of the tcgen05 kernel. 0 (the default) keeps the tcgen05 kernel. Both meet the
+ * same tolerance; the small-batch kernel also gives non-finite columns exactly as the FP32
+ * matvec does. Returns the old setting. No reference counterpart. */
+int efg_set_small_gemm(int enable);
+
 /* Bytes of one row of `cols` weights, or 0 with efg_last_error() set when a block type
  * gets cols % 32 != 0. Replaces ef::qtype_row_bytes (include/ef/quant.h:42,
  * src/quant.cpp:136-149), which throws in that case. */

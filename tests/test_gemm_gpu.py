@@ -193,16 +193,16 @@ def test_jobs_errors(cuda):
 
 @pytest.mark.parametrize("M,K,B", [(5632, 2048, 23), (2048, 5632, 8), (2560, 2048, 64), (300, 4096, 65)])
 def test_small_batch_path_and_switch(cuda, oracle, M, K, B):
-    """B <= 64 runs on the small-batch integer-MMA kernel (X columns as the A operand), B = 65 on
-    the tcgen05 kernel; efg_set_q4_mma(0) sends every size to the tcgen05 kernel. Both within
-    1e-5 of sum|w x|, each deterministic."""
+    """With efg_set_small_gemm(1), B <= 64 runs on the small-batch integer-MMA kernel (X columns as
+    the A operand) and B = 65 stays on the tcgen05 kernel; the default is the tcgen05 kernel for
+    every B. Both within 1e-5 of sum|w x|, each deterministic."""
     import torch
 
     W = _weights(torch, M, K, 21)
     X = torch.randn(B, K, generator=torch.Generator(device="cuda").manual_seed(22), device="cuda") * 2
     Ys = []
-    for mma in (True, False):
-        efg.set_q4_mma(mma)
+    for small in (True, False):
+        old = efg.set_small_gemm(small)
         try:
             Y = torch.full((B, M), float("nan"), device="cuda")
             efg.gemm_q4_0(Y, W, X, M, K, B)
@@ -210,7 +210,7 @@ def test_small_batch_path_and_switch(cuda, oracle, M, K, B):
             efg.gemm_q4_0(Y2, W, X, M, K, B)
             torch.cuda.synchronize()
         finally:
-            efg.set_q4_mma(True)
+            efg.set_small_gemm(old)
         assert torch.equal(Y, Y2)
         assert _rel_errors(oracle, W, X, Y, M, K).max() <= TOL
         Ys.append(Y)
@@ -219,12 +219,13 @@ def test_small_batch_path_and_switch(cuda, oracle, M, K, B):
 
 
 def test_small_batch_non_finite_columns(cuda, oracle):
-    """A column of X with an infinity, one with a NaN and one with values beyond the fixed-point
+    """On the small-batch kernel (efg_set_small_gemm(1)): a column of X with an infinity, one with a NaN and one with values beyond the fixed-point
     range come out as the FP32 matvec computes them (signed infinities stay infinities); the
     other columns keep the 1e-5 bound."""
     import torch
 
     M, K, B = 1000, 2048, 6
+    old = efg.set_small_gemm(True)
     W = _weights(torch, M, K, 31)
     X = torch.randn(B, K, generator=torch.Generator(device="cuda").manual_seed(32), device="cuda")
     X[1, 77] = float("inf")
@@ -246,4 +247,5 @@ def test_small_batch_non_finite_columns(cuda, oracle):
             assert fin.all()
             assert _rel_errors(oracle, W, X[b:b + 1], Y[b:b + 1], M, K).max() <= TOL, b
     assert np.isinf(Y[1].cpu().numpy()).any()
+    efg.set_small_gemm(old)
     assert efg.device_error() == 0
