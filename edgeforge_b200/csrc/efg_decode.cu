@@ -549,6 +549,14 @@ int check_mat(const Mat& m, const char* name) {
   return EFG_OK;
 }
 
+// The decode step's matvecs stay on the CUDA-core and large-matrix kernels: in its chain of
+// different kernels the small-matrix MMA kernel measured slower (1447-1501 tok/s against 1572
+// on the TinyLlama shape, whichever subset of the step's calls it took).
+MatvecArgs decode_args(MatvecArgs a) {
+  a.small_kernel = false;
+  return a;
+}
+
 // logits = lm_head . rmsnorm(x, final_norm) (src/model.cpp:266-270).
 int enqueue_lm_head(Decoder& D, const float* x, cudaStream_t s, float* out = nullptr) {
   cudaLaunchAttribute attr[1];
@@ -569,7 +577,7 @@ int enqueue_lm_head(Decoder& D, const float* x, cudaStream_t s, float* out = nul
     a.x = D.h;
     a.norm_w = nullptr;
   }
-  return launch_matvec(a, D.d_err, s);
+  return launch_matvec(decode_args(a), D.d_err, s);
 }
 
 // Next token = argmax(logits) at the device-side position, which then advances.
@@ -627,7 +635,7 @@ int enqueue_step(Decoder& D, bool logits, cudaStream_t s) {
         a.x = D.h;
         a.norm_w = nullptr;
       }
-      if (int st = launch_matvec(a, D.d_err, s)) return st;
+      if (int st = launch_matvec(decode_args(a), D.d_err, s)) return st;
     }
     {
       const size_t smem = (2 * hd + attn_stage_floats(hd) + D.max_seq) * sizeof(float);
@@ -648,7 +656,7 @@ int enqueue_step(Decoder& D, bool logits, cudaStream_t s) {
       a.pdl = true;
       a.n_jobs = 1;
       a.jobs[0] = MatvecJobDev{Ly.o.w, D.x, Ly.o.rows, 0};
-      if (int st = launch_matvec(a, D.d_err, s)) return st;
+      if (int st = launch_matvec(decode_args(a), D.d_err, s)) return st;
     }
     {  // gate/up with the ffn RMSNorm and SwiGLU (src/model.cpp:253-258)
       MatvecArgs a;
@@ -663,7 +671,7 @@ int enqueue_step(Decoder& D, bool logits, cudaStream_t s) {
       a.jobs[0] = MatvecJobDev{Ly.gate.w, D.act, Ly.gate.rows, 0};
       a.jobs[1] = MatvecJobDev{Ly.up.w, D.act, Ly.up.rows, 0};
       if (Ly.gate.type == Ly.up.type && matvec_fast_path_ok(a)) {
-        if (int st = launch_matvec(a, D.d_err, s)) return st;
+        if (int st = launch_matvec(decode_args(a), D.d_err, s)) return st;
       } else {
         cudaLaunchConfig_t cf = cfg_of(dim3(1), dim3(256), 0, s, attr);
         EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, rmsnorm_kernel, D.h, static_cast<const float*>(D.x), Ly.ffn_norm, Dm,
@@ -678,7 +686,7 @@ int enqueue_step(Decoder& D, bool logits, cudaStream_t s) {
           b.pdl = true;
           b.n_jobs = 1;
           b.jobs[0] = MatvecJobDev{M.w, m == 0 ? D.gate : D.up, M.rows, 0};
-          if (int st = launch_matvec(b, D.d_err, s)) return st;
+          if (int st = launch_matvec(decode_args(b), D.d_err, s)) return st;
         }
         cudaLaunchConfig_t cg = cfg_of(dim3(std::max(1u, std::min(64u, (F + 255) / 256))), dim3(256), 0, s, attr);
         EFG_TRY_CUDA(cudaLaunchKernelEx(&cg, swiglu_kernel, D.act, static_cast<const float*>(D.gate),
@@ -695,7 +703,7 @@ int enqueue_step(Decoder& D, bool logits, cudaStream_t s) {
       a.pdl = true;
       a.n_jobs = 1;
       a.jobs[0] = MatvecJobDev{Ly.down.w, D.x, Ly.down.rows, 0};
-      if (int st = launch_matvec(a, D.d_err, s)) return st;
+      if (int st = launch_matvec(decode_args(a), D.d_err, s)) return st;
     }
   }
   if (logits) {
@@ -1121,7 +1129,7 @@ int batched_proj(Decoder& D, const Mat& M, const float* X, float* Y, size_t n, c
     a.pdl = true;
     a.n_jobs = 1;
     a.jobs[0] = MatvecJobDev{M.w, Y + b * M.rows, M.rows, 0};
-    if (int st = launch_matvec(a, D.d_err, s)) return st;
+    if (int st = launch_matvec(decode_args(a), D.d_err, s)) return st;
   }
   return EFG_OK;
 }

@@ -720,7 +720,8 @@ int launch_matvec_on(const MatvecArgs& a, const DeviceInfo& devinfo, int* d_err,
     return EFG_OK;
   }
 
-  if (q4_mma_flag() && matvec_small_ok(a, *dev)) return launch_matvec_q4_small(a, *dev, d_err, stream, direct_smem_attr);
+  if (q4_mma_flag() && a.small_kernel && matvec_small_ok(a, *dev))
+    return launch_matvec_q4_small(a, *dev, d_err, stream, direct_smem_attr);
   if (q4_mma_flag() && matvec_mma_ok(a, *dev)) return launch_matvec_q4_mma(a, *dev, d_err, stream, direct_smem_attr);
 
   bool fast = true;

@@ -50,6 +50,8 @@ struct MatvecArgs {
   int n_jobs = 0;
   MatvecJobDev jobs[kMaxJobs] = {};
   bool pdl = false;               // launch with programmatic stream serialization
+  bool small_kernel = true;       // the small-matrix MMA kernel may take the call (the decode step
+                                  // turns it off: measured slower inside that chain of launches)
   GatherDev gather;               // nranks > 0: store every output into each peer's y too, and
                                   // return only once every peer's rows are here (one job, Store,
                                   // no norm; efg_gather.cuh)
