@@ -280,6 +280,106 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(
   attend_head(qh, k_layer, v_layer, kn, kv, hd, kvd, pos + 1, sc, stage, red_f, red_d, ctx + h * hd, staged);
 }
 
+// The same attention step for head_dim 64 and at most kWarpAttnMaxPos cached positions, one
+// warp per query head: lane i holds dims i and i + 32 (exactly the RoPE pairs), scores are one
+// position per lane, and the max, the softmax sum and every hand-over stay inside the warp (no
+// CTA barrier after the grid-dependency wait). The arithmetic per element is attend_head's:
+// the score dot in 8 partial sums combined pairwise, times 1/sqrt(hd); exp(x - max) summed in
+// double; each probability times float(1 / sum); values summed in position order.
+constexpr int kWarpAttnMaxPos = 128;
+// Shared floats for max_seq positions: the position count is padded to a multiple of 4, so the
+// values array (after n_pad * 65 key floats) starts 16-byte aligned for its float4 stores.
+__host__ __device__ constexpr size_t warp_attn_smem_floats(size_t max_seq) {
+  return ((max_seq + 3) / 4 * 4) * (65 + 64 + 1) + 64;
+}
+
+__global__ void __launch_bounds__(32) attention_warp_kernel(
+    const float* __restrict__ q, const float* __restrict__ knew, float* __restrict__ k_layer,
+    const float* __restrict__ v_layer, float* __restrict__ ctx, const float* __restrict__ rope_cos,
+    const float* __restrict__ rope_sin, const int32_t* __restrict__ pos_p, int H, int KV, int max_seq, int* err) {
+  extern __shared__ float sm[];
+  constexpr int hd = 64, half = 32;
+  const int n_cap = min(max_seq, kWarpAttnMaxPos);
+  const int n_pad = (n_cap + 3) / 4 * 4;
+  float* kc = sm;                   // [n_pad][65] keys (padded rows: lane t reads row t conflict-free)
+  float* vc = kc + n_pad * 65;      // [n_pad][64] values, 16-byte aligned (n_pad % 4 == 0)
+  float* sc = vc + n_pad * 64;      // [n_pad] scores, then probabilities
+  float* qh = sc + n_pad;           // [64] rotated query
+  const int lane = threadIdx.x;
+  const int pos = *pos_p;
+  if (pos < 0 || pos >= n_cap) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (lane == 0) record_error(err, EFG_ESTATE);
+    return;
+  }
+  const int h = blockIdx.x, group = H / KV, kv = h / group, kvd = KV * hd;
+  // the cached history (written by earlier steps) and the RoPE row, before the wait
+  for (int e = lane; e < pos * 16; e += 32) {
+    const int t = e >> 4, i4 = e & 15;
+    const size_t row = static_cast<size_t>(t) * kvd + kv * hd;
+    const float4 k4 = reinterpret_cast<const float4*>(k_layer + row)[i4];
+    reinterpret_cast<float4*>(vc + t * hd)[i4] = reinterpret_cast<const float4*>(v_layer + row)[i4];
+    float* d = kc + t * 65 + 4 * i4;
+    d[0] = k4.x;
+    d[1] = k4.y;
+    d[2] = k4.z;
+    d[3] = k4.w;
+  }
+  const float cs = rope_cos[static_cast<size_t>(pos) * half + lane], sn = rope_sin[static_cast<size_t>(pos) * half + lane];
+  pdl_wait();
+  pdl_launch_dependents();
+  float qa, qb, ka, kb;
+  rope_pair(q[h * hd + lane], q[h * hd + lane + half], cs, sn, qa, qb);
+  rope_pair(knew[kv * hd + lane], knew[kv * hd + lane + half], cs, sn, ka, kb);
+  if (h % group == 0) {  // the first head of each KV group writes the rotated key to the cache
+    k_layer[static_cast<size_t>(pos) * kvd + kv * hd + lane] = ka;
+    k_layer[static_cast<size_t>(pos) * kvd + kv * hd + lane + half] = kb;
+  }
+  qh[lane] = qa;
+  qh[lane + half] = qb;
+  kc[pos * 65 + lane] = ka;
+  kc[pos * 65 + lane + half] = kb;
+  vc[pos * hd + lane] = v_layer[static_cast<size_t>(pos) * kvd + kv * hd + lane];
+  vc[pos * hd + lane + half] = v_layer[static_cast<size_t>(pos) * kvd + kv * hd + lane + half];
+  __syncwarp();
+  const int n_pos = pos + 1;
+  const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(hd)));
+  float mx = -INFINITY;
+  for (int t = lane; t < n_pos; t += 32) {
+    const float* kt = kc + t * 65;
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < hd; i += 8)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) a[k] = __fadd_rn(a[k], __fmul_rn(qh[i + k], kt[i + k]));
+    const float dot = __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
+                                __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
+    sc[t] = __fmul_rn(dot, scale);
+    mx = fmaxf(mx, sc[t]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+  double sum = 0.0;
+  for (int t = lane; t < n_pos; t += 32) {
+    const float e = expf(__fsub_rn(sc[t], mx));
+    sc[t] = e;
+    sum += static_cast<double>(e);
+  }
+  sum = warp_sum_d(sum);
+  const float inv = static_cast<float>(1.0 / sum);
+  for (int t = lane; t < n_pos; t += 32) sc[t] = __fmul_rn(sc[t], inv);
+  __syncwarp();
+  float acc0 = 0.f, acc1 = 0.f;
+  for (int t = 0; t < n_pos; ++t) {
+    const float pr = sc[t];
+    acc0 = __fadd_rn(acc0, __fmul_rn(pr, vc[t * hd + lane]));
+    acc1 = __fadd_rn(acc1, __fmul_rn(pr, vc[t * hd + lane + half]));
+  }
+  ctx[h * hd + lane] = acc0;
+  ctx[h * hd + lane + half] = acc1;
+}
+
 // Batched prefill: rotate the keys of positions p0..p0+n-1, written unrotated into the
 // cache by the k projection, in place (grid.x = n, one position per CTA).
 __global__ void rope_keys_kernel(float* __restrict__ k_layer, const float* __restrict__ rope_cos,
@@ -637,7 +737,16 @@ int enqueue_step(Decoder& D, bool logits, cudaStream_t s) {
       }
       if (int st = launch_matvec(decode_args(a), D.d_err, s)) return st;
     }
-    {
+    if (hd == 64 && D.max_seq <= static_cast<size_t>(kWarpAttnMaxPos)) {
+      const size_t smem = warp_attn_smem_floats(D.max_seq) * sizeof(float);
+      cudaLaunchConfig_t cf = cfg_of(dim3(H), dim3(32), smem, s, attr);
+      EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, attention_warp_kernel, static_cast<const float*>(D.q),
+                                      static_cast<const float*>(D.knew), kl, static_cast<const float*>(vl), D.ctx,
+                                      static_cast<const float*>(D.rcos), static_cast<const float*>(D.rsin),
+                                      static_cast<const int32_t*>(D.pos_p()), H, KV, static_cast<int>(D.max_seq),
+                                      D.d_err),
+                   "attention launch");
+    } else {
       const size_t smem = (2 * hd + attn_stage_floats(hd) + D.max_seq) * sizeof(float);
       cudaLaunchConfig_t cf = cfg_of(dim3(H), dim3(kAttnThreads), smem, s, attr);
       EFG_TRY_CUDA(cudaLaunchKernelEx(&cf, attention_kernel, static_cast<const float*>(D.q),
@@ -1032,6 +1141,11 @@ int open_decoder(const char* path, size_t max_seq, Decoder** out) {
       (2 * static_cast<size_t>(c.head_dim) + attn_stage_floats(static_cast<int>(c.head_dim)) + max_seq) * sizeof(float);
   if (attn_smem > 227 * 1024)
     return fail(EFG_EINVAL, "decoder: max_seq %zu is too long for the attention kernel", max_seq);
+  if (c.head_dim == 64 && max_seq <= static_cast<size_t>(kWarpAttnMaxPos)) {
+    EFG_TRY_CUDA(cudaFuncSetAttribute(attention_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(warp_attn_smem_floats(max_seq) * sizeof(float))),
+                 "attention smem attribute");
+  }
   if (attn_smem > 48 * 1024) {
     EFG_TRY_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(attn_smem)),

@@ -322,3 +322,30 @@ def test_full_tinyllama_decode(tinyllama, persistent):
         n = int(tie[0]) if tie.size else FULL_STEPS
         np.testing.assert_array_equal(np.array(g.tokens[:n]), np.array(toks[:n]))
         assert efg.device_error() == 0
+
+
+def test_non_finite_weight_same_on_both_paths(tmp_path, z):
+    """An infinite FP16 scale in layer 0's q_proj (a weight of +-inf, and inf * 0 = NaN at code 8):
+    the per-token path (matvec) and the batched prompt path (tensor-core GEMM, whose split of an
+    infinite operand gives NaN where the matvec gives +-inf) both end in non-finite logits at the
+    same positions, so the GEMM's documented difference does not change what the decoder emits."""
+    import json as _json
+
+    src = GOLD / "decode_tiny_uniform.efq"
+    raw = bytearray(src.read_bytes())
+    hlen = int.from_bytes(raw[8:16], "little")
+    hdr = _json.loads(bytes(raw[16:16 + hlen]).decode())
+    t = next(t for t in hdr["tensors"] if t["name"] == "model.layers.0.self_attn.q_proj.weight")
+    assert t["type"].upper() == "Q4_0"
+    off = int(t["offset"])
+    raw[off:off + 2] = (0x7C00).to_bytes(2, "little")  # first block's scale: +inf
+    bad = tmp_path / "inf_scale.efq"
+    bad.write_bytes(bytes(raw))
+    prompt = [int(v) for v in z["prompt"]]
+    with efg.Decoder(bad, MAX_SEQ) as a, efg.Decoder(bad, MAX_SEQ) as b:
+        for i, tok in enumerate(prompt):
+            la = a.forward(tok, i, compute_logits=i + 1 == len(prompt))
+        lb = b.prefill(np.array(prompt, np.int32), 0)
+        assert np.array_equal(np.isfinite(la), np.isfinite(lb))
+        assert not np.isfinite(la).all()
+    assert efg.device_error() == 0
