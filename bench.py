@@ -272,11 +272,13 @@ def graphs_of(torch, fn, steps, warmup, chunk=60):
 
 def replay_timed(torch, g_full, g_rem, chunk, steps, barrier, world, clocks=None):
     """Device time (ms) of exactly `steps` steps replayed from the graphs, bracketed by a
-    barrier and a device synchronize on both sides; the max over ranks."""
-    barrier()
+    barrier and a device synchronize on both sides; the max over ranks. The clock sampler
+    starts before the barrier: its first NVML query takes a different time on every rank,
+    and a rank that starts early waits inside the first step for the others."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ctx = clocks if clocks is not None else _Null()
     with ctx:
+        barrier()
         start.record()
         for _ in range(steps // chunk):
             g_full.replay()
