@@ -15,7 +15,8 @@
 // grid-dependency wait), so CUDA graphs of these launches replay correctly.
 //
 // Order of one launch on rank r (epoch e = epoch + 1):
-//   1. CTA 0 stores ready[r] = e into every peer's area (release, system scope).
+//   1. CTA 0 stores ready[r] = e into every peer's area (release, system scope; one lane
+//      per peer).
 //   2. A warp that stores outputs first waits until ready[q] >= e here for every peer q.
 //   3. Each CTA: outputs to the local y and to every peer's y; the CTA barriers, then one
 //      thread fences at system scope (cumulative: it orders every store the barrier ordered
@@ -54,10 +55,11 @@ __device__ __forceinline__ uint32_t gather_epoch(const GatherDev& g) {
   return *reinterpret_cast<const volatile uint32_t*>(g.flags + kEpochOff) + 1u;
 }
 
-// Step 1, one thread of CTA 0 after the grid-dependency wait.
+// Step 1, the first warp of CTA 0 after the grid-dependency wait: lane q stores into rank
+// q's area, so the peers are told at once rather than one after another.
 __device__ __forceinline__ void gather_announce(const GatherDev& g, uint32_t epoch) {
-  for (int q = 0; q < g.nranks; ++q)
-    if (q != g.rank) st_release_sys(g.peer_flags[q] + kReadyOff + g.rank, epoch);
+  const int q = threadIdx.x & 31;
+  if (q < g.nranks && q != g.rank) st_release_sys(g.peer_flags[q] + kReadyOff + g.rank, epoch);
 }
 
 // Waits (bounded) until flags[off + q] >= epoch for every peer q. Lane q of the calling

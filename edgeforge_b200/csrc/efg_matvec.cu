@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1) matvec_fast_kernel(const __gri
   uint32_t epoch = 0;
   if constexpr (GATHER) {
     epoch = gather_epoch(p.g);
-    if (blockIdx.x == 0 && tid == 0) gather_announce(p.g, epoch);
+    if (blockIdx.x == 0 && tid < 32) gather_announce(p.g, epoch);
   }
   double ss = 0.0;
   if (p.x_vec4) {
@@ -353,7 +353,7 @@ __global__ void matvec_generic_kernel(const __grid_constant__ KParams p) {
   uint32_t epoch = 0;
   if constexpr (GATHER) {
     epoch = gather_epoch(p.g);
-    if (blockIdx.x == 0 && threadIdx.x == 0) gather_announce(p.g, epoch);
+    if (blockIdx.x == 0 && threadIdx.x < 32) gather_announce(p.g, epoch);
   }
   bool ready = true;
   constexpr uint32_t BB = F == Fmt::Q4 ? 18 : 34;

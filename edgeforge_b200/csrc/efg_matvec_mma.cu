@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) matvec_q4_mma_kernel(const __g
   uint32_t epoch = 0;
   if constexpr (GATHER) {
     epoch = gather_epoch(p.g);
-    if (blockIdx.x == 0 && tid == 0) gather_announce(p.g, epoch);
+    if (blockIdx.x == 0 && tid < 32) gather_announce(p.g, epoch);
   }
   float inv = 1.f;
   if constexpr (NORM) {  // rmsnorm scale (src/kernels.cpp:69-73): double sum of squares
