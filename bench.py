@@ -521,56 +521,62 @@ def config0_extra(torch, efg, hbm_peak, x_seed=2, launches=1280):
         del g, gr
     finally:
         efg.set_q4_mma(True)
-    # Independent matvecs (no data dependence between them) on 4 streams at once, each stream a
-    # CUDA graph of its own chain over its own 16 weight copies: the kernel's throughput when it
-    # is not waiting on the launch before it (multi-sequence / multi-model serving).
-    n_streams, per = 4, launches // 4
-    ys = [torch.empty(rows, device="cuda") for _ in range(n_streams)]
-    streams = [torch.cuda.Stream() for _ in range(n_streams)]
-    graphs = []
-    for k, st in enumerate(streams):
-        def fn(i, k=k):
-            efg.matvec(Q4_0, ys[k], W4[(k * 16 + i % 16) % copies], x, rows, cols)
-        for i in range(8):
-            fn(i)
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(st), torch.cuda.graph(g, stream=st):
-            for i in range(per):
-                fn(i)
-        graphs.append(g)
-    torch.cuda.synchronize()
+    # Independent matvecs (no data dependence between them) on several streams at once, each
+    # stream a CUDA graph of its own chain over its own share of the weight copies: the
+    # kernel's throughput when it is not waiting on the launch before it (multi-sequence /
+    # multi-model serving).
     main = torch.cuda.current_stream()
 
-    def run_all():
-        ev0 = torch.cuda.Event()
-        ev0.record(main)
-        ends = []
-        for st, g in zip(streams, graphs):
-            st.wait_event(ev0)
-            with torch.cuda.stream(st):
-                g.replay()
-            e = torch.cuda.Event()
-            e.record(st)
-            ends.append(e)
-        for e in ends:
-            main.wait_event(e)
+    def independent(n_streams):
+        per, share = launches // n_streams, copies // n_streams
+        ys = [torch.empty(rows, device="cuda") for _ in range(n_streams)]
+        streams = [torch.cuda.Stream() for _ in range(n_streams)]
+        graphs = []
+        for k, st in enumerate(streams):
+            def fn(i, k=k):
+                efg.matvec(Q4_0, ys[k], W4[k * share + i % share], x, rows, cols)
+            for i in range(8):
+                fn(i)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(st), torch.cuda.graph(g, stream=st):
+                for i in range(per):
+                    fn(i)
+            graphs.append(g)
+        torch.cuda.synchronize()
 
-    run_all()
-    torch.cuda.synchronize()
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s0.record(main)
-    run_all()
-    s1.record(main)
-    torch.cuda.synchronize()
-    ms_ind = s0.elapsed_time(s1) / (per * n_streams)
-    del graphs, W4
+        def run_all():
+            ev0 = torch.cuda.Event()
+            ev0.record(main)
+            ends = []
+            for st, g in zip(streams, graphs):
+                st.wait_event(ev0)
+                with torch.cuda.stream(st):
+                    g.replay()
+                e = torch.cuda.Event()
+                e.record(st)
+                ends.append(e)
+            for e in ends:
+                main.wait_event(e)
+
+        run_all()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(main)
+        run_all()
+        s1.record(main)
+        torch.cuda.synchronize()
+        del graphs
+        return s0.elapsed_time(s1) / (per * n_streams), per * n_streams
+
+    ind = {n: independent(n) for n in (4, 8)}
+    del W4
     nb = algo_bytes(Q4_0, rows, cols)
     return {"gbs": round(nb / ms / 1e6, 1), "frac_of_hbm": round(nb / ms / 1e6 / hbm_peak, 4),
             "measure": "dependent chain: each launch waits for the one before it (as in a decode step)",
-            "independent_4_streams": {"gbs": round(nb / ms_ind / 1e6, 1),
-                                      "frac_of_hbm": round(nb / ms_ind / 1e6 / hbm_peak, 4),
-                                      "us_per_launch": round(ms_ind * 1e3, 3), "launches": per * n_streams},
+            **{f"independent_{n}_streams": {"gbs": round(nb / m / 1e6, 1), "frac_of_hbm": round(nb / m / 1e6 / hbm_peak, 4),
+                                             "us_per_launch": round(m * 1e3, 3), "launches": k}
+               for n, (m, k) in ind.items()},
             "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": nb, "copies": copies,
             "kernel": "small-matrix integer tensor-core kernel (weights fetched ahead, next launch co-resident)",
             "us_per_launch_cuda_cores": round(ms_cc * 1e3, 3),
@@ -762,8 +768,9 @@ def lm_head_extra(torch, efg, world, rank, barrier, steps=200, warmup=10, rows=3
     """The decode step's last operation with lm_head (Q8_0 32000 x 2048) row-sharded over the
     job's GPUs: this rank's logits with the final RMSNorm fused, then the argmax over all
     ranks (efg_lm_head_argmax_sharded). Device time per call (CUDA graphs, max over ranks;
-    strong scaling). Verified: the token on every rank equals the argmax of all ranks'
-    logits gathered afterwards."""
+    strong scaling), at N > 1 with a buffer registered on the communicator (the pairs travel
+    by peer stores inside the argmax launch) and, for comparison, through NCCL. Verified: the
+    token on every rank equals the argmax of all ranks' logits gathered afterwards."""
     b, c = efg.shard_rows(rows, world, rank)
     rb = cols // 32 * 34
     g = torch.Generator(device="cuda").manual_seed(200)
@@ -782,6 +789,12 @@ def lm_head_extra(torch, efg, world, rank, barrier, steps=200, warmup=10, rows=3
         def step(i):
             efg.lm_head_argmax_sharded(Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
 
+        ms_nccl = None
+        reg = None
+        if world > 1:
+            ms_nccl = time_calls(torch, step, steps, warmup, barrier, world)
+            reg = torch.zeros(64, device="cuda")
+            comm.register(reg)
         ms = time_calls(torch, step, steps, warmup, barrier, world)
         tok.fill_(-1)
         step(0)
@@ -803,10 +816,14 @@ def lm_head_extra(torch, efg, world, rank, barrier, steps=200, warmup=10, rows=3
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
             ok = bool(t.item() == 1)
         assert efg.device_error() == 0
+        if reg is not None:
+            comm.deregister(reg)
     finally:
         comm.close()
     return {"us_per_call": round(ms * 1e3, 3), "ranks": world, "rows_per_rank": c, "token": int(tok.item()),
-            "verified": ok, "scaling": "strong"}
+            "verified": ok, "scaling": "strong",
+            "exchange": "peer stores in the argmax launch" if world > 1 else "none (one rank)",
+            "us_per_call_nccl": round(ms_nccl * 1e3, 3) if ms_nccl is not None else None}
 
 
 def quant_extra(torch, efg, hbm_peak, reps=5):

@@ -92,5 +92,11 @@ int launch_argmax_index(const float* x, size_t n, int32_t* index, cudaStream_t s
 int launch_argmax_local(const float* x, size_t n, size_t offset, ArgmaxPair* out, cudaStream_t s);
 // *index = the whole vector's argmax from every shard's pair, shards in index order.
 int launch_argmax_combine(const ArgmaxPair* pairs, int count, int32_t* index, cudaStream_t s);
+// The row-sharded argmax in one launch: this shard's pair (logits [offset, offset + n)) stored
+// into every rank's flag area by peer stores, the peers' pairs awaited (bounded: EFG_ETIMEOUT
+// in *err) and combined; every rank's flag area must be mapped (efg_comm_register).
+struct GatherDev;
+int launch_argmax_exchange(const float* x, size_t n, size_t offset, const GatherDev& g, int32_t* index, int* err,
+                           cudaStream_t s);
 
 }  // namespace efg

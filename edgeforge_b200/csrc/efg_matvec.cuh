@@ -19,7 +19,14 @@ constexpr uint32_t kReadyOff = 0;
 constexpr uint32_t kDoneOff = 32;
 constexpr uint32_t kEpochOff = 64;
 constexpr uint32_t kCountOff = 96;
-constexpr size_t kGatherFlagBytes = 128 * 4;
+// The row-sharded argmax's exchange (efg_argmax.cu) in the same area: [2 call parities][rank]
+// (value bits, index) pairs, their flags (the call number that wrote them), and this rank's
+// count of exchanges.
+constexpr uint32_t kPairOff = 128;
+constexpr uint32_t kPairFlagOff = kPairOff + 2 * kMaxGatherRanks * 2;
+constexpr uint32_t kPairEpochOff = kPairFlagOff + 2 * kMaxGatherRanks;
+constexpr size_t kGatherFlagBytes = 256 * 4;
+static_assert(kPairEpochOff < kGatherFlagBytes / 4, "flag area too small");
 
 struct GatherDev {
   int nranks = 0, rank = 0;

@@ -350,6 +350,9 @@ int efg_comm_deregister(efg_comm* c, void* d_buf) {
       if (it->map_flags[q]) close_peer(c, it->map_flags[q]);
     }
     c->bufs.erase(it);
+    if (c->bufs.empty())  // the last registration held the peers' flag mappings
+      for (int q = 0; q < c->nranks; ++q)
+        if (q != c->rank) c->peer_flags[q] = nullptr;
     return EFG_OK;
   }
   return fail(EFG_EINVAL, "comm_deregister: buffer not registered");
@@ -467,6 +470,20 @@ int efg_lm_head_argmax_sharded(int qtype, float* d_logits_shard, int32_t* d_toke
     a.n_jobs = 1;
     a.jobs[0] = MatvecJobDev{d_W_shard, d_logits_shard, static_cast<uint32_t>(cnt), 0};
     if (int st = launch_matvec(a, di->d_err, s)) return st;
+  }
+  // Every rank's flag area mapped (some buffer registered, an outcome all ranks share): the
+  // pairs travel by peer stores inside the argmax launch itself.
+  bool mapped = comm->nranks > 1 && comm->nranks <= kMaxGatherRanks && comm->d_flags && !comm->bufs.empty();
+  for (int q = 0; mapped && q < comm->nranks; ++q) mapped = comm->peer_flags[q] != nullptr;
+  if (mapped) {
+    DeviceInfo* di = current_device();
+    if (!di) return EFG_ECUDA;
+    GatherDev g;
+    g.nranks = comm->nranks;
+    g.rank = comm->rank;
+    g.flags = comm->d_flags;
+    for (int q = 0; q < comm->nranks; ++q) g.peer_flags[q] = comm->peer_flags[q];
+    return launch_argmax_exchange(d_logits_shard, cnt, b, g, d_token, di->d_err, s);
   }
   ArgmaxPair* mine = comm->d_pairs + comm->rank;
   if (int st = launch_argmax_local(d_logits_shard, cnt, b, mine, s)) return st;

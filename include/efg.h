@@ -266,8 +266,13 @@ int efg_argmax(const float* d_x, size_t n, int32_t* d_index, void* stream);
  * d_norm_w (or NULL) the final RMSNorm weights. Writes this rank's logits (its row count of
  * floats) to d_logits_shard and, on every rank, the argmax over all rows (the rule of
  * efg_argmax) to *d_token: each rank reduces its logits to one (value, index) pair and the
- * pairs travel in one 8-byte-per-rank all-gather. Every rank calls it with the same
- * rows/cols. No reference counterpart for the sharding itself. */
+ * pairs are exchanged. While any buffer is registered on the communicator
+ * (efg_comm_register; all ranks share the outcome) the argmax launch itself stores its pair
+ * into every rank's flag area over NVLink and waits (bounded, EFG_ETIMEOUT via
+ * efg_device_error) for the peers' pairs: two launches per call and no collective; every rank
+ * must then make the same sequence of these calls. Otherwise the pairs travel in one
+ * 8-byte-per-rank NCCL all-gather. Every rank calls it with the same rows/cols. No
+ * reference counterpart for the sharding itself. */
 int efg_lm_head_argmax_sharded(int qtype, float* d_logits_shard, int32_t* d_token, const uint8_t* d_W_shard,
                                const float* d_x, const float* d_norm_w, float eps, size_t rows, size_t cols,
                                efg_comm* comm, void* stream);

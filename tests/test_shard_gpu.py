@@ -176,7 +176,37 @@ def _rank_main(rank, world, port, cases, out_dir):
         efg.lm_head_argmax_sharded(QType.Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
         torch.cuda.synchronize()
         np.save(os.path.join(out_dir, f"lm_logits_{rank}.npy"), logits.cpu().numpy())
-        np.save(os.path.join(out_dir, f"lm_tok_{rank}.npy"), tok.cpu().numpy())
+        toks = {"nccl": int(tok.item())}
+        # the same with a buffer registered: the pairs travel by peer stores inside the argmax
+        # launch, twice in a row, as a CUDA graph of two calls replayed twice, and with a NaN in
+        # x (every logit NaN: element 0 of the whole vector is NaN, the token is 0)
+        reg = torch.zeros(64, device="cuda")
+        comm.register(reg)
+        for tag in ("peer", "peer2"):
+            tok.fill_(-1)
+            efg.lm_head_argmax_sharded(QType.Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
+            torch.cuda.synchronize()
+            toks[tag] = int(tok.item())
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+            for _ in range(2):
+                efg.lm_head_argmax_sharded(QType.Q8_0, logits, tok, shard, x, nw, 1e-5, rows, cols, comm)
+        tok.fill_(-1)
+        torch.cuda.synchronize()
+        g.replay()
+        g.replay()
+        torch.cuda.synchronize()
+        toks["graph"] = int(tok.item())
+        del g
+        x_nan = x.clone()
+        x_nan[5] = float("nan")
+        efg.lm_head_argmax_sharded(QType.Q8_0, logits, tok, shard, x_nan, nw, 1e-5, rows, cols, comm)
+        torch.cuda.synchronize()
+        toks["nan"] = int(tok.item())
+        comm.deregister(reg)
+        np.save(os.path.join(out_dir, f"lm_tok_{rank}.npy"), np.array([toks[k] for k in ("nccl", "peer", "peer2", "graph", "nan")]))
         assert efg.device_error() == 0
     finally:
         comm.close()
@@ -207,7 +237,10 @@ def test_multi_rank(tmp_path, oracle):
         W, x = np.load(tmp_path / f"W{i}.npy"), np.load(tmp_path / f"x{i}.npy")
         err = rel_dot_errors(oracle, qt, W, x, rows, ys[0])
         assert err.max() <= TOL, (i, err.max())
-    # the distributed argmax: the same token on every rank, the argmax of all shards' logits
+    # the distributed argmax, through NCCL and through the peer exchange (twice, in a graph):
+    # the same token on every rank, the argmax of all shards' logits; 0 when x holds a NaN
     full = np.concatenate([np.load(tmp_path / f"lm_logits_{r}.npy") for r in range(n)])
-    toks = [int(np.load(tmp_path / f"lm_tok_{r}.npy")[0]) for r in range(n)]
-    assert len(set(toks)) == 1 and toks[0] == oracle.argmax(full)
+    want = oracle.argmax(full)
+    for r in range(n):
+        toks = np.load(tmp_path / f"lm_tok_{r}.npy")
+        assert list(toks[:4]) == [want] * 4 and toks[4] == 0, (r, toks, want)
