@@ -513,6 +513,14 @@ def config0_extra(torch, efg, hbm_peak, x_seed=2, launches=1280):
     g.replay()
     ms = replay_timed(torch, g, gr, c, launches, torch.cuda.synchronize, 1) / launches
     del g, gr
+
+    def step_hot(i):  # one copy: W stays in L2 (the hot-cache number)
+        efg.matvec(Q4_0, y4, W4[0], x, rows, cols)
+
+    g, gr, c = graphs_of(torch, step_hot, launches, 64, chunk=640)
+    g.replay()
+    ms_hot = replay_timed(torch, g, gr, c, launches, torch.cuda.synchronize, 1) / launches
+    del g, gr
     efg.set_q4_mma(False)  # the same launches on the CUDA-core kernel, for comparison
     try:
         g, gr, c = graphs_of(torch, step, launches, 64, chunk=640)
@@ -578,6 +586,7 @@ def config0_extra(torch, efg, hbm_peak, x_seed=2, launches=1280):
                                              "us_per_launch": round(m * 1e3, 3), "launches": k}
                for n, (m, k) in ind.items()},
             "us_per_launch": round(ms * 1e3, 3), "bytes_per_launch": nb, "copies": copies,
+            "hot_cache_us_per_launch": round(ms_hot * 1e3, 3),
             "kernel": "small-matrix integer tensor-core kernel (weights fetched ahead, next launch co-resident)",
             "us_per_launch_cuda_cores": round(ms_cc * 1e3, 3),
             "frac_of_hbm_cuda_cores": round(nb / ms_cc / 1e6 / hbm_peak, 4)}
