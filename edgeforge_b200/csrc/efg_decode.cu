@@ -1210,7 +1210,9 @@ constexpr size_t kPrefillRows = 64;  // tokens per pass
 
 int ensure_prefill_buffers(Decoder& D) {
   if (D.pb) return EFG_OK;
-  const size_t P = std::min(kPrefillRows, D.max_seq), Dm = static_cast<size_t>(D.c.hidden),
+  // The pass size does not depend on max_seq: a prefill pass never exceeds the cache, but the
+  // rows of a multi-sequence step are different sequences, as many as there are slots.
+  const size_t P = kPrefillRows, Dm = static_cast<size_t>(D.c.hidden),
                F = static_cast<size_t>(D.c.intermediate);
   auto al = [](size_t n) { return (n * sizeof(float) + 255) / 256 * 256; };
   const size_t kvd = static_cast<size_t>(D.c.kv_dim());
